@@ -1,0 +1,161 @@
+/*
+ * tb_sparse.h -- C ABI of the B200 (sm_100a) sparse submanifold-convolution path.
+ *
+ * This is the drop-in boundary for the operator layer of pwilkin/trellis.cpp,
+ * `include/sparse.h` + `src/sparse.cpp`. Every entry point names the reference symbol it
+ * replaces (paths inside that project).
+ *
+ * Conventions (shared by every call):
+ *   - Pointers are DEVICE pointers unless the name ends in `_host`. The caller owns all
+ *     memory it passes in. A context may hold device workspace of its own (hash tables,
+ *     staging for the `_host` calls), grown on demand and freed by tb_ctx_destroy.
+ *   - Layouts follow the reference:
+ *       coords   int32 [N][3] = (x,y,z) or [N][4] = (b,x,y,z)     coord_stride 3 or 4
+ *       feats    [N][Ci], a voxel's channels contiguous (ggml ne [Ci,N], src/sparse.cpp:66)
+ *       weight   [Co][27][Ci] (torch [Co,3,3,3,Ci], tools/convert.py:141-146)
+ *       bias     float32 [Co] or NULL
+ *       nbr      int32 tap-major [27][N]; nbr[t*N+i] is the row of coords[i] + offset(t),
+ *                or N when that voxel is absent. t = kd*9 + kh*3 + kw and
+ *                offset = (kd-1, kh-1, kw-1) on (x,y,z)       (include/sparse.h:14-17)
+ *   - All calls return tb_status and never throw. A call enqueues work on the context's
+ *     stream and returns without synchronising, unless its comment says otherwise.
+ *   - One tb_ctx per device and stream. A context is not thread-safe; separate contexts
+ *     are.
+ */
+#ifndef TB_SPARSE_H
+#define TB_SPARSE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tb_status {
+    TB_OK = 0,
+    TB_ERR_INVALID_ARG = 1,   /* null pointer, negative size, bad stride, misaligned pointer */
+    TB_ERR_UNSUPPORTED = 2,   /* channel count or dtype combination without a kernel */
+    TB_ERR_CUDA = 3,          /* a CUDA runtime/driver call failed (see tb_ctx_last_error) */
+    TB_ERR_OUT_OF_MEMORY = 4, /* workspace allocation failed */
+    TB_ERR_DEVICE = 5,        /* a kernel reported a failed check (bounded wait ran out,
+                                 hash probe limit); see tb_ctx_check_device */
+    TB_ERR_TOO_LARGE = 6      /* size above a documented maximum */
+} tb_status;
+
+typedef enum tb_dtype { TB_F32 = 0, TB_F16 = 1, TB_BF16 = 2 } tb_dtype;
+
+/* Epilogue fused after bias. SILU = x * sigmoid(x) (the ggml_silu that follows the norms in
+ * src/sparse.cpp:127,261,293). */
+typedef enum tb_epilogue { TB_EPI_NONE = 0, TB_EPI_SILU = 1 } tb_epilogue;
+
+typedef struct tb_ctx tb_ctx;
+
+const char* tb_status_string(tb_status s);
+const char* tb_version(void);
+
+/* Create a context on `device`, enqueuing on `stream` (a cudaStream_t; NULL = legacy
+ * default stream). No reference counterpart: ggml's backend object plays this role
+ * (src/trellis_model.cpp:36-94). */
+tb_status tb_ctx_create(int device, void* stream, tb_ctx** out);
+tb_status tb_ctx_destroy(tb_ctx* ctx);
+tb_status tb_ctx_set_stream(tb_ctx* ctx, void* stream);
+/* Human-readable detail of the last failure on this context ("" if none). */
+const char* tb_ctx_last_error(const tb_ctx* ctx);
+/* Synchronise the stream and report device-side check failures since the last call
+ * (TB_OK or TB_ERR_DEVICE; the flag is cleared). */
+tb_status tb_ctx_check_device(tb_ctx* ctx);
+
+/* ---- neighbor map -------------------------------------------------------------------
+ * Replaces trellis::build_neighbor_table (include/sparse.h:14-17, src/sparse.cpp:21-39).
+ * Output is bit-exact with the reference: the same 64-bit key packing (src/sparse.cpp:25),
+ * a later duplicate row wins (src/sparse.cpp:26), sentinel N. With coord_stride 4 the
+ * batch b is XOR-ed into key bits 60..63, so batch 0 keys equal the reference's.
+ * nbr_out: int32 [27*n]. Uses a context-owned hash table of 16*next_pow2(2n) bytes. */
+tb_status tb_build_neighbor_map(tb_ctx* ctx, const int32_t* coords, int64_t n,
+                                int coord_stride, int32_t* nbr_out);
+
+/* Number of (voxel, tap) pairs with a present neighbor in `nbr` (the algorithmic work of
+ * one conv). Synchronises the stream. No reference counterpart (instrumentation). */
+tb_status tb_count_valid_pairs(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t* pairs);
+
+/* ---- submanifold conv -----------------------------------------------------------------
+ * Replaces sparse_submconv (include/sparse.h:19-22, src/sparse.cpp:87-92) and its
+ * submconv_range (src/sparse.cpp:64-79):
+ *   out[i][o] = epi( bias[o] + sum_t sum_c weight[o][t][c] * feats[nbr[t*n+i]][c] )
+ * with absent taps (nbr == n) contributing zero (the padded zero row, src/sparse.cpp:82-85).
+ *   dtype TB_BF16 / TB_F16: feats and weight in that type, fp32 accumulation on tcgen05
+ *        tensor cores. Needs ci in {16, 32} or a multiple of 64, co a multiple of 16 up
+ *        to 256 or a multiple of 256.
+ *   dtype TB_F32: fp32 operands and fp32 FFMA accumulation (the precision mode of
+ *        g_sparse_cast_f32 / --f32, src/sparse.cpp:16-19). Any ci, co >= 1.
+ *   out_dtype: TB_F32 or the operand dtype. Pointers must be 16-byte aligned.
+ * `out` must not alias `feats`. */
+tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n,
+                      const void* feats, int ci, const void* weight, const float* bias,
+                      int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
+
+/* ---- subdivide and channel-to-spatial gather (sparse_c2s, src/sparse.cpp:172-336) -------
+ * tb_subdivide replaces the host octant loop of src/sparse.cpp:205-222: for parent i
+ * ascending and octant o ascending with mask[o + 8i] != 0, emit the child
+ * (2x + (o&1), 2y + ((o>>1)&1), 2z + ((o>>2)&1)) (batch column copied when stride is 4),
+ * gidx = o + 8i, and mstart[i] = index of parent i's first child, mstart[n] = M.
+ * mask: uint8 [8n]. child_coords: int32 [max_children][coord_stride], gidx: int32
+ * [max_children], mstart: int32 [n+1] (may be NULL). Writes M to *m_out (host) and
+ * synchronises. Returns TB_ERR_TOO_LARGE (and writes M) when M > max_children; the
+ * outputs are then incomplete. */
+tb_status tb_subdivide(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord_stride,
+                       const uint8_t* mask, int32_t* child_coords, int32_t* gidx,
+                       int32_t* mstart, int64_t max_children, int64_t* m_out);
+
+/* Child m takes row gidx[m] of src viewed as [8n][c]: the SparseChannel2Spatial gather
+ * of src/sparse.cpp:263-266,288 (octant o of parent i is channels o*c..o*c+c-1 of conv1's
+ * [n][8c] output), and the skip gather of src/sparse.cpp:307 with c = Cin/8.
+ * out: [m][c] of `dtype`. */
+tb_status tb_c2s_gather(tb_ctx* ctx, const void* src, const int32_t* gidx, int64_t m,
+                        int c, tb_dtype dtype, void* out);
+
+/* In-place bias + activation over x [n][c] (the bias add of src/sparse.cpp:78 and the
+ * SiLU of src/sparse.cpp:127 as a standalone pass). bias may be NULL. */
+tb_status tb_bias_act(tb_ctx* ctx, void* x, int64_t n, int c, const float* bias,
+                      tb_dtype dtype, tb_epilogue epi);
+
+/* ---- host-buffer end-to-end call --------------------------------------------------------
+ * Mirrors one decoder stage graph run (run1 / GraphRun::run: upload inputs, compute, read
+ * back; src/shape_decoder.cpp:34-51, src/sparse.cpp:145-169), without the LayerNorm/MLP
+ * tail. It copies coords_host and feats_host to the device, builds the neighbor map, runs
+ * `nlayers` stacked submanifold convs (layer l reads layer l-1's output) and copies the
+ * last output to out_host. Weights and biases are DEVICE pointers: they are resident
+ * model parameters, as in the reference's backend buffer. Intermediate outputs use
+ * `dtype`; the last layer writes `out_dtype`. Synchronises before returning. Host
+ * buffers may be pageable; pinned buffers copy faster. */
+typedef struct tb_conv_layer {
+    const void* weight;   /* [co][27][ci] of dtype, device */
+    const float* bias;    /* [co] float32, device, or NULL */
+    int ci;
+    int co;
+    tb_epilogue epi;
+} tb_conv_layer;
+
+tb_status tb_submconv_stack_host(tb_ctx* ctx, const int32_t* coords_host, int64_t n,
+                                 int coord_stride, const void* feats_host,
+                                 const tb_conv_layer* layers, int nlayers, tb_dtype dtype,
+                                 tb_dtype out_dtype, void* out_host);
+
+/* ---- multi-GPU z-slab sharding (no reference counterpart: the reference is single-GPU,
+ * it only chunks output ranges on one device, src/sparse.cpp:94-118) -----------------------
+ * tb_zslab_counts: histogram of voxels per z plane, counts[z - z_min] for z in
+ * [z_min, z_min + nz); voxels outside the range are ignored. counts is int64 [nz], zeroed by
+ * the call.
+ * tb_gather_rows: out[k] = src[rows[k]] for k < m, row_bytes per row (halo packing and
+ * owned-row extraction). row_bytes must be a multiple of 4. */
+tb_status tb_zslab_counts(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord_stride,
+                          int32_t z_min, int32_t nz, int64_t* counts);
+tb_status tb_gather_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t m,
+                         int64_t row_bytes, void* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TB_SPARSE_H */

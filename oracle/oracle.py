@@ -9,6 +9,7 @@ Functions and the reference lines they follow (paths inside pwilkin/trellis.cpp)
 
 * :func:`build_neighbor_table` -- ``src/sparse.cpp:21-39``
 * :func:`submconv` -- ``src/sparse.cpp:64-92`` (fp64 accumulation of the given operands)
+* :func:`submconv_rows` -- the same for a subset of output rows
 * :func:`submconv_f32_mt` -- the same loop in fp32 on host threads (timed CPU baseline)
 * :func:`subdivide` -- ``src/sparse.cpp:205-222``
 * :func:`c2s_gather` -- ``src/sparse.cpp:263-266,288``
@@ -53,6 +54,10 @@ def lib():
         L.orc_submconv_f64.restype = ctypes.c_int
         L.orc_submconv_f64.argtypes = [_i32p, ctypes.c_int64, _f32p, ctypes.c_int, _f32p,
                                        _f32p, ctypes.c_int, ctypes.c_int, _f64p]
+        L.orc_submconv_rows_f64.restype = ctypes.c_int
+        L.orc_submconv_rows_f64.argtypes = [_i32p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64), ctypes.c_int64,
+                                            _f32p, ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int,
+                                            _f64p]
         L.orc_weight_tap_major.restype = None
         L.orc_weight_tap_major.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p]
         L.orc_submconv_f32_mt.restype = ctypes.c_int
@@ -112,6 +117,24 @@ def submconv(nbr: np.ndarray, feats: np.ndarray, weight: np.ndarray, bias=None,
                                 _p(out, _f64p))
     if rc != 0:
         raise ValueError("orc_submconv_f64 failed")
+    return out
+
+
+def submconv_rows(nbr, feats, weight, rows, bias=None, silu: bool = False) -> np.ndarray:
+    """:func:`submconv` for the output rows ``rows`` only; returns float64 [len(rows), Co]."""
+    f = np.ascontiguousarray(feats, dtype=np.float32)
+    n, ci = f.shape
+    w = np.ascontiguousarray(weight, dtype=np.float32).reshape(weight.shape[0], 27, ci)
+    co = w.shape[0]
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    r = np.ascontiguousarray(rows, dtype=np.int64)
+    nb = np.ascontiguousarray(nbr, dtype=np.int32)
+    out = np.empty((r.size, co), dtype=np.float64)
+    rc = lib().orc_submconv_rows_f64(_p(nb, _i32p), n, r.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), r.size,
+                                     _p(f, _f32p), ci, _p(w, _f32p), None if b is None else _p(b, _f32p), co,
+                                     1 if silu else 0, _p(out, _f64p))
+    if rc != 0:
+        raise ValueError("orc_submconv_rows_f64 failed")
     return out
 
 

@@ -13,6 +13,7 @@
  *                                                        sentinel N
  *   orc_submconv_f64           src/sparse.cpp:64-92     per-tap gather -> GEMM -> accumulate
  *                                                        + bias; absent taps read a zero row
+ *   orc_submconv_rows_f64      same, for a subset of output rows
  *   orc_submconv_f32_mt        same, fp32, threads over voxel blocks (the CPU baseline)
  *   orc_subdivide              src/sparse.cpp:205-222   octant loop, child coords, gidx
  *   orc_c2s_gather             src/sparse.cpp:263-266,288  child takes channel block o
@@ -125,6 +126,34 @@ int orc_submconv_f64(const int32_t* nbr, int64_t n, const float* feats, int ci,
         }
     }
     free(acc);
+    return 0;
+}
+
+/* The same as orc_submconv_f64 for a subset of output rows (rows[k] < n); out is
+ * [nrows][Co]. Lets the tests check sampled rows of full-size configurations. */
+int orc_submconv_rows_f64(const int32_t* nbr, int64_t n, const int64_t* rows, int64_t nrows,
+                          const float* feats, int ci, const float* w, const float* bias, int co,
+                          int epi, double* out) {
+    if (n < 0 || ci <= 0 || co <= 0) return -1;
+    for (int64_t k = 0; k < nrows; ++k) {
+        const int64_t i = rows[k];
+        if (i < 0 || i >= n) return -1;
+        double* acc = out + k * co;
+        for (int o = 0; o < co; ++o) acc[o] = bias ? (double)bias[o] : 0.0;
+        for (int t = 0; t < 27; ++t) {
+            int64_t j = nbr[(int64_t)t * n + i];
+            if (j < 0 || j >= n) continue;
+            const float* x = feats + j * ci;
+            for (int o = 0; o < co; ++o) {
+                const float* wr = w + ((int64_t)o * 27 + t) * ci;
+                double sum = 0.0;
+                for (int c = 0; c < ci; ++c) sum += (double)wr[c] * (double)x[c];
+                acc[o] += sum;
+            }
+        }
+        if (epi == 1)
+            for (int o = 0; o < co; ++o) acc[o] = acc[o] / (1.0 + exp(-acc[o]));
+    }
     return 0;
 }
 

@@ -49,3 +49,21 @@ def max_rel(mine, ref):
     mine = np.asarray(mine, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     return float(np.max(np.abs(mine - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    """Round float32 values to bf16/f16 (nearest even) and return them as float32."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    td = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[dtype]
+    return t.to(td).to(torch.float32).numpy()
+
+
+def random_voxels(n: int, box: int, seed: int, batch: bool = False) -> np.ndarray:
+    """n distinct voxels drawn uniformly from [0, box)^3 (int32 [n,3] or [n,4] with b=0)."""
+    rng = np.random.default_rng(seed)
+    flat = rng.choice(box ** 3, size=n, replace=False)
+    c = np.stack([flat // (box * box), (flat // box) % box, flat % box], 1).astype(np.int32)
+    if batch:
+        c = np.concatenate([np.zeros((n, 1), np.int32), c], 1)
+    return c

@@ -1,0 +1,194 @@
+// C-ABI glue: contexts, status reporting, workspace, conv dispatch and the host-buffer
+// stack call. The kernels live in tb_nbr.cu, tb_conv_tc.cu, tb_conv_f32.cu, tb_subdiv.cu.
+#include "tb_common.cuh"
+
+#include <algorithm>
+#include <cstring>
+#include <new>
+
+tb_status tb_fail(tb_ctx* ctx, tb_status s, const std::string& msg) {
+    if (ctx) ctx->last_error = msg;
+    return s;
+}
+
+tb_status tb_cuda_fail(tb_ctx* ctx, cudaError_t e, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+    if (e == cudaErrorMemoryAllocation) return tb_fail(ctx, TB_ERR_OUT_OF_MEMORY, m);
+    return tb_fail(ctx, TB_ERR_CUDA, m);
+}
+
+tb_status tb_ensure(tb_ctx* ctx, void** buf, size_t* cap, size_t bytes, const char* what) {
+    if (*cap >= bytes && *buf) return TB_OK;
+    if (*buf) {
+        // the old buffer may still be read by queued work on this stream
+        cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaStreamSynchronize before workspace growth");
+        cudaFree(*buf);
+        *buf = nullptr;
+        *cap = 0;
+    }
+    size_t want = std::max<size_t>(bytes, 1 << 20);
+    cudaError_t e = cudaMalloc(buf, want);
+    if (e != cudaSuccess) {
+        *buf = nullptr;
+        return tb_fail(ctx, TB_ERR_OUT_OF_MEMORY, std::string("workspace allocation failed (") + what + ")");
+    }
+    *cap = want;
+    return TB_OK;
+}
+
+extern "C" {
+
+const char* tb_status_string(tb_status s) {
+    switch (s) {
+        case TB_OK: return "ok";
+        case TB_ERR_INVALID_ARG: return "invalid argument";
+        case TB_ERR_UNSUPPORTED: return "unsupported configuration";
+        case TB_ERR_CUDA: return "CUDA error";
+        case TB_ERR_OUT_OF_MEMORY: return "out of device memory";
+        case TB_ERR_DEVICE: return "device-side check failed";
+        case TB_ERR_TOO_LARGE: return "size above the supported maximum";
+    }
+    return "unknown status";
+}
+
+const char* tb_version(void) { return "tb_sparse 0.1.0 (sm_100a)"; }
+
+tb_status tb_ctx_create(int device, void* stream, tb_ctx** out) {
+    if (!out) return TB_ERR_INVALID_ARG;
+    *out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return TB_ERR_INVALID_ARG;
+    tb_ctx* ctx = new (std::nothrow) tb_ctx();
+    if (!ctx) return TB_ERR_OUT_OF_MEMORY;
+    ctx->device = device;
+    ctx->stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSetDevice(device);
+    cudaDeviceProp prop;
+    if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, device);
+    if (e == cudaSuccess && prop.major != 10) {
+        delete ctx;
+        return TB_ERR_UNSUPPORTED;   // sm_100a kernels only
+    }
+    if (e == cudaSuccess) {
+        ctx->num_sms = prop.multiProcessorCount;
+        ctx->max_smem_optin = (int)prop.sharedMemPerBlockOptin;
+        e = cudaMalloc(&ctx->d_err, sizeof(int));
+    }
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        if (ctx->d_err) cudaFree(ctx->d_err);
+        delete ctx;
+        return e == cudaErrorMemoryAllocation ? TB_ERR_OUT_OF_MEMORY : TB_ERR_CUDA;
+    }
+    *out = ctx;
+    return TB_OK;
+}
+
+tb_status tb_ctx_destroy(tb_ctx* ctx) {
+    if (!ctx) return TB_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->host_stage) cudaFree(ctx->host_stage);
+    if (ctx->d_err) cudaFree(ctx->d_err);
+    delete ctx;
+    return TB_OK;
+}
+
+tb_status tb_ctx_set_stream(tb_ctx* ctx, void* stream) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    ctx->stream = reinterpret_cast<cudaStream_t>(stream);
+    return TB_OK;
+}
+
+const char* tb_ctx_last_error(const tb_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+tb_status tb_ctx_check_device(tb_ctx* ctx) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    int h = 0;
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    if (h != TB_DEVERR_NONE) {
+        TB_CUDA_TRY(ctx, cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream));
+        TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        const char* what = h == TB_DEVERR_HASH_PROBE ? "hash probe bound exceeded"
+                         : h == TB_DEVERR_WAIT_TIMEOUT ? "bounded mbarrier wait timed out in the conv kernel"
+                         : h == TB_DEVERR_TMEM_ALLOC ? "TMEM allocation failed" : "unknown device error";
+        return tb_fail(ctx, TB_ERR_DEVICE, what);
+    }
+    return TB_OK;
+}
+
+tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
+                      const void* weight, const float* bias, int co, tb_dtype dtype, tb_dtype out_dtype,
+                      tb_epilogue epi, void* out) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (n < 0 || ci <= 0 || co <= 0) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: n < 0 or channels <= 0");
+    if (epi != TB_EPI_NONE && epi != TB_EPI_SILU) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: bad epilogue");
+    if (dtype != TB_F32 && dtype != TB_F16 && dtype != TB_BF16)
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: bad dtype");
+    if (out_dtype != TB_F32 && out_dtype != dtype)
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "tb_submconv: out_dtype must be TB_F32 or the operand dtype");
+    if (n == 0) return TB_OK;
+    if (!nbr || !feats || !weight || !out) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: null pointer");
+    if (n >= (int64_t)INT32_MAX) return tb_fail(ctx, TB_ERR_TOO_LARGE, "tb_submconv: n must be < 2^31-1");
+    if (!tb_aligned16(feats) || !tb_aligned16(weight) || !tb_aligned16(out) || (bias && !tb_aligned16(bias)))
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: feats/weight/bias/out must be 16-byte aligned");
+    if (feats == out) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: out must not alias feats");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    if (dtype == TB_F32)
+        return tb_conv_f32_launch(ctx, nbr, n, reinterpret_cast<const float*>(feats), ci,
+                                  reinterpret_cast<const float*>(weight), bias, co, epi, reinterpret_cast<float*>(out));
+    return tb_conv_tc_launch(ctx, nbr, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
+}
+
+tb_status tb_submconv_stack_host(tb_ctx* ctx, const int32_t* coords_host, int64_t n, int coord_stride,
+                                 const void* feats_host, const tb_conv_layer* layers, int nlayers,
+                                 tb_dtype dtype, tb_dtype out_dtype, void* out_host) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (n < 0 || nlayers <= 0 || !layers || (coord_stride != 3 && coord_stride != 4))
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_stack_host: bad arguments");
+    for (int l = 0; l < nlayers; ++l) {
+        if (layers[l].ci <= 0 || layers[l].co <= 0 || !layers[l].weight)
+            return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_stack_host: bad layer");
+        if (l > 0 && layers[l].ci != layers[l - 1].co)
+            return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_stack_host: layer ci != previous co");
+    }
+    if (n == 0) return TB_OK;
+    if (!coords_host || !feats_host || !out_host)
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_stack_host: null pointer");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    const size_t es = tb_dtype_size(dtype);
+    int cmax = layers[0].ci;
+    for (int l = 0; l < nlayers; ++l) cmax = std::max(cmax, layers[l].co);
+    auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+    const size_t coords_b = al((size_t)n * coord_stride * 4);
+    const size_t nbr_b = al((size_t)n * 27 * 4);
+    const size_t feat_b = al((size_t)n * cmax * std::max<size_t>(es, tb_dtype_size(out_dtype)));
+    tb_status s = tb_ensure(ctx, &ctx->host_stage, &ctx->host_stage_bytes, coords_b + nbr_b + 2 * feat_b, "host-call staging");
+    if (s != TB_OK) return s;
+    uint8_t* base = reinterpret_cast<uint8_t*>(ctx->host_stage);
+    int32_t* d_coords = reinterpret_cast<int32_t*>(base);
+    int32_t* d_nbr = reinterpret_cast<int32_t*>(base + coords_b);
+    uint8_t* buf[2] = {base + coords_b + nbr_b, base + coords_b + nbr_b + feat_b};
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(d_coords, coords_host, (size_t)n * coord_stride * 4, cudaMemcpyHostToDevice, ctx->stream));
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(buf[0], feats_host, (size_t)n * layers[0].ci * es, cudaMemcpyHostToDevice, ctx->stream));
+    s = tb_build_neighbor_map(ctx, d_coords, n, coord_stride, d_nbr);
+    if (s != TB_OK) return s;
+    int cur = 0;
+    for (int l = 0; l < nlayers; ++l) {
+        const tb_dtype od = (l == nlayers - 1) ? out_dtype : dtype;
+        s = tb_submconv(ctx, d_nbr, n, buf[cur], layers[l].ci, layers[l].weight, layers[l].bias, layers[l].co,
+                        dtype, od, layers[l].epi, buf[cur ^ 1]);
+        if (s != TB_OK) return s;
+        cur ^= 1;
+    }
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(out_host, buf[cur], (size_t)n * layers[nlayers - 1].co * tb_dtype_size(out_dtype),
+                                     cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return tb_ctx_check_device(ctx);
+}
+
+}  // extern "C"

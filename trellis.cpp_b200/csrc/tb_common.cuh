@@ -1,0 +1,76 @@
+// Shared host/device helpers of the sparse-conv library: the context, status plumbing,
+// workspace growth and the 64-bit coordinate key of the reference (src/sparse.cpp:25).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda.h>
+#include <stdint.h>
+#include <string>
+
+#include "tb_sparse.h"
+
+// Device-side error codes written to tb_ctx::d_err (first failure wins).
+enum tb_device_error : int {
+    TB_DEVERR_NONE = 0,
+    TB_DEVERR_HASH_PROBE = 1,     // hash insert/lookup exceeded its probe bound
+    TB_DEVERR_WAIT_TIMEOUT = 2,   // a bounded mbarrier wait in the conv kernel ran out
+    TB_DEVERR_TMEM_ALLOC = 3,     // TMEM allocation returned an unusable address
+};
+
+struct tb_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    int max_smem_optin = 0;
+    int* d_err = nullptr;          // one int on the device
+    void* ws = nullptr;            // hash table / scratch
+    size_t ws_bytes = 0;
+    void* host_stage = nullptr;    // device buffers of the *_host calls
+    size_t host_stage_bytes = 0;
+    std::string last_error;
+    void* encode_tiled = nullptr;  // cuTensorMapEncodeTiled, fetched once
+};
+
+// Record a failure on the context and return the status.
+tb_status tb_fail(tb_ctx* ctx, tb_status s, const std::string& msg);
+tb_status tb_cuda_fail(tb_ctx* ctx, cudaError_t e, const char* what);
+// Grow a context-owned device buffer to at least `bytes` (never shrinks).
+tb_status tb_ensure(tb_ctx* ctx, void** buf, size_t* cap, size_t bytes, const char* what);
+
+#define TB_CUDA_TRY(ctx, call)                                          \
+    do {                                                                \
+        cudaError_t e_ = (call);                                        \
+        if (e_ != cudaSuccess) return tb_cuda_fail((ctx), e_, #call);   \
+    } while (0)
+
+#define TB_LAUNCH_CHECK(ctx, what)                                      \
+    do {                                                                \
+        cudaError_t e_ = cudaGetLastError();                            \
+        if (e_ != cudaSuccess) return tb_cuda_fail((ctx), e_, what);    \
+    } while (0)
+
+// ---- the packed key (src/sparse.cpp:25), with the batch folded into bits 60..63 ----------
+__host__ __device__ __forceinline__ uint64_t tb_key3(int32_t x, int32_t y, int32_t z) {
+    return ((uint64_t)(uint32_t)x << 40) | ((uint64_t)(uint32_t)y << 20) | (uint64_t)(uint32_t)z;
+}
+
+__host__ __device__ __forceinline__ uint64_t tb_mix64(uint64_t k) {   // murmur3 fmix64
+    k ^= k >> 33; k *= 0xff51afd7ed558ccdULL; k ^= k >> 33; k *= 0xc4ceb9fe1a85ec53ULL; k ^= k >> 33;
+    return k;
+}
+
+inline size_t tb_dtype_size(tb_dtype d) { return d == TB_F32 ? 4 : 2; }
+
+inline bool tb_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch helpers implemented in the individual .cu files (all enqueue on ctx->stream).
+tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride,
+                            int32_t* nbr, void* table, uint64_t cap);
+tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
+                            const void* weight, const float* bias, int co, tb_dtype dtype,
+                            tb_dtype out_dtype, tb_epilogue epi, void* out);
+tb_status tb_conv_f32_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const float* feats, int ci,
+                             const float* weight, const float* bias, int co, tb_epilogue epi,
+                             float* out);
+bool tb_conv_tc_supported(int ci, int co);
+uint64_t tb_hash_capacity(int64_t n);

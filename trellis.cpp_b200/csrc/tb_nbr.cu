@@ -1,0 +1,215 @@
+// Coordinate hash table and 27-tap neighbor map on the GPU.
+//
+// Replaces trellis::build_neighbor_table (src/sparse.cpp:21-39), which inserts every voxel
+// into a std::unordered_map keyed by the packed coordinate (src/sparse.cpp:25-26, a later
+// duplicate overwrites) and then does 27 lookups per voxel into a tap-major [27*N] table
+// whose absent entries hold N.
+//
+// GPU design: open addressing with linear probing over 16-byte slots {key, row}. The
+// capacity is the next power of two >= 2N (load factor <= 1/2), so one 16-byte load per
+// probe. Insert: atomicCAS claims the slot for the key, then atomicMax on the row makes the
+// largest row index win, which is exactly "last writer wins" of the sequential reference.
+// The all-ones key is reachable (coords (-1,-1,-1)) and is the empty marker, so that one
+// key lives in a separate cell. Lookups run one thread per voxel, 27 probes each, and write
+// nbr[t*N + i] coalesced across the warp for every tap.
+#include "tb_common.cuh"
+
+namespace {
+
+constexpr unsigned long long kEmpty = ~0ull;
+
+struct __align__(16) Slot {
+    unsigned long long key;
+    int row;
+    int pad;
+};
+
+__device__ __forceinline__ uint64_t key_of(const int32_t* c, int stride, int dx, int dy, int dz) {
+    if (stride == 4)
+        return tb_key3(c[1] + dx, c[2] + dy, c[3] + dz) ^ ((uint64_t)(uint32_t)c[0] << 60);
+    return tb_key3(c[0] + dx, c[1] + dy, c[2] + dz);
+}
+
+__global__ void k_hash_clear(Slot* __restrict__ t, uint64_t cap, int* __restrict__ special) {
+    uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (; i < cap; i += stride) {
+        ulonglong2 v; v.x = kEmpty; v.y = 0xFFFFFFFFull;   // row = -1
+        reinterpret_cast<ulonglong2*>(t)[i] = v;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) *special = -1;
+}
+
+__global__ void k_hash_insert(const int32_t* __restrict__ coords, int64_t n, int stride,
+                              Slot* __restrict__ t, uint64_t mask, int* __restrict__ special,
+                              int* __restrict__ err) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint64_t k = key_of(coords + i * stride, stride, 0, 0, 0);
+    if (k == kEmpty) { atomicMax(special, (int)i); return; }
+    uint64_t h = tb_mix64(k) & mask;
+    for (uint64_t probe = 0; probe <= mask; ++probe) {
+        const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
+        if (prev == kEmpty || prev == k) { atomicMax(&t[h].row, (int)i); return; }
+        h = (h + 1) & mask;
+    }
+    atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
+}
+
+__device__ __forceinline__ int lookup(const Slot* __restrict__ t, uint64_t mask, int special,
+                                      uint64_t k, int absent, int* __restrict__ err) {
+    if (k == kEmpty) return special >= 0 ? special : absent;
+    uint64_t h = tb_mix64(k) & mask;
+    for (uint64_t probe = 0; probe <= mask; ++probe) {
+        const ulonglong2 s = __ldg(reinterpret_cast<const ulonglong2*>(t) + h);
+        if (s.x == k) return (int)(uint32_t)s.y;
+        if (s.x == kEmpty) return absent;
+        h = (h + 1) & mask;
+    }
+    atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
+    return absent;
+}
+
+__global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int stride,
+                             const Slot* __restrict__ t, uint64_t mask,
+                             const int* __restrict__ special_p, int32_t* __restrict__ nbr,
+                             int* __restrict__ err) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int special = *special_p;
+    int32_t c[4];
+    for (int d = 0; d < stride; ++d) c[d] = coords[i * stride + d];
+#pragma unroll
+    for (int tap = 0; tap < 27; ++tap) {
+        const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+        const uint64_t k = key_of(c, stride, kd - 1, kh - 1, kw - 1);
+        nbr[(int64_t)tap * n + i] = lookup(t, mask, special, k, (int)n, err);
+    }
+}
+
+__global__ void k_count_valid(const int32_t* __restrict__ nbr, int64_t total, int32_t n,
+                              unsigned long long* __restrict__ out) {
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    unsigned long long local = 0;
+    for (; i < total; i += stride) local += (nbr[i] != n);
+    for (int o = 16; o > 0; o >>= 1) local += __shfl_down_sync(0xffffffffu, local, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(out, local);
+}
+
+__global__ void k_zslab_counts(const int32_t* __restrict__ coords, int64_t n, int stride,
+                               int32_t z_min, int32_t nz, unsigned long long* __restrict__ counts) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int32_t z = coords[i * stride + (stride - 1)];
+    const int64_t b = (int64_t)z - z_min;
+    if (b >= 0 && b < nz) atomicAdd(&counts[b], 1ull);
+}
+
+__global__ void k_gather_rows(const uint32_t* __restrict__ src, const int32_t* __restrict__ rows,
+                              int64_t m, int64_t words, uint32_t* __restrict__ out) {
+    // one warp per row, 4-byte words (16-byte vectors when the row allows it)
+    const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= m) return;
+    const int64_t r = rows[warp];
+    const uint32_t* s = src + r * words;
+    uint32_t* d = out + warp * words;
+    if ((words & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+        const int64_t v = words >> 2;
+        for (int64_t k = lane; k < v; k += 32)
+            reinterpret_cast<uint4*>(d)[k] = reinterpret_cast<const uint4*>(s)[k];
+    } else {
+        for (int64_t k = lane; k < words; k += 32) d[k] = s[k];
+    }
+}
+
+}  // namespace
+
+uint64_t tb_hash_capacity(int64_t n) {
+    uint64_t cap = 1024;
+    while (cap < (uint64_t)(2 * n)) cap <<= 1;
+    return cap;
+}
+
+// `table` holds cap Slots followed by one int (the all-ones key cell); 16*cap + 16 bytes.
+tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride,
+                            int32_t* nbr, void* table, uint64_t cap) {
+    Slot* t = reinterpret_cast<Slot*>(table);
+    int* special = reinterpret_cast<int*>(t + cap);
+    const uint64_t mask = cap - 1;
+    const int tpb = 256;
+    const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
+    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap, special);
+    TB_LAUNCH_CHECK(ctx, "k_hash_clear");
+    const int64_t blocks = (n + tpb - 1) / tpb;
+    k_hash_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, ctx->d_err);
+    TB_LAUNCH_CHECK(ctx, "k_hash_insert");
+    k_nbr_lookup<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, nbr, ctx->d_err);
+    TB_LAUNCH_CHECK(ctx, "k_nbr_lookup");
+    return TB_OK;
+}
+
+extern "C" tb_status tb_build_neighbor_map(tb_ctx* ctx, const int32_t* coords, int64_t n,
+                                           int coord_stride, int32_t* nbr_out) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (n < 0 || (coord_stride != 3 && coord_stride != 4))
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_build_neighbor_map: n < 0 or coord_stride not 3/4");
+    if (n == 0) return TB_OK;
+    if (!coords || !nbr_out) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_build_neighbor_map: null pointer");
+    if (n >= (int64_t)INT32_MAX) return tb_fail(ctx, TB_ERR_TOO_LARGE, "tb_build_neighbor_map: n must be < 2^31-1");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    const uint64_t cap = tb_hash_capacity(n);
+    tb_status s = tb_ensure(ctx, &ctx->ws, &ctx->ws_bytes, cap * sizeof(Slot) + 16, "hash table");
+    if (s != TB_OK) return s;
+    return tb_nbr_build_impl(ctx, coords, n, coord_stride, nbr_out, ctx->ws, cap);
+}
+
+extern "C" tb_status tb_count_valid_pairs(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t* pairs) {
+    if (!ctx || !pairs || n < 0) return TB_ERR_INVALID_ARG;
+    *pairs = 0;
+    if (n == 0) return TB_OK;
+    if (!nbr) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_count_valid_pairs: null nbr");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    tb_status s = tb_ensure(ctx, &ctx->ws, &ctx->ws_bytes, 16, "counter");
+    if (s != TB_OK) return s;
+    unsigned long long* d = reinterpret_cast<unsigned long long*>(ctx->ws);
+    TB_CUDA_TRY(ctx, cudaMemsetAsync(d, 0, sizeof(unsigned long long), ctx->stream));
+    k_count_valid<<<ctx->num_sms * 8, 256, 0, ctx->stream>>>(nbr, 27 * n, (int32_t)n, d);
+    TB_LAUNCH_CHECK(ctx, "k_count_valid");
+    unsigned long long h = 0;
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(&h, d, sizeof(h), cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    *pairs = (int64_t)h;
+    return TB_OK;
+}
+
+extern "C" tb_status tb_zslab_counts(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord_stride,
+                                     int32_t z_min, int32_t nz, int64_t* counts) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (n < 0 || nz <= 0 || (coord_stride != 3 && coord_stride != 4) || !counts)
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_zslab_counts: bad arguments");
+    if (n > 0 && !coords) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_zslab_counts: null coords");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    TB_CUDA_TRY(ctx, cudaMemsetAsync(counts, 0, sizeof(int64_t) * (size_t)nz, ctx->stream));
+    if (n == 0) return TB_OK;
+    k_zslab_counts<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
+        coords, n, coord_stride, z_min, nz, reinterpret_cast<unsigned long long*>(counts));
+    TB_LAUNCH_CHECK(ctx, "k_zslab_counts");
+    return TB_OK;
+}
+
+extern "C" tb_status tb_gather_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t m,
+                                    int64_t row_bytes, void* out) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (m < 0 || row_bytes <= 0 || (row_bytes & 3))
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_gather_rows: m < 0 or row_bytes not a positive multiple of 4");
+    if (m == 0) return TB_OK;
+    if (!src || !rows || !out) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_gather_rows: null pointer");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    const int64_t threads = m * 32;
+    k_gather_rows<<<(unsigned)((threads + 255) / 256), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const uint32_t*>(src), rows, m, row_bytes / 4, reinterpret_cast<uint32_t*>(out));
+    TB_LAUNCH_CHECK(ctx, "k_gather_rows");
+    return TB_OK;
+}

@@ -1,0 +1,154 @@
+// C++ host mirror of the reference's sparse.h host functions, over the C ABI (see
+// include/trellis_sparse.hpp). Uploads host inputs, runs the device path, reads back.
+#include "trellis_sparse.hpp"
+
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+
+namespace trellis {
+namespace {
+
+int g_device = 0;
+
+struct Ctx {
+    tb_ctx* ctx = nullptr;
+    explicit Ctx(int dev) {
+        if (tb_ctx_create(dev, nullptr, &ctx) != TB_OK) throw std::runtime_error("trellis: tb_ctx_create failed");
+    }
+    ~Ctx() { tb_ctx_destroy(ctx); }
+};
+
+tb_ctx* ctx() {
+    thread_local std::unique_ptr<Ctx> c;
+    thread_local int dev = -1;
+    if (!c || dev != g_device) {
+        c.reset();
+        c.reset(new Ctx(g_device));
+        dev = g_device;
+    }
+    return c->ctx;
+}
+
+void ok(tb_status s, const char* what) {
+    if (s != TB_OK)
+        throw std::runtime_error(std::string("trellis: ") + what + ": " + tb_status_string(s) + " (" +
+                                 tb_ctx_last_error(ctx()) + ")");
+}
+
+void cuda_ok(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string("trellis: ") + what + ": " + cudaGetErrorString(e));
+}
+
+// Device buffer owned by the caller's scope.
+struct DBuf {
+    void* p = nullptr;
+    explicit DBuf(size_t bytes) { cuda_ok(cudaMalloc(&p, bytes ? bytes : 16), "cudaMalloc"); }
+    ~DBuf() { cudaFree(p); }
+    template <class T> T* as() const { return reinterpret_cast<T*>(p); }
+};
+
+uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return (uint16_t)((u >> 16) | 0x40);   // NaN
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// IEEE binary32 -> binary16, round to nearest even (subnormals and overflow included).
+uint16_t f32_to_f16_rne(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    const uint32_t sign = (u >> 16) & 0x8000u;
+    const uint32_t absu = u & 0x7FFFFFFFu;
+    if (absu >= 0x7F800000u) return (uint16_t)(sign | 0x7C00u | (absu > 0x7F800000u ? 0x200u : 0u));
+    if (absu >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u);   // rounds to >= 65520: inf
+    const int exp = (int)(absu >> 23) - 127;
+    if (exp >= -14) {   // normal half
+        uint32_t mant = absu & 0x7FFFFFu;
+        uint32_t h = ((uint32_t)(exp + 15) << 10) | (mant >> 13);
+        const uint32_t rem = mant & 0x1FFFu;
+        if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+        return (uint16_t)(sign | h);
+    }
+    if (exp < -25) return (uint16_t)sign;   // below half the smallest subnormal
+    // subnormal: value = mant_full * 2^(exp-23), half subnormal unit = 2^-24
+    const uint32_t mant_full = (absu & 0x7FFFFFu) | 0x800000u;
+    const int drop = -exp - 1;              // right shift that lands on 2^-24 units (14..24)
+    uint32_t h = mant_full >> drop;
+    const uint32_t rem = mant_full & ((1u << drop) - 1u);
+    const uint32_t halfway = 1u << (drop - 1);
+    if (rem > halfway || (rem == halfway && (h & 1u))) ++h;
+    return (uint16_t)(sign | h);
+}
+
+}  // namespace
+
+void set_device(int device) { g_device = device; }
+
+std::vector<int32_t> build_neighbor_table(const std::vector<std::array<int, 3>>& coords) {
+    const int64_t n = (int64_t)coords.size();
+    std::vector<int32_t> nbr((size_t)27 * n);
+    if (n == 0) return nbr;
+    cuda_ok(cudaSetDevice(g_device), "cudaSetDevice");
+    DBuf dc((size_t)n * 12), dn((size_t)n * 27 * 4);
+    cuda_ok(cudaMemcpy(dc.p, coords.data(), (size_t)n * 12, cudaMemcpyHostToDevice), "upload coords");
+    ok(tb_build_neighbor_map(ctx(), dc.as<int32_t>(), n, 3, dn.as<int32_t>()), "tb_build_neighbor_map");
+    cuda_ok(cudaMemcpy(nbr.data(), dn.p, nbr.size() * 4, cudaMemcpyDeviceToHost), "download nbr");
+    ok(tb_ctx_check_device(ctx()), "neighbor map device check");
+    return nbr;
+}
+
+std::vector<float> sparse_submconv(const ConvWeights& w, const std::vector<float>& feats,
+                                   const std::vector<int32_t>& nbr, int N, tb_epilogue epi) {
+    if ((int64_t)feats.size() != (int64_t)N * w.ci || (int64_t)nbr.size() != (int64_t)27 * N)
+        throw std::runtime_error("trellis: sparse_submconv: feats/nbr size mismatch");
+    std::vector<float> out((size_t)N * w.co);
+    if (N == 0) return out;
+    cuda_ok(cudaSetDevice(g_device), "cudaSetDevice");
+    const size_t es = w.dtype == TB_F32 ? 4 : 2;
+    DBuf df((size_t)N * w.ci * es), dn((size_t)N * 27 * 4), dout((size_t)N * w.co * 4);
+    if (w.dtype == TB_F32) {
+        cuda_ok(cudaMemcpy(df.p, feats.data(), feats.size() * 4, cudaMemcpyHostToDevice), "upload feats");
+    } else {
+        std::vector<uint16_t> h(feats.size());
+        for (size_t k = 0; k < feats.size(); ++k)
+            h[k] = w.dtype == TB_BF16 ? f32_to_bf16_rne(feats[k]) : f32_to_f16_rne(feats[k]);
+        cuda_ok(cudaMemcpy(df.p, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "upload feats");
+    }
+    cuda_ok(cudaMemcpy(dn.p, nbr.data(), nbr.size() * 4, cudaMemcpyHostToDevice), "upload nbr");
+    ok(tb_submconv(ctx(), dn.as<int32_t>(), N, df.p, w.ci, w.weight, w.bias, w.co, w.dtype, TB_F32, epi, dout.p),
+       "tb_submconv");
+    cuda_ok(cudaMemcpy(out.data(), dout.p, out.size() * 4, cudaMemcpyDeviceToHost), "download out");
+    ok(tb_ctx_check_device(ctx()), "conv device check");
+    return out;
+}
+
+SubdivideResult subdivide(const std::vector<std::array<int, 3>>& coords, const std::vector<uint8_t>& mask) {
+    const int64_t n = (int64_t)coords.size();
+    if ((int64_t)mask.size() != 8 * n) throw std::runtime_error("trellis: subdivide: mask must have 8*N entries");
+    SubdivideResult r;
+    r.mstart.assign((size_t)n + 1, 0);
+    if (n == 0) return r;
+    int64_t mmax = 0;
+    for (uint8_t v : mask) mmax += v != 0;
+    cuda_ok(cudaSetDevice(g_device), "cudaSetDevice");
+    DBuf dc((size_t)n * 12), dm((size_t)n * 8), dch((size_t)mmax * 12), dg((size_t)mmax * 4), ds((size_t)(n + 1) * 4);
+    cuda_ok(cudaMemcpy(dc.p, coords.data(), (size_t)n * 12, cudaMemcpyHostToDevice), "upload coords");
+    cuda_ok(cudaMemcpy(dm.p, mask.data(), (size_t)n * 8, cudaMemcpyHostToDevice), "upload mask");
+    int64_t m = 0;
+    ok(tb_subdivide(ctx(), dc.as<int32_t>(), n, 3, dm.as<uint8_t>(), dch.as<int32_t>(), dg.as<int32_t>(),
+                    ds.as<int32_t>(), mmax, &m), "tb_subdivide");
+    r.coords.resize((size_t)m);
+    r.gidx.resize((size_t)m);
+    cuda_ok(cudaMemcpy(r.coords.data(), dch.p, (size_t)m * 12, cudaMemcpyDeviceToHost), "download children");
+    cuda_ok(cudaMemcpy(r.gidx.data(), dg.p, (size_t)m * 4, cudaMemcpyDeviceToHost), "download gidx");
+    cuda_ok(cudaMemcpy(r.mstart.data(), ds.p, (size_t)(n + 1) * 4, cudaMemcpyDeviceToHost), "download mstart");
+    return r;
+}
+
+}  // namespace trellis

@@ -1,0 +1,187 @@
+"""Host-side operator mirror of the reference's sparse op layer, over the C ABI.
+
+Names and argument meanings follow pwilkin/trellis.cpp's ``include/sparse.h``:
+
+* :func:`build_neighbor_table` -- ``trellis::build_neighbor_table`` (sparse.h:14-17)
+* :func:`sparse_submconv` -- ``trellis::sparse_submconv`` (sparse.h:19-22), with explicit
+  weight / bias tensors in place of a Model + name prefix
+* :func:`subdivide` / :func:`c2s_gather` -- the subdivide and channel-to-spatial steps of
+  ``trellis::sparse_c2s`` (src/sparse.cpp:205-222, 263-266, 288, 307)
+* :func:`submconv_stack_host` -- a host-buffer stage run (upload, map, convs, read back), the
+  shape of ``run1`` / ``GraphRun::run`` (src/shape_decoder.cpp:34-51)
+
+Device tensors are torch CUDA tensors used only as memory; every computation runs in
+libtb_sparse.so. Errors raise :class:`TBError` (the reference throws std::runtime_error).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import TBError, check  # noqa: F401
+
+_DT = {torch.float32: _lib.TB_F32, torch.float16: _lib.TB_F16, torch.bfloat16: _lib.TB_BF16}
+_EPI = {"none": _lib.TB_EPI_NONE, None: _lib.TB_EPI_NONE, "silu": _lib.TB_EPI_SILU}
+_ctxs: dict = {}
+
+
+def _ptr(t) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def context(device=None):
+    """The per-device tb_ctx, bound to torch's current stream on that device."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index or 0)
+    lib = _lib.load()
+    h = _ctxs.get(dev.index)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    if h is None:
+        h = ctypes.c_void_p()
+        check(lib.tb_ctx_create(dev.index, ctypes.c_void_p(stream), ctypes.byref(h)), "tb_ctx_create")
+        _ctxs[dev.index] = h
+    else:
+        check(lib.tb_ctx_set_stream(h, ctypes.c_void_p(stream)), "tb_ctx_set_stream", h)
+    return h
+
+
+def check_device(device=None):
+    """Synchronise and raise if a kernel reported a failed device-side check."""
+    ctx = context(device)
+    check(_lib.load().tb_ctx_check_device(ctx), "tb_ctx_check_device", ctx)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise ValueError("expected contiguous CUDA tensors")
+
+
+def build_neighbor_table(coords: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Tap-major int32 [27*N] neighbor map (sentinel N) of int32 coords [N,3] or [N,4]."""
+    _need_cuda(coords)
+    if coords.dtype != torch.int32 or coords.dim() != 2 or coords.shape[1] not in (3, 4):
+        raise ValueError("coords must be int32 [N,3] or [N,4]")
+    n = coords.shape[0]
+    if out is None:
+        out = torch.empty(27 * n, dtype=torch.int32, device=coords.device)
+    ctx = context(coords.device)
+    check(_lib.load().tb_build_neighbor_map(ctx, _ptr(coords), n, coords.shape[1], _ptr(out)),
+          "tb_build_neighbor_map", ctx)
+    return out
+
+
+def count_valid_pairs(nbr: torch.Tensor, n: int) -> int:
+    _need_cuda(nbr)
+    ctx = context(nbr.device)
+    v = ctypes.c_int64()
+    check(_lib.load().tb_count_valid_pairs(ctx, _ptr(nbr), n, ctypes.byref(v)), "tb_count_valid_pairs", ctx)
+    return int(v.value)
+
+
+def sparse_submconv(feats: torch.Tensor, nbr: torch.Tensor, weight: torch.Tensor,
+                    bias: torch.Tensor | None = None, epi: str = "none", out_dtype=None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = epi(bias + sum_t W_t . feats[nbr_t]), feats [N,Ci], weight [Co,27,Ci] or
+    [Co,3,3,3,Ci] (same dtype as feats), bias float32 [Co] or None."""
+    _need_cuda(feats, nbr, weight, bias)
+    if feats.dtype not in _DT or weight.dtype != feats.dtype:
+        raise ValueError("feats and weight must share a dtype among float32/float16/bfloat16")
+    n, ci = feats.shape
+    co = weight.shape[0]
+    if weight.numel() != co * 27 * ci:
+        raise ValueError("weight must be [Co,27,Ci]")
+    if bias is not None and (bias.dtype != torch.float32 or bias.numel() != co):
+        raise ValueError("bias must be float32 [Co]")
+    if nbr.numel() != 27 * n:
+        raise ValueError("nbr must have 27*N entries")
+    od = feats.dtype if out_dtype is None else out_dtype
+    if out is None:
+        out = torch.empty((n, co), dtype=od, device=feats.device)
+    ctx = context(feats.device)
+    check(_lib.load().tb_submconv(ctx, _ptr(nbr), n, _ptr(feats), ci, _ptr(weight), _ptr(bias), co,
+                                  _DT[feats.dtype], _DT[od], _EPI[epi], _ptr(out)), "tb_submconv", ctx)
+    return out
+
+
+def subdivide(coords: torch.Tensor, mask: torch.Tensor, max_children: int | None = None):
+    """(child coords [M,s], gidx [M], mstart [N+1]) for uint8/bool mask [N,8]."""
+    _need_cuda(coords, mask)
+    n, s = coords.shape
+    m8 = mask.to(torch.uint8).contiguous() if mask.dtype != torch.uint8 else mask
+    if max_children is None:
+        max_children = 8 * n
+    child = torch.empty((max_children, s), dtype=torch.int32, device=coords.device)
+    gidx = torch.empty(max_children, dtype=torch.int32, device=coords.device)
+    mstart = torch.empty(n + 1, dtype=torch.int32, device=coords.device)
+    m = ctypes.c_int64()
+    ctx = context(coords.device)
+    check(_lib.load().tb_subdivide(ctx, _ptr(coords), n, s, _ptr(m8), _ptr(child), _ptr(gidx), _ptr(mstart),
+                                   max_children, ctypes.byref(m)), "tb_subdivide", ctx)
+    return child[: m.value], gidx[: m.value], mstart
+
+
+def c2s_gather(src: torch.Tensor, gidx: torch.Tensor, c: int) -> torch.Tensor:
+    """Child m takes row gidx[m] of src viewed as [8N, c]."""
+    _need_cuda(src, gidx)
+    m = gidx.numel()
+    out = torch.empty((m, c), dtype=src.dtype, device=src.device)
+    ctx = context(src.device)
+    check(_lib.load().tb_c2s_gather(ctx, _ptr(src), _ptr(gidx), m, c, _DT[src.dtype], _ptr(out)),
+          "tb_c2s_gather", ctx)
+    return out
+
+
+def bias_act(x: torch.Tensor, bias: torch.Tensor | None = None, epi: str = "silu") -> torch.Tensor:
+    _need_cuda(x, bias)
+    n, c = x.shape
+    ctx = context(x.device)
+    check(_lib.load().tb_bias_act(ctx, _ptr(x), n, c, _ptr(bias), _DT[x.dtype], _EPI[epi]), "tb_bias_act", ctx)
+    return x
+
+
+def gather_rows(src: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
+    _need_cuda(src, rows)
+    m = rows.numel()
+    out = torch.empty((m,) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+    row_bytes = src[0].numel() * src.element_size() if src.shape[0] else 4
+    ctx = context(src.device)
+    check(_lib.load().tb_gather_rows(ctx, _ptr(src), _ptr(rows), m, row_bytes, _ptr(out)), "tb_gather_rows", ctx)
+    return out
+
+
+def zslab_counts(coords: torch.Tensor, z_min: int, nz: int) -> torch.Tensor:
+    _need_cuda(coords)
+    counts = torch.empty(nz, dtype=torch.int64, device=coords.device)
+    ctx = context(coords.device)
+    check(_lib.load().tb_zslab_counts(ctx, _ptr(coords), coords.shape[0], coords.shape[1], z_min, nz,
+                                      _ptr(counts)), "tb_zslab_counts", ctx)
+    return counts
+
+
+def submconv_stack_host(coords: np.ndarray, feats: np.ndarray, layers, dtype: torch.dtype,
+                        out_dtype: torch.dtype, out: np.ndarray | None = None, device=None) -> np.ndarray:
+    """Host coords + host feats in, host features out, through ``tb_submconv_stack_host``.
+
+    ``layers`` is a list of (weight, bias, epi) with device weight [Co,27,Ci] / bias [Co].
+    ``feats`` holds the raw bits of ``dtype`` (np.uint16 for f16/bf16, float32 for f32)."""
+    coords = np.ascontiguousarray(coords, dtype=np.int32)
+    n, s = coords.shape
+    arr = (_lib.ConvLayer * len(layers))()
+    for k, (w, b, epi) in enumerate(layers):
+        arr[k].weight = w.data_ptr()
+        arr[k].bias = b.data_ptr() if b is not None else None
+        arr[k].ci = w.shape[-1]
+        arr[k].co = w.shape[0]
+        arr[k].epi = _EPI[epi]
+    co = layers[-1][0].shape[0]
+    if out is None:
+        out = np.empty((n, co), dtype=np.float32 if out_dtype == torch.float32 else np.uint16)
+    ctx = context(device if device is not None else layers[0][0].device)
+    check(_lib.load().tb_submconv_stack_host(
+        ctx, coords.ctypes.data_as(ctypes.c_void_p), n, s, feats.ctypes.data_as(ctypes.c_void_p), arr,
+        len(layers), _DT[dtype], _DT[out_dtype], out.ctypes.data_as(ctypes.c_void_p)),
+        "tb_submconv_stack_host", ctx)
+    return out
