@@ -1,0 +1,387 @@
+#!/usr/bin/env python3
+"""Benchmark of the sparse submanifold-conv path on B200 (one JSON line on rank 0).
+
+Workload: the res-1024 noisy-sphere shell, ~4.9M active voxels, two
+stacked 3x3x3 submanifold convs at Cin=Cout=64, bf16 operands, fp32 accumulation.
+One step = build the neighbor map from the coordinates + conv(SiLU) + conv, with coords,
+features and weights resident in HBM. Metric: active voxels/s (whole job).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 (torchrun, one rank per GPU): the voxels are cut into z-slabs at voxel-count
+quantiles; each rank owns one slab plus a one-voxel halo exchanged over NCCL (send/recv)
+before each conv, builds its local neighbor map and computes its owned rows. Total work is
+fixed as N grows ("scaling": "strong").
+
+`--impl reference` times the reference algorithm's CPU implementation (the oracle port in
+oracle/, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "trellis.cpp_b200")
+WORKLOAD = "c4"
+CI = CO = 64
+METRIC = "active voxels/s, 3^3 submanifold conv x2 + neighbor map, ~4.9M voxels C=64 (config 4)"
+
+
+def _load_package():
+    if "trellis_cpp_b200" in sys.modules:
+        return sys.modules["trellis_cpp_b200"]
+    spec = importlib.util.spec_from_file_location(
+        "trellis_cpp_b200", os.path.join(PKG_DIR, "__init__.py"), submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["trellis_cpp_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def _profile_traffic():
+    """DRAM bytes per conv launch from the committed ncu summary, or None."""
+    p = os.path.join(ROOT, "profiles", "submconv_tc_c4.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("dram_bytes_per_launch_full_size"):
+            try:
+                return int(line.split("=")[1].strip().strip("`"))
+            except (IndexError, ValueError):
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples of one GPU (by UUID) while running."""
+
+    FIELDS = ["uuid", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.hw_slowdown",
+              "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
+              "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + ",".join(self.FIELDS), "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == len(self.FIELDS) and self.uuid in parts[0]:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in self.rows for k in range(4) if r[4 + k] == "Active"})
+        loaded = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
+        return {"sm_mhz": float(np.median(loaded)) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_reference_step(coords, nbr_full, feats, wt1, wt2, sample, nthreads):
+    """One bounded CPU step of the reference algorithm (oracle port): the full neighbor map
+    (single-threaded, as src/sparse.cpp:21-39 is) and both convs on `sample` output rows.
+    Returns seconds per voxel."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    n = coords.shape[0]
+    t0 = time.perf_counter()
+    oracle.build_neighbor_table(coords)
+    t_map = time.perf_counter() - t0
+    row0 = (n - sample) // 2
+    h = feats.copy()          # rows outside the sample stand in for the first conv's output
+    t0 = time.perf_counter()
+    oracle.submconv_f32_mt_range(nbr_full, feats, wt1, row0, sample, silu=True, nthreads=nthreads, out=h)
+    # the second conv reads neighbors of the sample rows; those rows' inputs are computed by
+    # the first conv in a full run, here they reuse the first conv's sample output region
+    oracle.submconv_f32_mt_range(nbr_full, h, wt2, row0, sample, nthreads=nthreads)
+    t_conv = time.perf_counter() - t0
+    return t_map / n + t_conv / sample, t_map, t_conv
+
+
+def _cpu_inputs(coords):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    rng = np.random.default_rng(1)
+    n = coords.shape[0]
+    feats = rng.standard_normal((n, CI), dtype=np.float32)
+    w1 = (rng.standard_normal((CO, 27, CI)) / np.sqrt(27 * CI)).astype(np.float32)
+    w2 = (rng.standard_normal((CO, 27, CO)) / np.sqrt(27 * CO)).astype(np.float32)
+    nbr = oracle.build_neighbor_table(coords)
+    return feats, oracle.weight_tap_major(w1), oracle.weight_tap_major(w2), nbr
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    pkg = _load_package()
+    from trellis_cpp_b200 import synth
+    del pkg
+    coords = synth.coords_for(WORKLOAD)
+    n = coords.shape[0]
+    nthreads = os.cpu_count() or 1
+    feats, wt1, wt2, nbr = _cpu_inputs(coords)
+    sample = min(n, 1 << 19)
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_reference_step(coords, nbr, feats, wt1, wt2, min(sample, 1 << 16), nthreads)
+    per_voxel = []
+    for _ in range(max(1, min(args.steps, 3))):
+        spv, _, _ = cpu_reference_step(coords, nbr, feats, wt1, wt2, sample, nthreads)
+        per_voxel.append(spv)
+    spv = float(np.median(per_voxel))
+    value = 1.0 / spv
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": args.gpus,
+        "steps": len(per_voxel), "warmup": min(args.warmup, 1), "ms_per_step": spv * n * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded noisy shell, random N(0,1) features, N(0,1/(27*64)) weights)",
+        "config": {"workload": "c4: res-1024 noisy shell, map + conv(SiLU) + conv, C=64", "voxels": n},
+        "cpu_baseline": {"value": value, "unit": "voxels/s", "cores": nthreads, "kind": "port",
+                         "sample": f"full single-threaded neighbor map over {n} voxels + both fp32 convs on "
+                                   f"{sample} output rows (threads={nthreads}); per-voxel times summed"},
+        "e2e": {"value": value, "unit": "voxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _load_package()
+    from trellis_cpp_b200 import ops, synth
+
+    coords_np = synth.coords_for(args.workload)
+    n_total = coords_np.shape[0]
+    g = torch.Generator(device=dev).manual_seed(1234)
+    w1 = (torch.randn((CO, 27, CI), device=dev, generator=g) / np.sqrt(27 * CI)).bfloat16()
+    w2 = (torch.randn((CO, 27, CO), device=dev, generator=g) / np.sqrt(27 * CO)).bfloat16()
+
+    if world > 1:
+        from trellis_cpp_b200 import dist as tbdist
+        runner = tbdist.SlabRunner(coords_np, CI, dev, g)
+        step = lambda: runner.step(w1, w2)  # noqa: E731
+        n_local = runner.n_owned
+        nbr_for_flops = None
+    else:
+        coords = torch.from_numpy(coords_np).to(dev)
+        feats = torch.randn((n_total, CI), device=dev, generator=g).bfloat16()
+        nbr = torch.empty(27 * n_total, dtype=torch.int32, device=dev)
+        h = torch.empty((n_total, CO), dtype=torch.bfloat16, device=dev)
+        out = torch.empty((n_total, CO), dtype=torch.bfloat16, device=dev)
+        conv_events = []
+
+        def step(record=False):
+            ops.build_neighbor_table(coords, out=nbr)
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e2 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                ops.sparse_submconv(feats, nbr, w1, None, epi="silu", out=h)
+                e1.record()
+                ops.sparse_submconv(h, nbr, w2, None, out=out)
+                e2.record()
+                conv_events.append((e0, e1, e2))
+            else:
+                ops.sparse_submconv(feats, nbr, w1, None, epi="silu", out=h)
+                ops.sparse_submconv(h, nbr, w2, None, out=out)
+        n_local = n_total
+        nbr_for_flops = nbr
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if nbr_for_flops is not None:
+        pairs = ops.count_valid_pairs(nbr_for_flops, n_total)
+    else:
+        pairs = runner.count_valid_pairs()
+    ops.check_device()
+
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    sampler = ClockSampler(uuid)
+    sampler.start()
+    time.sleep(0.8)   # nvidia-smi needs a moment before its first sample
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        if world > 1:
+            step()
+        else:
+            step(record=True)
+    t_end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    ms_total = t_start.elapsed_time(t_end)
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+        allp = torch.tensor([pairs], device=dev, dtype=torch.int64)
+        dist.all_reduce(allp)
+        pairs_total = int(allp.item())
+    else:
+        pairs_total = pairs
+    ops.check_device()
+    ms_step = ms_total / args.steps
+    value = n_total / (ms_step / 1e3)
+    flops_step = 2 * 2.0 * CI * CO * pairs_total          # two convs, algorithmic (present pairs)
+    eff_tflops = flops_step / (ms_step / 1e3) / 1e12
+    peak_tf, peak_bw, peak_kind = _peaks()
+
+    roofline = None
+    kernel_stats = {}
+    if world == 1:
+        c1 = [a.elapsed_time(b) for a, b, _ in conv_events]
+        c2 = [b.elapsed_time(c) for _, b, c in conv_events]
+        conv_ms = float(np.mean(c1 + c2))
+        flops_launch = 2.0 * CI * CO * pairs
+        achieved = flops_launch / (conv_ms / 1e3) / 1e12
+        traffic = _profile_traffic()
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                    "frac": achieved / peak_tf, "traffic": traffic,
+                    "peak_source": f"{peak_kind} bf16_tflops (burst)", "kernel": "k_submconv_tc<128>",
+                    "flops_per_launch": flops_launch}
+        kernel_stats = {"conv_ms_avg": conv_ms, "conv1_ms": float(np.mean(c1)), "conv2_ms": float(np.mean(c2)),
+                        "map_ms_est": ms_step - float(np.mean(c1)) - float(np.mean(c2))}
+
+    # ---- end to end through the host-buffer C-ABI call (pinned host in, host out)
+    e2e = None
+    if world == 1 and not args.no_e2e:
+        feats_h = torch.empty((n_total, CI), dtype=torch.bfloat16).pin_memory()
+        feats_h.copy_(feats.cpu())
+        coords_h = torch.from_numpy(coords_np).pin_memory()
+        out_h = torch.empty((n_total, CO), dtype=torch.bfloat16).pin_memory()
+        layers = [(w1, None, "silu"), (w2, None, "none")]
+        fe = feats_h.view(torch.int16).numpy()
+        oh = out_h.view(torch.int16).numpy()
+        ch = coords_h.numpy()
+        for _ in range(2):
+            ops.submconv_stack_host(ch, fe, layers, torch.bfloat16, torch.bfloat16, out=oh, device=dev)
+        k_e2e = max(3, min(args.steps, 10))
+        t0 = time.perf_counter()
+        for _ in range(k_e2e):
+            ops.submconv_stack_host(ch, fe, layers, torch.bfloat16, torch.bfloat16, out=oh, device=dev)
+        dt = (time.perf_counter() - t0) / k_e2e
+        e2e = {"value": n_total / dt, "unit": "voxels/s",
+               "h2d_bytes_per_step": int(coords_h.numel() * 4 + feats_h.numel() * 2),
+               "d2h_bytes_per_step": int(out_h.numel() * 2), "steps": k_e2e, "ms_per_step": dt * 1e3,
+               "call": "tb_submconv_stack_host"}
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        feats_c, wt1, wt2, nbr_c = _cpu_inputs(coords_np)
+        nthreads = os.cpu_count() or 1
+        sample = min(n_total, 1 << 18)
+        spv, t_map, t_conv = cpu_reference_step(coords_np, nbr_c, feats_c, wt1, wt2, sample, nthreads)
+        cpu_baseline = {"value": 1.0 / spv, "unit": "voxels/s", "cores": nthreads, "kind": "port",
+                        "sample": f"oracle port: full single-threaded neighbor map ({n_total} voxels, "
+                                  f"{t_map:.2f} s) + both fp32 convs on {sample} rows with {nthreads} threads "
+                                  f"({t_conv:.2f} s); per-voxel times summed"}
+
+    launches_per_step = 5   # hash clear, hash insert, neighbor lookup, conv, conv
+    if world > 1:
+        launches_per_step = runner.launches_per_step
+    if rank == 0:
+        clocks = sampler.summary()
+        line = {
+            "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded noisy shell, random N(0,1) features, N(0,1/(27*64)) weights)",
+            "config": {"workload": "c4: res-1024 noisy shell, neighbor map + conv(SiLU) + conv, C=64 bf16, "
+                                   "fp32 accumulate", "voxels": n_total, "voxels_per_gpu": n_local,
+                       "valid_pairs": pairs_total, "mean_valid_taps": pairs_total / n_total,
+                       "parallelism": f"zslab{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (features 625 MB, map 527 MB per step)"},
+            "effective_tflops": eff_tflops,
+            "dense27_equiv_tflops": 2 * 2.0 * 27 * CI * CO * n_total / (ms_step / 1e3) / 1e12,
+            "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps, "clocks": clocks, "kernels": kernel_stats,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        runner.close()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--workload", default=WORKLOAD, choices=["c4", "c4s"],
+                    help="c4 (default, the benchmark) or c4s (half scale, for profiler captures)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

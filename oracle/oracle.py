@@ -63,6 +63,10 @@ def lib():
         L.orc_submconv_f32_mt.restype = ctypes.c_int
         L.orc_submconv_f32_mt.argtypes = [_i32p, ctypes.c_int64, _f32p, ctypes.c_int, _f32p,
                                           _f32p, ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
+        L.orc_submconv_f32_mt_range.restype = ctypes.c_int
+        L.orc_submconv_f32_mt_range.argtypes = [_i32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _f32p,
+                                                ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int, _f32p,
+                                                ctypes.c_int]
         L.orc_subdivide.restype = ctypes.c_int64
         L.orc_subdivide.argtypes = [_i32p, ctypes.c_int64, ctypes.c_int, _u8p, _i32p, _i32p, _i32p]
         L.orc_c2s_gather.restype = None
@@ -162,6 +166,24 @@ def submconv_f32_mt(nbr, feats, wt, bias=None, silu=False, nthreads=None, out=No
                                    _p(out, _f32p), nt)
     if rc != 0:
         raise ValueError("orc_submconv_f32_mt failed")
+    return out
+
+
+def submconv_f32_mt_range(nbr, feats, wt, row0, nrows, bias=None, silu=False, nthreads=None, out=None):
+    """Rows [row0, row0+nrows) of :func:`submconv_f32_mt` (a bounded sample for timing)."""
+    f = np.ascontiguousarray(feats, dtype=np.float32)
+    n, ci = f.shape
+    co = wt.shape[2]
+    if out is None:
+        out = np.empty((n, co), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    nb = np.ascontiguousarray(nbr, dtype=np.int32)
+    nt = nthreads or os.cpu_count() or 1
+    rc = lib().orc_submconv_f32_mt_range(_p(nb, _i32p), n, row0, nrows, _p(f, _f32p), ci, _p(wt, _f32p),
+                                         None if b is None else _p(b, _f32p), co, 1 if silu else 0,
+                                         _p(out, _f32p), nt)
+    if rc != 0:
+        raise ValueError("orc_submconv_f32_mt_range failed")
     return out
 
 

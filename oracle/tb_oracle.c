@@ -169,17 +169,19 @@ void orc_weight_tap_major(const float* w, int ci, int co, float* wt) {
 
 typedef struct {
     const int32_t* nbr; int64_t n; const float* feats; int ci; const float* wt;
-    const float* bias; int co; int epi; float* out; int64_t b0, b1;
+    const float* bias; int co; int epi; float* out; int64_t i_begin, i_end;
 } orc_mt_job;
 
+/* Output rows [i_begin, i_end) in blocks of 32; out row k of the job's range is written to
+ * out[(i - row0) * co] where row0 is the first row of the whole call (the caller offsets out). */
 static void* orc_mt_worker(void* arg) {
     enum { B = 32 };
     const orc_mt_job* J = (const orc_mt_job*)arg;
     const int64_t n = J->n; const int ci = J->ci, co = J->co;
     float* acc = (float*)malloc(sizeof(float) * (size_t)B * co);
     if (!acc) return (void*)1;
-    for (int64_t bi = J->b0; bi < J->b1; ++bi) {
-        int64_t i0 = bi * B, nb = (n - i0 < B) ? (n - i0) : B;
+    for (int64_t i0 = J->i_begin; i0 < J->i_end; i0 += B) {
+        const int64_t nb = (J->i_end - i0 < B) ? (J->i_end - i0) : B;
         for (int64_t r = 0; r < nb; ++r)
             for (int o = 0; o < co; ++o) acc[r * co + o] = J->bias ? J->bias[o] : 0.f;
         for (int t = 0; t < 27; ++t) {
@@ -207,20 +209,22 @@ static void* orc_mt_worker(void* arg) {
     return NULL;
 }
 
-/* nthreads worker threads (pthreads), each over a contiguous range of 32-voxel blocks. */
-int orc_submconv_f32_mt(const int32_t* nbr, int64_t n, const float* feats, int ci,
-                        const float* wt, const float* bias, int co, int epi, float* out,
-                        int nthreads) {
-    if (n < 0 || ci <= 0 || co <= 0) return -1;
+/* Rows [row0, row0 + nrows) of the conv over all n voxels (nbr is the full tap-major map,
+ * sentinel n), on nthreads pthreads. out points at row 0 of a [n][Co] buffer. */
+int orc_submconv_f32_mt_range(const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                              const float* feats, int ci, const float* wt, const float* bias, int co,
+                              int epi, float* out, int nthreads) {
+    if (n < 0 || ci <= 0 || co <= 0 || row0 < 0 || nrows < 0 || row0 + nrows > n) return -1;
     if (nthreads < 1) nthreads = 1;
     if (nthreads > 256) nthreads = 256;
-    const int64_t nblk = (n + 31) / 32;
+    const int64_t nblk = (nrows + 31) / 32;
     orc_mt_job jobs[256];
     pthread_t th[256];
     int rc = 0;
     for (int k = 0; k < nthreads; ++k) {
-        orc_mt_job j = { nbr, n, feats, ci, wt, bias, co, epi, out,
-                         nblk * k / nthreads, nblk * (k + 1) / nthreads };
+        int64_t b0 = nblk * k / nthreads, b1 = nblk * (k + 1) / nthreads;
+        int64_t e = row0 + b1 * 32;
+        orc_mt_job j = { nbr, n, feats, ci, wt, bias, co, epi, out, row0 + b0 * 32, e < row0 + nrows ? e : row0 + nrows };
         jobs[k] = j;
     }
     for (int k = 1; k < nthreads; ++k)
@@ -228,6 +232,12 @@ int orc_submconv_f32_mt(const int32_t* nbr, int64_t n, const float* feats, int c
     if (orc_mt_worker(&jobs[0])) rc = -1;
     for (int k = 1; k < nthreads; ++k) { void* r = NULL; pthread_join(th[k], &r); if (r) rc = -1; }
     return rc;
+}
+
+int orc_submconv_f32_mt(const int32_t* nbr, int64_t n, const float* feats, int ci,
+                        const float* wt, const float* bias, int co, int epi, float* out,
+                        int nthreads) {
+    return orc_submconv_f32_mt_range(nbr, n, 0, n, feats, ci, wt, bias, co, epi, out, nthreads);
 }
 
 /* ---- subdivide: src/sparse.cpp:205-222 ------------------------------------------------

@@ -17,8 +17,9 @@ TORCH_DT = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
 TOL = {"bf16": 1e-2, "f16": 1e-2, "f32": 1e-4}
 
 
-def _run(coords, feats, weight, bias, dtype, epi="none", out_dtype=None, nbr=None):
+def _run(coords, feats, weight, bias, dtype, epi="none", out_dtype=None, nbr=None, path="auto"):
     from trellis_cpp_b200 import ops
+    ops.set_conv_path(path)
     dt = TORCH_DT[dtype]
     c = torch.from_numpy(np.ascontiguousarray(coords, dtype=np.int32)).cuda()
     if nbr is None:
@@ -27,8 +28,11 @@ def _run(coords, feats, weight, bias, dtype, epi="none", out_dtype=None, nbr=Non
     co = weight.shape[0]
     w = torch.from_numpy(np.ascontiguousarray(weight, dtype=np.float32).reshape(co, 27, -1)).cuda().to(dt)
     b = None if bias is None else torch.from_numpy(np.ascontiguousarray(bias, dtype=np.float32)).cuda()
-    out = ops.sparse_submconv(f, nbr, w, b, epi=epi, out_dtype=TORCH_DT[out_dtype] if out_dtype else None)
-    ops.check_device()
+    try:
+        out = ops.sparse_submconv(f, nbr, w, b, epi=epi, out_dtype=TORCH_DT[out_dtype] if out_dtype else None)
+        ops.check_device()
+    finally:
+        ops.set_conv_path("auto")
     return out.float().cpu().numpy(), nbr
 
 
@@ -59,12 +63,18 @@ def test_golden_half_modes(tb, golden, dtype):
     assert max_rel(out, ref) < 1e-4
 
 
-@pytest.mark.parametrize("ci,co", [(16, 16), (32, 32), (64, 64), (64, 128), (128, 64), (128, 128),
-                                   (256, 256), (32, 128), (256, 32), (64, 512), (512, 512)])
+SHAPES = [(16, 16), (32, 32), (64, 64), (64, 128), (128, 64), (128, 128), (256, 256), (32, 128), (256, 32),
+          (64, 512), (512, 512), (64, 16), (192, 48)]
+
+
+@pytest.mark.parametrize("path", ["gather", "brick"])
+@pytest.mark.parametrize("ci,co", SHAPES)
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-def test_channel_shapes(tb, ci, co, dtype):
+def test_channel_shapes(tb, ci, co, dtype, path):
+    if path == "brick" and ci % 64:
+        pytest.skip("the brick kernel takes ci multiples of 64")
     coords, feats, w, b = _problem(3000, ci, co, 20, ci * 7 + co, dtype)
-    out, nbr = _run(coords, feats, w, b, dtype, out_dtype="f32")
+    out, nbr = _run(coords, feats, w, b, dtype, out_dtype="f32", path=path)
     ref = oracle.submconv(nbr.cpu().numpy(), feats, w, b)
     assert max_rel(out, ref) < 1e-4
 
@@ -85,10 +95,11 @@ def test_silu_epilogue_and_low_precision_output(tb, dtype):
     assert max_rel(out, ref) < TOL[dtype]
 
 
+@pytest.mark.parametrize("path", ["gather", "brick"])
 @pytest.mark.parametrize("n", [1, 2, 127, 128, 129, 255, 1000])
-def test_sizes_and_partial_tiles(tb, n):
+def test_sizes_and_partial_tiles(tb, n, path):
     coords, feats, w, b = _problem(n, 64, 64, 16, n, "bf16")
-    out, nbr = _run(coords, feats, w, b, "bf16", out_dtype="f32")
+    out, nbr = _run(coords, feats, w, b, "bf16", out_dtype="f32", path=path)
     ref = oracle.submconv(nbr.cpu().numpy(), feats, w, b)
     assert max_rel(out, ref) < 1e-4
 
@@ -104,11 +115,12 @@ def test_isolated_voxels_only_centre_tap(tb):
     assert max_rel(out, ref) < 1e-4
 
 
-def test_duplicate_coordinates(tb):
+@pytest.mark.parametrize("ci", [32, 64])
+def test_duplicate_coordinates(tb, ci):
     rng = np.random.default_rng(2)
     c = rng.integers(0, 9, size=(1500, 3)).astype(np.int32)
-    feats = round_to(rng.standard_normal((1500, 32)).astype(np.float32), "bf16")
-    w = round_to(rng.standard_normal((32, 27, 32)).astype(np.float32) / 30, "bf16")
+    feats = round_to(rng.standard_normal((1500, ci)).astype(np.float32), "bf16")
+    w = round_to(rng.standard_normal((32, 27, ci)).astype(np.float32) / 30, "bf16")
     out, nbr = _run(c, feats, w, None, "bf16", out_dtype="f32")
     ref = oracle.submconv(nbr.cpu().numpy(), feats, w, None)
     assert max_rel(out, ref) < 1e-4
@@ -119,6 +131,19 @@ def test_deterministic(tb):
     a, nbr = _run(coords, feats, w, b, "bf16")
     c, _ = _run(coords, feats, w, b, "bf16", nbr=nbr)
     assert np.array_equal(a, c)
+
+
+def test_scattered_voxels_overflow_brick(tb):
+    # voxels spread over a large grid in random order: tile neighbor ranges exceed the brick
+    # capacity, so rows come through the global-memory fallback
+    rng = np.random.default_rng(5)
+    coords = random_voxels(6000, 200, 5)
+    rng.shuffle(coords)
+    feats = round_to(rng.standard_normal((6000, 64)).astype(np.float32), "bf16")
+    w = round_to((rng.standard_normal((64, 27, 64)) / 40).astype(np.float32), "bf16")
+    out, nbr = _run(coords, feats, w, None, "bf16", out_dtype="f32", path="brick")
+    ref = oracle.submconv(nbr.cpu().numpy(), feats, w, None)
+    assert max_rel(out, ref) < 1e-4
 
 
 def test_unsupported_shape_reports_status(tb):
@@ -136,10 +161,12 @@ def _sample_rows(n, k, seed):
     return rows
 
 
-@pytest.mark.parametrize("name,ci,co,dtype", [("c2", 256, 256, "f16"), ("c4", 64, 64, "bf16"),
-                                              ("c5_32", 32, 32, "f16"), ("c5_512", 512, 512, "f16")])
-def test_config_full_size_sampled_rows(tb, name, ci, co, dtype):
+@pytest.mark.parametrize("name,ci,co,dtype,path", [("c2", 256, 256, "f16", "auto"), ("c4", 64, 64, "bf16", "auto"),
+                                                   ("c4", 64, 64, "bf16", "gather"),
+                                                   ("c5_32", 32, 32, "f16", "auto"), ("c5_512", 512, 512, "f16", "auto")])
+def test_config_full_size_sampled_rows(tb, name, ci, co, dtype, path):
     from trellis_cpp_b200 import ops, synth
+    ops.set_conv_path(path)
     coords = synth.coords_for(name)
     n = coords.shape[0]
     rng = np.random.default_rng(11)
@@ -150,8 +177,11 @@ def test_config_full_size_sampled_rows(tb, name, ci, co, dtype):
     f = torch.randn((n, ci), device="cuda", generator=g).to(dt)
     w = (torch.randn((co, 27, ci), device="cuda", generator=g) / np.sqrt(27 * ci)).to(dt)
     b = (0.01 * torch.randn(co, device="cuda", generator=g)).float()
-    out = ops.sparse_submconv(f, nbr, w, b, out_dtype=torch.float32)
-    ops.check_device()
+    try:
+        out = ops.sparse_submconv(f, nbr, w, b, out_dtype=torch.float32)
+        ops.check_device()
+    finally:
+        ops.set_conv_path("auto")
     rows = _sample_rows(n, 3000, 3)
     ref = oracle.submconv_rows(nbr.cpu().numpy(), f.float().cpu().numpy(), w.float().cpu().numpy(), rows,
                                b.cpu().numpy())

@@ -16,6 +16,7 @@ STATUS = {0: "TB_OK", 1: "TB_ERR_INVALID_ARG", 2: "TB_ERR_UNSUPPORTED", 3: "TB_E
           4: "TB_ERR_OUT_OF_MEMORY", 5: "TB_ERR_DEVICE", 6: "TB_ERR_TOO_LARGE"}
 TB_F32, TB_F16, TB_BF16 = 0, 1, 2
 TB_EPI_NONE, TB_EPI_SILU = 0, 1
+TB_CONV_AUTO, TB_CONV_GATHER, TB_CONV_BRICK = 0, 1, 2
 
 # Every symbol include/tb_sparse.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -38,6 +39,7 @@ SIGNATURES = {
     "tb_ctx_set_stream": (_st, [_vp, _vp]),
     "tb_ctx_last_error": (ctypes.c_char_p, [_vp]),
     "tb_ctx_check_device": (_st, [_vp]),
+    "tb_ctx_set_conv_path": (_st, [_vp, _int]),
     "tb_build_neighbor_map": (_st, [_vp, _vp, _i64, _int, _vp]),
     "tb_count_valid_pairs": (_st, [_vp, _vp, _i64, ctypes.POINTER(_i64)]),
     "tb_submconv": (_st, [_vp, _vp, _i64, _vp, _int, _vp, _vp, _int, _int, _int, _int, _vp]),

@@ -29,6 +29,7 @@ struct tb_ctx {
     size_t host_stage_bytes = 0;
     std::string last_error;
     void* encode_tiled = nullptr;  // cuTensorMapEncodeTiled, fetched once
+    int conv_path = 0;             // tb_conv_path
 };
 
 // Record a failure on the context and return the status.
@@ -73,4 +74,8 @@ tb_status tb_conv_f32_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const f
                              const float* weight, const float* bias, int co, tb_epilogue epi,
                              float* out);
 bool tb_conv_tc_supported(int ci, int co);
+tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
+                               const void* weight, const float* bias, int co, tb_dtype dtype,
+                               tb_dtype out_dtype, tb_epilogue epi, void* out);
+bool tb_conv_brick_supported(int ci, int co);
 uint64_t tb_hash_capacity(int64_t n);

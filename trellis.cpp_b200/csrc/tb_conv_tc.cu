@@ -9,36 +9,40 @@
 //        A_t,k [128 x KC]  (gathered feature rows, bf16/f16, smem)
 //      x B_t,k [KC x NB]   (weight tap slice, smem)
 //
-// Roles (288 threads):
+// Roles (224 threads):
 //   warps 0-3  epilogue: tcgen05.ld the accumulator (warp w owns TMEM lanes 32w..32w+31,
 //              i.e. tile rows), add bias, optional SiLU, convert, store rows.
-//   warps 4-7  producers: stage the tile's 27x128 neighbor indices in smem, OR their
-//              presence bits into a tile tap mask, then for every present tap and channel
-//              chunk gather A with cp.async (absent rows are zero-filled by a src-size-0
-//              copy, the padded zero row of src/sparse.cpp:82-85) and issue one TMA load
-//              of B from the [Co][27*Ci] weight view.
-//   warp 8     MMA: one thread issues tcgen05.mma kind::f16 (M=128, N=NB, K=16) per
+//   warp 4     neighbor loader: copies the tile's 27x128 neighbor indices into one of two
+//              smem buffers and ORs their presence bits into the tile's tap mask, one or
+//              two tiles ahead of the producer.
+//   warp 5     producer: for every present tap and channel chunk, each lane issues one TMA
+//              tile::gather4 (4 feature rows -> swizzled smem rows of A); absent rows use
+//              the row index N, which is out of bounds and arrives zero-filled (the padded
+//              zero row of src/sparse.cpp:82-85). Lane 0 adds one TMA load of B from the
+//              [Co][27*Ci] weight view. All of it completes on the stage's mbarrier.
+//   warp 6     MMA: one thread issues tcgen05.mma kind::f16 (M=128, N=NB, K=16) per
 //              16-channel step and tcgen05.commit to release smem stages and hand the
 //              accumulator to the epilogue. Two accumulator buffers let the epilogue of
 //              tile i overlap the MMAs of tile i+1.
-// Taps that no row of a tile has are skipped for the whole tile.
+// Taps that no row of a tile has are skipped for the whole tile. TMA writes straight into
+// shared memory, so the gather is not limited by the L1 left over after the smem carve-out.
 //
 // Every mbarrier wait is bounded (about 2 s of clock). On timeout the kernel records
 // TB_DEVERR_WAIT_TIMEOUT, raises a CTA abort flag that all waits observe, lets its own
 // copies land, drains its MMAs, frees TMEM and returns.
 #include "tb_common.cuh"
+#include "tb_tc_ptx.cuh"
 
 #include <algorithm>
-#include <cuda_bf16.h>
-#include <cuda_fp16.h>
 
 namespace {
 
+using namespace tbtc;
+
 constexpr int kTileM = 128;
-constexpr int kThreads = 288;
+constexpr int kThreads = 224;
 constexpr int kMaxStages = 8;
 constexpr int kNbrSmem = 27 * kTileM * 4;   // staged neighbor indices of one tile
-constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 1.9 GHz
 
 struct ConvParams {
     const int32_t* nbr;
@@ -46,6 +50,7 @@ struct ConvParams {
     const float* bias;
     uint8_t* out;
     int* err;
+    const int32_t* perm;    // optional tile order: tile position -> output row
     int64_t n;
     int ci, co;
     int out_kind;       // 0 f32, 1 f16, 2 bf16
@@ -57,148 +62,37 @@ struct ConvParams {
     uint32_t a_bytes, b_bytes, stage_bytes;
     uint32_t idesc;
     uint32_t tmem_cols;
+    long long* trace;   // TB_TRACE builds only: per-role event stamps of CTA 0, else null
 };
 
-// ---------------------------------------------------------------- PTX wrappers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-    return ok != 0;
-}
-// Bounded wait: false when the CTA aborted or the clock limit ran out (then aborts it).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitCycles) {
-            *abort_flag = 1;
-            atomicCAS(err, 0, TB_DEVERR_WAIT_TIMEOUT);
-            return false;
-        }
-        __nanosleep(64);
-    }
-}
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(bar) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.wait_all;" ::: "memory");
-}
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3}], [%4];"
-                 :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 :: "r"(bar) : "memory");
-}
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "setp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-                 :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
-}
-// K-major operand tile: rows of RB bytes, 8-row atoms, swizzle width = RB (32/64/128 B).
-template <int RB>
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-    constexpr uint64_t layout = RB == 128 ? 2 : (RB == 64 ? 4 : 6);
-    constexpr uint64_t sbo = (8 * RB) >> 4;
-    return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (sbo << 32) | (1ull << 46) | (layout << 61);
-}
-// Byte offset of 16-byte chunk c of row r inside a swizzled tile with RB-byte rows.
-template <int RB>
-__device__ __forceinline__ uint32_t swz_off(int r, int c) {
-    if (RB == 128) return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
-    if (RB == 64) return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-    return (uint32_t)(r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
-}
-
-#define TMEM_LD_X16(taddr, v)                                                              \
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "                                 \
-                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"          \
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),  \
-                   "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),\
-                   "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])                       \
-                 : "r"(taddr))
-
-__device__ __forceinline__ void tmem_wait_ld() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ float apply_epi(float v, int epi) {
-    return epi == TB_EPI_SILU ? v / (1.0f + __expf(-v)) : v;
-}
-
-// Store 16 consecutive output channels of one row.
-__device__ __forceinline__ void store16(uint8_t* dst, const float* v, int kind) {
-    if (kind == 0) {
-        float4* d = reinterpret_cast<float4*>(dst);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    } else {
-        uint32_t w[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            if (kind == 2) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
-                w[q] = *reinterpret_cast<uint32_t*>(&h);
-            } else {
-                __half2 h = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
-                w[q] = *reinterpret_cast<uint32_t*>(&h);
-            }
-        }
-        uint4* d = reinterpret_cast<uint4*>(dst);
-        d[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        d[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    }
-}
+// Pipeline tracing (compiled in with -DTB_TRACE): CTA 0 stamps clock64 at each hand-off into
+// p.trace laid out as [role][kTraceCap]; role 0 producer issue, 1 MMA full-wait done,
+// 2 epilogue accumulator ready, 3 epilogue done, 4 loader tile staged.
+constexpr int kTraceCap = 4096;
+#ifdef TB_TRACE
+#define TB_STAMP(role, idx)                                                                      \
+    do {                                                                                         \
+        if (p.trace && blockIdx.x == 0 && (idx) < kTraceCap) p.trace[(role) * kTraceCap + (idx)] = clock64(); \
+    } while (0)
+#else
+#define TB_STAMP(role, idx) do { } while (0)
+#endif
 
 template <int RB>
 __global__ void __launch_bounds__(kThreads, 1)
-k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const ConvParams p) {
-    constexpr int CH = RB / 16;          // 16-byte chunks per gathered row
+k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap fmap,
+              const ConvParams p) {
     constexpr int KSTEPS = RB / 32;      // K=16 MMAs per chunk
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
     uint8_t* stage_base = smem;
-    int32_t* s_nbr = reinterpret_cast<int32_t*>(smem + (size_t)p.stages * p.stage_bytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_nbr) + kNbrSmem);
-    // bars: full[kMaxStages] empty[kMaxStages] acc_full[2] acc_empty[2] prod_sync drain
-    uint32_t* s_hdr = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 6);
-    uint32_t* s_misc = s_hdr + kMaxStages;   // [0] tmem base, [1] tap mask, [2] abort
-    volatile int* s_abort = reinterpret_cast<volatile int*>(s_misc + 2);
+    int32_t* s_nbr = reinterpret_cast<int32_t*>(smem + (size_t)p.stages * p.stage_bytes);   // [2][27*128]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_nbr) + 2 * kNbrSmem);
+    // bars: full[kMaxStages] empty[kMaxStages] acc_full[2] acc_empty[2] nbr_full[2] nbr_empty[2] drain
+    uint32_t* s_hdr = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 9);
+    uint32_t* s_misc = s_hdr + kMaxStages;   // [0] tmem base, [1..2] tap masks, [3] abort
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_misc + 3);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -207,26 +101,28 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const ConvParams p) {
     auto empty_bar = [&](int s) { return bar0 + 8u * (kMaxStages + s); };
     auto accf_bar = [&](int b) { return bar0 + 8u * (2 * kMaxStages + b); };
     auto acce_bar = [&](int b) { return bar0 + 8u * (2 * kMaxStages + 2 + b); };
-    const uint32_t prod_bar = bar0 + 8u * (2 * kMaxStages + 4);
-    const uint32_t drain_bar = bar0 + 8u * (2 * kMaxStages + 5);
+    auto nbrf_bar = [&](int b) { return bar0 + 8u * (2 * kMaxStages + 4 + b); };
+    auto nbre_bar = [&](int b) { return bar0 + 8u * (2 * kMaxStages + 6 + b); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kMaxStages + 8);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
-            mbar_init(full_bar(s), 128 + 1);
+            mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(accf_bar(b), 1);
             mbar_init(acce_bar(b), 128);
+            mbar_init(nbrf_bar(b), 1);
+            mbar_init(nbre_bar(b), 1);
         }
-        mbar_init(prod_bar, 128);
         mbar_init(drain_bar, 1);
-        s_misc[1] = 0;
-        s_misc[2] = 0;
+        s_misc[3] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&fmap)) : "memory");
     }
-    if (warp == 8) {
+    if (warp == 6) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_u32(s_misc)), "r"(p.tmem_cols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -237,78 +133,88 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const ConvParams p) {
     const uint32_t tmem_base = s_misc[0];
 
     const int nunits = p.ntiles * p.ncb;
+    const int32_t sentinel = (int32_t)p.n;
 
-    if (warp >= 4 && warp < 8) {
-        // ------------------------------------------------------------------ producers
-        const int pt = threadIdx.x - 128;
+    if (warp == 4) {
+        // ------------------------------------------------------------------ neighbor loader
+        int it = 0;
+        for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
+            const int tile = u / p.ncb;
+            const int buf = it & 1;
+            const uint32_t ph = (it >> 1) & 1;
+            if (!mbar_wait(nbre_bar(buf), ph ^ 1, s_abort, p.err)) break;
+            const int64_t r0 = (int64_t)tile * kTileM;
+            int32_t* dst = s_nbr + buf * (27 * kTileM);
+            uint32_t bits = 0;
+#pragma unroll 3
+            for (int t = 0; t < 27; ++t) {
+                const int32_t* src = p.nbr + (int64_t)t * p.n + r0;
+                int32_t v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int64_t row = r0 + lane + 32 * q;
+                    v[q] = row < p.n ? __ldg(src + lane + 32 * q) : sentinel;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    dst[t * kTileM + lane + 32 * q] = v[q];
+                    bits |= (uint32_t)(v[q] != sentinel) << t;
+                }
+            }
+            bits = __reduce_or_sync(0xffffffffu, bits);
+            if (lane == 0) s_misc[1 + buf] = bits;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(nbrf_bar(buf));
+            if (lane == 0) TB_STAMP(4, it);
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------------------------ TMA producer
+        int gsi = 0;
         int stage = 0;
         uint32_t phase = 0;
-        uint32_t prod_phase = 0;
         bool ok = true;
-        // TMA loads issued by thread 0 whose completion has not been observed.
-        auto prod_sync = [&]() -> bool {
-            mbar_arrive(prod_bar);
-            const bool r = mbar_wait(prod_bar, prod_phase, s_abort, p.err);
-            prod_phase ^= 1;
-            return r;
-        };
-        for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-            const int tile = u / p.ncb, cb = u % p.ncb;
-            const int64_t r0 = (int64_t)tile * kTileM;
-            if (!prod_sync()) { ok = false; break; }            // previous unit done with s_nbr
-            for (int idx = pt; idx < 27 * kTileM; idx += 128) {
-                const int t = idx >> 7, r = idx & 127;
-                const int64_t row = r0 + r;
-                s_nbr[idx] = row < p.n ? __ldg(p.nbr + (int64_t)t * p.n + row) : (int32_t)p.n;
-            }
-            if (pt == 0) s_misc[1] = 0;
-            if (!prod_sync()) { ok = false; break; }
-            uint32_t bits = 0;
-#pragma unroll
-            for (int t = 0; t < 27; ++t) bits |= (uint32_t)(s_nbr[t * kTileM + pt] != (int32_t)p.n) << t;
-            bits = __reduce_or_sync(0xffffffffu, bits);
-            if (lane == 0) atomicOr(&s_misc[1], bits);
-            if (!prod_sync()) { ok = false; break; }
-            uint32_t taps = s_misc[1];
+        int it = 0;
+        for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++it) {
+            const int cb = u % p.ncb;
+            const int buf = it & 1;
+            const uint32_t ph = (it >> 1) & 1;
+            if (!mbar_wait(nbrf_bar(buf), ph, s_abort, p.err)) { ok = false; break; }
+            const int32_t* rows_s = s_nbr + buf * (27 * kTileM);
+            uint32_t taps = s_misc[1 + buf];
             const int nstages_unit = __popc(taps) * p.nkc;
             int si = 0;
             while (taps && ok) {
                 const int t = __ffs(taps) - 1;
                 taps &= taps - 1;
+                const int4 rows = *reinterpret_cast<const int4*>(rows_s + t * kTileM + 4 * lane);
                 for (int kc = 0; kc < p.nkc; ++kc, ++si) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1, s_abort, p.err)) { ok = false; break; }
-                    uint8_t* a_tile = stage_base + (size_t)stage * p.stage_bytes;
-                    const uint32_t a_addr = smem_u32(a_tile);
-                    const int c = pt % CH;
-#pragma unroll
-                    for (int j = 0; j < CH; ++j) {
-                        const int r = pt / CH + j * (kTileM / CH);
-                        const int32_t src_row = s_nbr[t * kTileM + r];
-                        const bool present = src_row != (int32_t)p.n;
-                        const uint8_t* src = present
-                            ? p.feats + ((int64_t)src_row * p.ci + (int64_t)kc * p.kc) * 2 + c * 16
-                            : p.feats;
-                        cp_async_16(a_addr + swz_off<RB>(r, c), src, present ? 16u : 0u);
-                    }
-                    cp_async_mbar_arrive_noinc(full_bar(stage));
-                    if (pt == 0) {
+                    const uint32_t a_addr = smem_u32(stage_base + (size_t)stage * p.stage_bytes);
+                    if (lane == 0) TB_STAMP(0, gsi);
+                    ++gsi;
+                    if (lane == 0) {
                         s_hdr[stage] = (si == 0 ? 1u : 0u) | (si == nstages_unit - 1 ? 2u : 0u);
-                        mbar_arrive_expect_tx(full_bar(stage), p.b_bytes);
-                        tma_load_2d(a_addr + p.a_bytes, &wmap, t * p.ci + kc * p.kc, cb * p.nb, full_bar(stage));
+                        mbar_arrive_expect_tx(full_bar(stage), p.a_bytes + p.b_bytes);
                     }
+                    __syncwarp();
+                    tma_gather4(a_addr + (uint32_t)(4 * lane * RB), &fmap, kc * p.kc, rows, full_bar(stage));
+                    if (lane == 0)
+                        tma_load_2d(a_addr + p.a_bytes, &wmap, t * p.ci + kc * p.kc, cb * p.nb, full_bar(stage));
                     if (++stage == p.stages) { stage = 0; phase ^= 1; }
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(nbre_bar(buf));   // row indices are in registers / issued
         }
-        cp_async_wait_all();
-        if (!ok && pt == 0) {
+        if (!ok && lane == 0) {
             // let this CTA's in-flight TMA loads land before the CTA can exit
             const long long t0 = clock64();
             while (clock64() - t0 < 4000000ll) __nanosleep(256);
         }
-    } else if (warp == 8) {
+    } else if (warp == 6) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
+            int gsi = 0;
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -322,7 +228,8 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const ConvParams p) {
                 bool first = true;
                 while (true) {
                     if (!mbar_wait(full_bar(stage), phase, s_abort, p.err)) { ok = false; break; }
-                    fence_proxy_async();
+                    TB_STAMP(1, gsi);
+                    ++gsi;
                     tc_fence_after();
                     const uint32_t hdr = s_hdr[stage];
                     const uint32_t a_addr = smem_u32(stage_base + (size_t)stage * p.stage_bytes);
@@ -349,14 +256,17 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const ConvParams p) {
         // ------------------------------------------------------------------ epilogue
         const int q = warp;          // TMEM lanes 32q..32q+31
         int it = 0;
+        const size_t esize = p.out_kind == 0 ? 4 : 2;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
             const int tile = u / p.ncb, cb = u % p.ncb;
             const int ab = it & 1;
             const uint32_t aph = (it >> 1) & 1;
             if (!mbar_wait(accf_bar(ab), aph, s_abort, p.err)) break;
+            if (threadIdx.x == 0) TB_STAMP(2, it);
             tc_fence_after();
-            const int64_t row = (int64_t)tile * kTileM + q * 32 + lane;
-            const size_t esize = p.out_kind == 0 ? 4 : 2;
+            const int64_t pos = (int64_t)tile * kTileM + q * 32 + lane;
+            const bool valid = pos < p.n;
+            const int64_t row = (valid && p.perm) ? (int64_t)__ldg(p.perm + pos) : pos;
             uint8_t* orow = p.out + ((size_t)row * p.co + (size_t)cb * p.nb) * esize;
             for (int c0 = 0; c0 < p.nb; c0 += 16) {
                 uint32_t v[16];
@@ -370,25 +280,27 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const ConvParams p) {
                     float x = __uint_as_float(v[j]) + (p.bias ? __ldg(p.bias + o) : 0.0f);
                     f[j] = apply_epi(x, p.epi);
                 }
-                if (row < p.n) store16(orow + (size_t)c0 * esize, f, p.out_kind);
+                if (valid) store16(orow + (size_t)c0 * esize, f, p.out_kind);
             }
             tc_fence_before();
             mbar_arrive(acce_bar(ab));
+            if (threadIdx.x == 0) TB_STAMP(3, it);
         }
     }
 
     __syncthreads();
-    if (warp == 8) {
+    if (warp == 6) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem_base), "r"(p.tmem_cols) : "memory");
     }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
 }  // namespace
+
+#ifdef TB_TRACE
+long long* g_trace_buffer = nullptr;
+extern "C" void tb_debug_set_trace(long long* buf) { g_trace_buffer = buf; }
+#endif
 
 bool tb_conv_tc_supported(int ci, int co) {
     const bool ci_ok = ci == 16 || ci == 32 || (ci > 0 && ci % 64 == 0);
@@ -414,6 +326,11 @@ tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const vo
     const int nb = co <= 256 ? co : 256;
     ConvParams p{};
     p.nbr = nbr;
+    p.perm = nullptr;
+    p.trace = nullptr;
+#ifdef TB_TRACE
+    p.trace = g_trace_buffer;
+#endif
     p.feats = reinterpret_cast<const uint8_t*>(feats);
     p.bias = bias;
     p.out = reinterpret_cast<uint8_t*>(out);
@@ -439,7 +356,7 @@ tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const vo
     const uint32_t fmt = dtype == TB_BF16 ? 1u : 0u;
     p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(nb >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
 
-    const size_t fixed = kNbrSmem + 8 * (2 * kMaxStages + 6) + 4 * (kMaxStages + 4) + 1024;
+    const size_t fixed = 2 * kNbrSmem + 8 * (2 * kMaxStages + 9) + 4 * (kMaxStages + 4) + 1024;
     const size_t budget = (size_t)ctx->max_smem_optin;
     int stages = (int)std::min<size_t>(kMaxStages, (budget - fixed) / p.stage_bytes);
     if (stages < 2) return tb_fail(ctx, TB_ERR_UNSUPPORTED, "tb_submconv: stage does not fit in shared memory");
@@ -461,19 +378,30 @@ tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const vo
         const_cast<void*>(weight), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the weight view");
+    // feature rows for tile::gather4: [n][ci], box = one row of kc channels; row index n is out
+    // of bounds and reads as zeros
+    CUtensorMap fmap;
+    const cuuint64_t fdim[2] = {(cuuint64_t)ci, (cuuint64_t)n};
+    const cuuint64_t fstride[1] = {(cuuint64_t)ci * 2};
+    const cuuint32_t fbox[2] = {(cuuint32_t)kc, 1};
+    cr = reinterpret_cast<EncodeTiledFn>(ctx->encode_tiled)(
+        &fmap, dtype == TB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+        const_cast<void*>(feats), fdim, fstride, fbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the feature view");
 
     const int units = p.ntiles * p.ncb;
     const int grid = std::min(units, ctx->num_sms);
     cudaError_t e;
     if (rb == 128) {
         e = cudaFuncSetAttribute(k_submconv_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) k_submconv_tc<128><<<grid, kThreads, smem, ctx->stream>>>(map, p);
+        if (e == cudaSuccess) k_submconv_tc<128><<<grid, kThreads, smem, ctx->stream>>>(map, fmap, p);
     } else if (rb == 64) {
         e = cudaFuncSetAttribute(k_submconv_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) k_submconv_tc<64><<<grid, kThreads, smem, ctx->stream>>>(map, p);
+        if (e == cudaSuccess) k_submconv_tc<64><<<grid, kThreads, smem, ctx->stream>>>(map, fmap, p);
     } else {
         e = cudaFuncSetAttribute(k_submconv_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) k_submconv_tc<32><<<grid, kThreads, smem, ctx->stream>>>(map, p);
+        if (e == cudaSuccess) k_submconv_tc<32><<<grid, kThreads, smem, ctx->stream>>>(map, fmap, p);
     }
     if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_submconv_tc)");
     TB_LAUNCH_CHECK(ctx, "k_submconv_tc");

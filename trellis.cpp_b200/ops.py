@@ -47,6 +47,13 @@ def context(device=None):
     return h
 
 
+def set_conv_path(path: str = "auto", device=None):
+    """Select the tensor-core conv kernel: "auto", "gather" or "brick" (tuning/testing)."""
+    ctx = context(device)
+    code = {"auto": _lib.TB_CONV_AUTO, "gather": _lib.TB_CONV_GATHER, "brick": _lib.TB_CONV_BRICK}[path]
+    check(_lib.load().tb_ctx_set_conv_path(ctx, code), "tb_ctx_set_conv_path", ctx)
+
+
 def check_device(device=None):
     """Synchronise and raise if a kernel reported a failed device-side check."""
     ctx = context(device)

@@ -8,6 +8,7 @@ Coordinates are int32 [N,4] = (b=0, x, y, z) in x-major lexicographic order.
   C2  grid 256,  shell |d - (100 + 8 n(p))| < 1, noise spacings 32/16/8 (seed 2)
   C3  the C2 shell; children kept where |d - r| < 0.5 at the child centre (seed 2)
   C4  grid 1024, shell |d - (440 + 16 n(p))| < 1, noise spacings 128/64/32 (seed 4)
+  C4s grid 512,  half-scale C4 (r=220+-8, spacings 64/32/16) for profiler captures
   C5  grid 512,  4096 boxes, edges U{4..32} per axis, union kept with p=0.3 (seed 5)
 """
 from __future__ import annotations
@@ -112,6 +113,8 @@ def coords_for(name: str, nthreads=None) -> np.ndarray:
         return shell(256, 100.0, 8.0, 32.0, 2, 2.0, nthreads)
     if name == "c4":
         return shell(1024, 440.0, 16.0, 128.0, 4, 2.0, nthreads)
+    if name == "c4s":   # half-scale C4 for profiler captures (still larger than L2)
+        return shell(512, 220.0, 8.0, 64.0, 4, 2.0, nthreads)
     if name.startswith("c5"):
         return boxes(512, 4096, 4, 32, 0.3, 5, nthreads)
     raise KeyError(name)
