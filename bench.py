@@ -301,7 +301,7 @@ def run_gpu(args):
         traffic = _profile_traffic()
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                     "frac": achieved / peak_tf, "traffic": traffic,
-                    "peak_source": f"{peak_kind} bf16_tflops (burst)", "kernel": "k_submconv_tc<128>",
+                    "peak_source": f"{peak_kind} bf16_tflops (burst)", "kernel": "k_submconv_brick",
                     "flops_per_launch": flops_launch}
         kernel_stats = {"conv_ms_avg": conv_ms, "conv1_ms": float(np.mean(c1)), "conv2_ms": float(np.mean(c2)),
                         "map_ms_est": ms_step - float(np.mean(c1)) - float(np.mean(c2))}

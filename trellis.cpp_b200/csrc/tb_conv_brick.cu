@@ -10,21 +10,30 @@
 // So each tile's neighbors are fetched once with large TMA boxes, and the per-tap gathers
 // become shared-memory reads.
 //
-// Per 64-channel chunk kc of a work unit (tile, output-column block cb):
-//   loader warp   stages the tile's 27x128 neighbor indices in smem, reduces them to the
-//                 three [min, max] row ranges, and loads those rows (channels kc*64..+63) as
-//                 32-row SW128 TMA boxes into one of two brick buffers. Rows beyond the
-//                 brick capacity stay in global memory.
-//   builder warps for each tap t, thread i (TMEM lane i = tile row i) reads its neighbor
-//   (4-7)         row from the brick (or global memory if it overflowed; zeros if absent,
-//                 the padded zero row of src/sparse.cpp:82-85) and writes it to a TMEM A slot
-//                 with tcgen05.st (row i in lane i, bf16 pairs per column).
-//   weight warp   TMA-loads the [nb x 64] weight slice of (t, kc) into a smem stage.
-//   MMA warp      tcgen05.mma kind::f16, A from TMEM, B from smem, D (fp32) in TMEM;
-//                 commits release the A slot, the weight stage and finally the accumulator.
-//   epilogue      warps 0-3: tcgen05.ld, bias, SiLU, convert, store each row once.
+// Per 64-channel chunk kc of a work unit (tile, output-column block cb) -- a "group" of 27
+// stages, one per tap, numbered by a running stage sequence:
+//   loader warp     stages the tile's 27x128 neighbor indices in smem, reduces them to the
+//                   three [min, max] row ranges, and loads those rows (channels kc*64..+63) as
+//                   32-row SW128 TMA boxes into one of two brick buffers. Rows beyond the
+//                   brick capacity stay in global memory.
+//   builder warps   two warpgroups take alternate stages. Thread i (TMEM lane i = tile row i)
+//   (4-11)          reads its neighbor row from the brick (or global memory if it overflowed;
+//                   zeros if absent, the padded zero row of src/sparse.cpp:82-85) and writes
+//                   it to a TMEM A slot with tcgen05.st (row i in lane i, bf16 pairs per
+//                   column). Each warp keeps two stages' rows in flight.
+//   weight warps    up to four warps, each owning every fourth stage, TMA-load the [nb x 64]
+//   (13-16)         weight slice of (tap, kc) into a smem stage (one thread's TMA issues
+//                   serialise, so several threads issue).
+//   MMA warps       tcgen05.mma kind::f16, A from TMEM, B from smem, D (fp32) in TMEM. For
+//   (17-18)         nb <= 64 two warps issue alternate stages into two accumulators, because
+//                   one issuing thread sustains one MMA per ~64 cycles, twice the math time of
+//                   a 128x64x16 MMA; the epilogue adds the two. Commits release the A slot,
+//                   the weight stage and finally the accumulator.
+//   epilogue        warps 0-3: tcgen05.ld, bias, SiLU, convert, store each row once.
 // All 27 taps are issued for every tile (absent neighbors are zero rows); in this voxel order
-// the union of present taps over 128 rows is 27 for almost every tile.
+// the union of present taps over 128 rows is 27 for almost every tile. Each unit starts its
+// tap sequence at tap (unit mod 27); the fp32 accumulation order therefore differs between
+// tiles but is fixed for a given launch shape.
 #include "tb_common.cuh"
 #include "tb_tc_ptx.cuh"
 
@@ -36,12 +45,36 @@ namespace {
 using namespace tbtc;
 
 constexpr int kTileM = 128;
-constexpr int kThreads = 352;        // 11 warps
+constexpr int kWarpBuild0 = 4;       // builders: warps 4-11
+constexpr int kWarpLoader = 12;
+constexpr int kWarpWeight0 = 13;     // weight producers: warps 13-16
+constexpr int kWeightWarps = 4;
+constexpr int kWarpMma0 = 17;        // MMA issuers: warps 17-18
+constexpr int kThreads = 19 * 32;
 constexpr int kBox = 32;             // rows per brick TMA box
 constexpr int kNbrInts = 27 * kTileM;
-constexpr int kNA = 8;               // TMEM A slots (32 columns each)
-constexpr int kMaxB = 4;             // weight smem stages
-constexpr int kNumBars = 2 + 2 + 2 + 2 + kNA + kNA + kMaxB + kMaxB + 2 + 2 + 1;
+constexpr int kNA = 8;               // TMEM A slots (32 columns each); a power of two
+constexpr int kMaxB = 8;             // weight smem stages (nbst is 2, 4 or 8)
+// nbrf[2] nbre[2] brkf[2] brke[2] af[8] ae[8] bf[8] be[8] df[2][2] de[2][2] drain
+constexpr int kNumBars = 2 + 2 + 2 + 2 + kNA + kNA + kMaxB + kMaxB + 4 + 4 + 1;
+
+// Pipeline tracing (compiled in with -DTB_TRACE): CTA 0 stamps clock64 into p.trace laid out
+// as [role][kTraceCap]: 0 loader brick issued, 1 builder A slot written, 2 MMA stage inputs
+// ready, 3 weight stage issued, 4 epilogue accumulator ready.
+constexpr int kTraceCap = 4096;
+#ifdef TB_TRACE
+#define TB_STAMP(role, idx)                                                                       \
+    do {                                                                                          \
+        if (p.trace && blockIdx.x == 0 && (idx) < kTraceCap) p.trace[(role) * kTraceCap + (idx)] = clock64(); \
+    } while (0)
+#define TB_PROGRESS(slot, v)                                                                      \
+    do {                                                                                          \
+        if (p.trace) *(volatile long long*)&p.trace[5 * kTraceCap + blockIdx.x * 8 + (slot)] = (v);  \
+    } while (0)
+#else
+#define TB_STAMP(role, idx) do { } while (0)
+#define TB_PROGRESS(slot, v) do { } while (0)
+#endif
 
 struct BrickMeta {
     int32_t lo[3];     // first row of each tap group's range
@@ -61,15 +94,54 @@ struct BrickParams {
     int ci, co;
     int out_kind, epi;
     int ntiles, ncb, nkc, nb;
-    int nbst;              // weight stages
+    int nbst, nbst_log2;   // weight stages (2, 4 or 8)
     int brick_cap;         // rows per brick buffer (multiple of kBox)
     uint32_t b_bytes;      // nb * 128
     uint32_t b_alloc;      // b_bytes rounded up to 1024
-    int nd;                // accumulator buffers
+    int nd;                // accumulator buffers per issuer (1 or 2)
+    int niss;              // MMA issuer warps (1 or 2)
     uint32_t a_col0;       // first TMEM column of the A slots
     uint32_t idesc;
     uint32_t tmem_cols;
+    long long* trace;      // TB_TRACE builds only
 };
+
+// Tap order within a stage group starts at tap `rot` (the unit index mod 27), so CTAs that
+// run at the same time fetch different weight slices instead of all hitting the same L2 lines.
+__device__ __forceinline__ int rot_tap(int rot, int j) {
+    const int t = rot + j;
+    return t >= 27 ? t - 27 : t;
+}
+
+// Row of the tap-t neighbor for this thread, from the brick or global memory (zeros if absent).
+__device__ __forceinline__ void load_nbr_row(const BrickParams& p, const BrickMeta& m, const uint8_t* brick,
+                                             int32_t v, int t, int kc, uint32_t* r) {
+    if (v == (int32_t)p.n) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) r[k] = 0u;
+        return;
+    }
+    const int glo = t < 9 ? m.lo[0] : (t < 18 ? m.lo[1] : m.lo[2]);
+    const int glen = t < 9 ? m.len[0] : (t < 18 ? m.len[1] : m.len[2]);
+    const int goff = t < 9 ? m.off[0] : (t < 18 ? m.off[1] : m.off[2]);
+    const int pos = v - glo;
+    if (pos < glen) {
+        const int b = goff + pos;
+        const uint8_t* rowp = brick + (size_t)b * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 x = *reinterpret_cast<const uint4*>(rowp + ((c ^ (b & 7)) << 4));
+            r[4 * c] = x.x; r[4 * c + 1] = x.y; r[4 * c + 2] = x.z; r[4 * c + 3] = x.w;
+        }
+    } else {
+        const uint4* gp = reinterpret_cast<const uint4*>(p.feats + ((size_t)v * p.ci + (size_t)kc * 64) * 2);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 x = __ldg(gp + c);
+            r[4 * c] = x.x; r[4 * c + 1] = x.y; r[4 * c + 2] = x.z; r[4 * c + 3] = x.w;
+        }
+    }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
 k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap fmap,
@@ -88,20 +160,21 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t bar0 = smem_u32(bars);
-    // barrier table
     const uint32_t nbrf = bar0, nbre = bar0 + 16, brkf = bar0 + 32, brke = bar0 + 48;
     const uint32_t af = bar0 + 64, ae = af + 8 * kNA;
     const uint32_t bf = ae + 8 * kNA, be = bf + 8 * kMaxB;
-    const uint32_t df = be + 8 * kMaxB, de = df + 16, drain = de + 16;
+    const uint32_t df = be + 8 * kMaxB, de = df + 32, drain = de + 32;   // df/de: [issuer][buffer]
 
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2; ++b) {
             mbar_init(nbrf + 8 * b, 1);
-            mbar_init(nbre + 8 * b, 4);
+            mbar_init(nbre + 8 * b, 8);
             mbar_init(brkf + 8 * b, 1);
-            mbar_init(brke + 8 * b, 4);
-            mbar_init(df + 8 * b, 1);
-            mbar_init(de + 8 * b, 128);
+            mbar_init(brke + 8 * b, 8);
+        }
+        for (int k = 0; k < 4; ++k) {
+            mbar_init(df + 8 * k, 1);
+            mbar_init(de + 8 * k, 128);
         }
         for (int a = 0; a < kNA; ++a) {
             mbar_init(af + 8 * a, 4);
@@ -111,13 +184,13 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
             mbar_init(bf + 8 * s, 1);
             mbar_init(be + 8 * s, 1);
         }
-        mbar_init(drain, 1);
+        mbar_init(drain, (uint32_t)p.niss);   // one commit from each issuer completes phase 0
         s_misc[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
         asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&fmap)) : "memory");
     }
-    if (warp == 10) {
+    if (warp == kWarpMma0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_u32(s_misc)), "r"(p.tmem_cols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -129,7 +202,7 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     const int nunits = p.ntiles * p.ncb;
     const int32_t sentinel = (int32_t)p.n;
 
-    if (warp == 8) {
+    if (warp == kWarpLoader) {
         // ------------------------------------------------------------------ loader
         int it = 0, bseq = 0;
         bool ok = true;
@@ -139,21 +212,27 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
             if (!mbar_wait(nbre + 8 * buf, ((it >> 1) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
             const int64_t r0 = (int64_t)tile * kTileM;
             int32_t* dst = s_nbr + buf * kNbrInts;
+            // all 108 indices of this lane in flight at once (the map is usually not L2-resident)
+            for (int t = 0; t < 27; ++t) {
+                const int32_t* src = p.nbr + (int64_t)t * p.n + r0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int r = lane + 32 * q;
+                    if (r0 + r < p.n) cp_async_4(smem_u32(dst + t * kTileM + r), src + r);
+                    else dst[t * kTileM + r] = sentinel;
+                }
+            }
+            cp_async_wait_all();
+            __syncwarp();
             int lo[3] = {INT_MAX, INT_MAX, INT_MAX}, hi[3] = {-1, -1, -1};
 #pragma unroll
             for (int g = 0; g < 3; ++g) {
-#pragma unroll 3
                 for (int tt = 0; tt < 9; ++tt) {
                     const int t = 9 * g + tt;
-                    const int32_t* src = p.nbr + (int64_t)t * p.n + r0;
-                    int32_t v[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        v[q] = (r0 + lane + 32 * q) < p.n ? __ldg(src + lane + 32 * q) : sentinel;
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        dst[t * kTileM + lane + 32 * q] = v[q];
-                        if (v[q] != sentinel) { lo[g] = min(lo[g], v[q]); hi[g] = max(hi[g], v[q]); }
+                        const int32_t v = dst[t * kTileM + lane + 32 * q];
+                        if (v != sentinel) { lo[g] = min(lo[g], v); hi[g] = max(hi[g], v); }
                     }
                 }
             }
@@ -162,9 +241,9 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
                 lo[g] = __reduce_min_sync(0xffffffffu, lo[g]);
                 hi[g] = __reduce_max_sync(0xffffffffu, hi[g]);
             }
-            // brick layout: group g at 32-row aligned offset, clipped to the capacity
+            // brick layout: group g at a 32-row aligned offset, clipped to the capacity
             int off = 0, nbox = 0;
-            int glo[3], glen[3], goff[3];
+            int glo[3], glen[3], goff[3], gbox[3];
 #pragma unroll
             for (int g = 0; g < 3; ++g) {
                 const int len = hi[g] >= 0 ? hi[g] - lo[g] + 1 : 0;
@@ -173,9 +252,9 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
                 glo[g] = hi[g] >= 0 ? lo[g] : 0;
                 glen[g] = held;
                 goff[g] = off;
-                const int boxes = (held + kBox - 1) / kBox;
-                off += boxes * kBox;
-                nbox += boxes;
+                gbox[g] = (held + kBox - 1) / kBox;
+                off += gbox[g] * kBox;
+                nbox += gbox[g];
             }
             if (lane == 0) {
                 BrickMeta& m = s_meta[buf];
@@ -191,73 +270,63 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
                 const uint32_t bdst = smem_u32(brick_base + (size_t)slot * brick_bytes);
                 if (lane == 0) mbar_arrive_expect_tx(brkf + 8 * slot, (uint32_t)nbox * kBox * 128);
                 __syncwarp();
-                // box j -> (group, index): lanes issue in parallel (nbox <= brick_cap/32 <= 32)
+                // box j -> (group, index); lanes issue in parallel (nbox <= brick_cap/32 <= 32)
                 for (int j = lane; j < nbox; j += 32) {
                     int g = 0, k = j;
-                    const int b0 = (glen[0] + kBox - 1) / kBox, b1 = (glen[1] + kBox - 1) / kBox;
-                    if (k >= b0) { k -= b0; g = 1; if (k >= b1) { k -= b1; g = 2; } }
-                    tma_load_2d(bdst + (uint32_t)(goff[g] + k * kBox) * 128, &fmap, kc * 64, glo[g] + k * kBox,
-                                brkf + 8 * slot);
+                    if (k >= gbox[0]) { k -= gbox[0]; g = 1; if (k >= gbox[1]) { k -= gbox[1]; g = 2; } }
+                    const int go = g == 0 ? goff[0] : (g == 1 ? goff[1] : goff[2]);
+                    const int gl = g == 0 ? glo[0] : (g == 1 ? glo[1] : glo[2]);
+                    tma_load_2d(bdst + (uint32_t)(go + k * kBox) * 128, &fmap, kc * 64, gl + k * kBox, brkf + 8 * slot);
                 }
+                if (lane == 0) { TB_STAMP(0, bseq); TB_PROGRESS(0, bseq + 1); }
             }
         }
         if (!ok && lane == 0) {
             const long long t0 = clock64();
             while (clock64() - t0 < 4000000ll) __nanosleep(256);
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= kWarpBuild0 && warp < kWarpBuild0 + 8) {
         // ------------------------------------------------------------------ A builders
-        const int q = warp - 4;
+        const int q = warp & 3;                         // TMEM subpartition (warp id % 4)
+        const int half = (warp - kWarpBuild0) >> 2;     // builds stages with seq % 2 == half
         const int i = q * 32 + lane;                    // tile row = TMEM lane
-        int it = 0, bseq = 0, aseq = 0;
+        const uint32_t a_lane = tmem_base + ((uint32_t)(q * 32) << 16) + p.a_col0;
+        int it = 0, bseq = 0, seq0 = 0;                 // seq0: stage sequence of tap 0 of the group
         bool ok = true;
         for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++it) {
             const int buf = it & 1;
             if (!mbar_wait(nbrf + 8 * buf, (it >> 1) & 1, s_abort, p.err)) { ok = false; break; }
             const BrickMeta m = s_meta[buf];
             const int32_t* rows = s_nbr + buf * kNbrInts;
-            for (int kc = 0; kc < p.nkc && ok; ++kc, ++bseq) {
+            const int rot = u % 27;
+            for (int kc = 0; kc < p.nkc && ok; ++kc, ++bseq, seq0 += 27) {
                 const int slot = bseq & 1;
                 if (!mbar_wait(brkf + 8 * slot, (bseq >> 1) & 1, s_abort, p.err)) { ok = false; break; }
                 const uint8_t* brick = brick_base + (size_t)slot * brick_bytes;
-#pragma unroll
-                for (int g = 0; g < 3; ++g) {
-                    const int glo = m.lo[g], glen = m.len[g], goff = m.off[g];
-#pragma unroll 1
-                    for (int tt = 0; tt < 9 && ok; ++tt, ++aseq) {
-                        const int t = 9 * g + tt;
-                        const int a = aseq % kNA;
-                        if (!mbar_wait(ae + 8 * a, ((aseq / kNA) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
-                        const int32_t v = rows[t * kTileM + i];
-                        uint32_t r[32];
-                        if (v == sentinel) {
-#pragma unroll
-                            for (int k = 0; k < 32; ++k) r[k] = 0u;
-                        } else {
-                            const int pos = v - glo;
-                            if (pos < glen) {
-                                const int b = goff + pos;
-                                const uint8_t* rowp = brick + (size_t)b * 128;
-#pragma unroll
-                                for (int c = 0; c < 8; ++c) {
-                                    const uint4 x = *reinterpret_cast<const uint4*>(rowp + ((c ^ (b & 7)) << 4));
-                                    r[4 * c] = x.x; r[4 * c + 1] = x.y; r[4 * c + 2] = x.z; r[4 * c + 3] = x.w;
-                                }
-                            } else {
-                                const uint4* gp = reinterpret_cast<const uint4*>(
-                                    p.feats + ((size_t)v * p.ci + (size_t)kc * 64) * 2);
-#pragma unroll
-                                for (int c = 0; c < 8; ++c) {
-                                    const uint4 x = __ldg(gp + c);
-                                    r[4 * c] = x.x; r[4 * c + 1] = x.y; r[4 * c + 2] = x.z; r[4 * c + 3] = x.w;
-                                }
-                            }
-                        }
-                        tmem_st_x32(tmem_base + ((uint32_t)(q * 32) << 16) + p.a_col0 + 32u * a, r);
-                        tmem_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(af + 8 * a);
+                // this half's stages: position j with (seq0 + j) % 2 == half, two at a time; the
+                // tap of position j is (rot + j) % 27
+                for (int j = (half ^ seq0) & 1; j < 27 && ok; j += 4) {
+                    const int j2 = j + 2;
+                    const bool has2 = j2 < 27;
+                    const int t = rot_tap(rot, j), t2 = rot_tap(rot, j2);
+                    uint32_t r0[32], r1[32];
+                    load_nbr_row(p, m, brick, rows[t * kTileM + i], t, kc, r0);
+                    if (has2) load_nbr_row(p, m, brick, rows[t2 * kTileM + i], t2, kc, r1);
+                    const int s1 = seq0 + j, s2 = seq0 + j2;
+                    const int a1 = s1 & (kNA - 1), a2 = s2 & (kNA - 1);
+                    if (!mbar_wait(ae + 8 * a1, ((s1 >> 3) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
+                    tmem_st_x32(a_lane + 32u * a1, r0);
+                    if (has2) {
+                        if (!mbar_wait(ae + 8 * a2, ((s2 >> 3) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
+                        tmem_st_x32(a_lane + 32u * a2, r1);
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(af + 8 * a1);
+                        if (has2) mbar_arrive(af + 8 * a2);
+                        if (q == 0) { TB_STAMP(1, s1); TB_PROGRESS(1 + half, s1 + 1); }
                     }
                 }
                 __syncwarp();
@@ -266,21 +335,30 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
             __syncwarp();
             if (lane == 0) mbar_arrive(nbre + 8 * buf);
         }
-    } else if (warp == 9) {
-        // ------------------------------------------------------------------ weight producer
-        if (lane == 0) {
-            int seq = 0;
+    } else if (warp >= kWarpWeight0 && warp < kWarpWeight0 + kWeightWarps) {
+        // ------------------------------------------------------------------ weight producers
+        // stage st is always loaded by warp st % nw (nbst is a multiple of nw), so each stage's
+        // loads stay in order; a stage shared by two warps could be refilled a phase early
+        const int wk = warp - kWarpWeight0;
+        const int nw = p.nbst < kWeightWarps ? p.nbst : kWeightWarps;
+        if (lane == 0 && wk < nw) {
+            int seq = wk;
             bool ok = true;
-            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+            const int stages_per_unit = 27 * p.nkc;
+            int it = 0;
+            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++it) {
                 const int cb = u % p.ncb;
-                for (int kc = 0; kc < p.nkc && ok; ++kc) {
-                    for (int t = 0; t < 27; ++t, ++seq) {
-                        const int st = seq % p.nbst;
-                        if (!mbar_wait(be + 8 * st, ((seq / p.nbst) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
-                        mbar_arrive_expect_tx(bf + 8 * st, p.b_bytes);
-                        tma_load_2d(smem_u32(wst_base + (size_t)st * p.b_alloc), &wmap, t * p.ci + kc * 64,
-                                    cb * p.nb, bf + 8 * st);
-                    }
+                const int unit_end = (it + 1) * stages_per_unit;
+                for (; seq < unit_end; seq += nw) {
+                    const int local = seq - it * stages_per_unit;
+                    const int kc = local / 27, t = rot_tap(u % 27, local - kc * 27);
+                    const int st = seq & (p.nbst - 1);
+                    if (!mbar_wait(be + 8 * st, ((seq >> p.nbst_log2) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(bf + 8 * st, p.b_bytes);
+                    tma_load_2d(smem_u32(wst_base + (size_t)st * p.b_alloc), &wmap, t * p.ci + kc * 64, cb * p.nb,
+                                bf + 8 * st);
+                    TB_STAMP(3, seq);
+                    TB_PROGRESS(3, seq + 1);
                 }
             }
             if (!ok) {
@@ -288,80 +366,105 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
                 while (clock64() - t0 < 4000000ll) __nanosleep(256);
             }
         }
-    } else if (warp == 10) {
-        // ------------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            int seq = 0, it = 0;
+    } else if (warp >= kWarpMma0 && warp < kWarpMma0 + 2) {
+        // ------------------------------------------------------------------ MMA issuers
+        const int mi = warp - kWarpMma0;
+        if (lane == 0 && mi < p.niss) {
+            const uint64_t bdesc0 = smem_desc<128>(smem_u32(wst_base));
+            const uint32_t bstep = p.b_alloc >> 4;              // descriptor address units per stage
+            const uint32_t a0 = tmem_base + p.a_col0;
+            const int stages_per_unit = 27 * p.nkc;
+            int seq = mi, it = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++it) {
-                const int d = it % p.nd;
-                if (!mbar_wait(de + 8 * d, ((it / p.nd) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
+                const int d = p.nd == 2 ? (it & 1) : 0;
+                const uint32_t dph = p.nd == 2 ? ((it >> 1) & 1) : (it & 1);
+                const int dk = mi * 2 + d;
+                if (!mbar_wait(de + 8 * dk, dph ^ 1, s_abort, p.err)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t dt = tmem_base + (uint32_t)(d * p.nb);
-                for (int kc = 0; kc < p.nkc && ok; ++kc) {
-                    for (int t = 0; t < 27; ++t, ++seq) {
-                        const int a = seq % kNA;
-                        const int st = seq % p.nbst;
-                        if (!mbar_wait(af + 8 * a, (seq / kNA) & 1, s_abort, p.err)) { ok = false; break; }
-                        if (!mbar_wait(bf + 8 * st, (seq / p.nbst) & 1, s_abort, p.err)) { ok = false; break; }
-                        tc_fence_after();
-                        const uint32_t at = tmem_base + p.a_col0 + 32u * a;
-                        const uint32_t baddr = smem_u32(wst_base + (size_t)st * p.b_alloc);
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            tc_mma_ts(dt, at + 8u * k, smem_desc<128>(baddr + 32 * k), p.idesc,
-                                      (kc | t | k) != 0 ? 1u : 0u);
-                        tc_commit(ae + 8 * a);
-                        tc_commit(be + 8 * st);
-                    }
+                const uint32_t dt = tmem_base + (uint32_t)((mi * p.nd + d) * p.nb);
+                const int unit_end = (it + 1) * stages_per_unit;
+                uint32_t acc = 0;
+                for (; seq < unit_end; seq += p.niss) {
+                    const int a = seq & (kNA - 1);
+                    const int st = seq & (p.nbst - 1);
+                    if (!mbar_wait(af + 8 * a, (seq >> 3) & 1, s_abort, p.err)) { ok = false; break; }
+                    if (!mbar_wait(bf + 8 * st, (seq >> p.nbst_log2) & 1, s_abort, p.err)) { ok = false; break; }
+                    TB_STAMP(2, seq);
+                    TB_PROGRESS(4 + mi, seq + 1);
+                    tc_fence_after();
+                    const uint32_t at = a0 + 32u * (uint32_t)a;
+                    const uint64_t bd = bdesc0 + (uint64_t)(bstep * (uint32_t)st);
+                    tc_mma_ts(dt, at, bd, p.idesc, acc);
+                    tc_mma_ts(dt, at + 8, bd + 2, p.idesc, 1u);
+                    tc_mma_ts(dt, at + 16, bd + 4, p.idesc, 1u);
+                    tc_mma_ts(dt, at + 24, bd + 6, p.idesc, 1u);
+                    acc = 1u;
+                    tc_commit(ae + 8 * a);
+                    tc_commit(be + 8 * st);
                 }
                 if (!ok) break;
-                tc_commit(df + 8 * d);
+                tc_commit(df + 8 * dk);
             }
             tc_commit(drain);
             const long long t0 = clock64();
             while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) __nanosleep(64);
         }
-    } else {
+    } else if (warp < 4) {
         // ------------------------------------------------------------------ epilogue
         const int q = warp;
         int it = 0;
         const size_t esize = p.out_kind == 0 ? 4 : 2;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
             const int tile = u / p.ncb, cb = u % p.ncb;
-            const int d = it % p.nd;
-            if (!mbar_wait(df + 8 * d, (it / p.nd) & 1, s_abort, p.err)) break;
+            const int d = p.nd == 2 ? (it & 1) : 0;
+            const uint32_t dph = p.nd == 2 ? ((it >> 1) & 1) : (it & 1);
+            bool ok = mbar_wait(df + 8 * d, dph, s_abort, p.err);
+            if (ok && p.niss == 2) ok = mbar_wait(df + 8 * (2 + d), dph, s_abort, p.err);
+            if (!ok) break;
+            if (threadIdx.x == 0) { TB_STAMP(4, it); TB_PROGRESS(6, it + 1); }
             tc_fence_after();
             const int64_t row = (int64_t)tile * kTileM + q * 32 + lane;
             const bool valid = row < p.n;
             uint8_t* orow = p.out + ((size_t)row * p.co + (size_t)cb * p.nb) * esize;
+            const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+            const uint32_t d0 = lane_base + (uint32_t)(d * p.nb);
+            const uint32_t d1 = lane_base + (uint32_t)((p.nd + d) * p.nb);
             for (int c0 = 0; c0 < p.nb; c0 += 16) {
-                uint32_t v[16];
-                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(d * p.nb + c0);
-                TMEM_LD_X16(taddr, v);
+                uint32_t v[16], w[16];
+                TMEM_LD_X16(d0 + c0, v);
+                if (p.niss == 2) {
+                    TMEM_LD_X16(d1 + c0, w);
+                }
                 tmem_wait_ld();
                 float f[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int o = cb * p.nb + c0 + j;
-                    const float x = __uint_as_float(v[j]) + (p.bias ? __ldg(p.bias + o) : 0.0f);
+                    float x = __uint_as_float(v[j]) + (p.bias ? __ldg(p.bias + o) : 0.0f);
+                    if (p.niss == 2) x += __uint_as_float(w[j]);
                     f[j] = apply_epi(x, p.epi);
                 }
                 if (valid) store16(orow + (size_t)c0 * esize, f, p.out_kind);
             }
             tc_fence_before();
             mbar_arrive(de + 8 * d);
+            if (p.niss == 2) mbar_arrive(de + 8 * (2 + d));
         }
     }
 
     __syncthreads();
-    if (warp == 10) {
+    if (warp == kWarpMma0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem_base), "r"(p.tmem_cols) : "memory");
     }
 }
 
 }  // namespace
+
+#ifdef TB_TRACE
+extern long long* g_trace_buffer;
+#endif
 
 bool tb_conv_brick_supported(int ci, int co) {
     return ci > 0 && ci % 64 == 0 && co > 0 && co % 16 == 0 && (co <= 256 || co % 256 == 0);
@@ -382,6 +485,10 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const
     }
     const int nb = co <= 256 ? co : 256;
     BrickParams p{};
+    p.trace = nullptr;
+#ifdef TB_TRACE
+    p.trace = g_trace_buffer;
+#endif
     p.nbr = nbr;
     p.feats = reinterpret_cast<const uint8_t*>(feats);
     p.bias = bias;
@@ -398,9 +505,12 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const
     p.nb = nb;
     p.b_bytes = (uint32_t)nb * 128;
     p.b_alloc = (p.b_bytes + 1023u) & ~1023u;
-    p.nbst = nb <= 128 ? kMaxB : 2;
-    p.nd = (2 * nb + 32 * kNA <= 512) ? 2 : 1;
-    p.a_col0 = (uint32_t)(p.nd * nb);
+    // 64 KB of weight stages; each stage is owned by weight warp (seq % 4)
+    p.nbst = nb <= 64 ? kMaxB : (nb <= 128 ? 4 : 2);
+    p.nbst_log2 = p.nbst == 8 ? 3 : (p.nbst == 4 ? 2 : 1);
+    p.niss = nb <= 64 ? 2 : 1;
+    p.nd = (p.niss * 2 * nb + 32 * kNA <= 512) ? 2 : 1;
+    p.a_col0 = (uint32_t)(p.niss * p.nd * nb);
     uint32_t cols = 32;
     while (cols < p.a_col0 + 32u * kNA) cols <<= 1;
     p.tmem_cols = cols;

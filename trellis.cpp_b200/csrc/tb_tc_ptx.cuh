@@ -130,6 +130,14 @@ __device__ __forceinline__ void store16(uint8_t* dst, const float* v, int kind) 
 }
 
 
+// 4-byte asynchronous global -> shared copy (L1-allocating) and its completion wait.
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // A operand in TMEM (M=128: row m in lane m, two 16-bit values per 32-bit column), B from smem.
 __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                           uint32_t accumulate) {
