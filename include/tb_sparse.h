@@ -75,6 +75,27 @@ tb_status tb_ctx_check_device(tb_ctx* ctx);
 tb_status tb_build_neighbor_map(tb_ctx* ctx, const int32_t* coords, int64_t n,
                                 int coord_stride, int32_t* nbr_out);
 
+/* ---- neighbor map without device allocation --------------------------------------------
+ * No counterpart in the reference. For callers that cannot allocate device memory when they
+ * need a map -- a host framework that serves every device buffer from its own pool, or code
+ * that must not call cudaMalloc because it can synchronise the device -- this builds exactly
+ * the map of tb_build_neighbor_map without a context and without allocating or freeing
+ * anything. Its hash table is a static device array inside the library, TB_NOALLOC_SCRATCH
+ * bytes, which every GPU that loads the library holds until the process exits.
+ *   - n may be at most TB_NOALLOC_MAX_VOXELS; a larger n returns TB_ERR_TOO_LARGE and enqueues
+ *     nothing.
+ *   - Runs on the calling thread's current device and enqueues on `stream` (a cudaStream_t,
+ *     NULL = legacy default stream); returns without synchronising.
+ *   - The first call on a device looks up the array's device address (with that device
+ *     current); make that first call before any stream capture.
+ *   - All calls on one device share the single table, and each call clears it before use:
+ *     calls that overlap on the GPU (for example on two streams) race and corrupt each
+ *     other's maps. Serialise them on one stream. */
+#define TB_NOALLOC_MAX_VOXELS 524288
+#define TB_NOALLOC_SCRATCH (2 * TB_NOALLOC_MAX_VOXELS * 16 + 256)
+tb_status tb_build_neighbor_map_noalloc(void* stream, const int32_t* coords, int64_t n,
+                                        int coord_stride, int32_t* nbr_out);
+
 /* Number of (voxel, tap) pairs with a present neighbor in `nbr` (the algorithmic work of
  * one conv). Synchronises the stream. No reference counterpart (instrumentation). */
 tb_status tb_count_valid_pairs(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t* pairs);

@@ -41,6 +41,7 @@ SIGNATURES = {
     "tb_ctx_check_device": (_st, [_vp]),
     "tb_ctx_set_conv_path": (_st, [_vp, _int]),
     "tb_build_neighbor_map": (_st, [_vp, _vp, _i64, _int, _vp]),
+    "tb_build_neighbor_map_noalloc": (_st, [_vp, _vp, _i64, _int, _vp]),
     "tb_count_valid_pairs": (_st, [_vp, _vp, _i64, ctypes.POINTER(_i64)]),
     "tb_submconv": (_st, [_vp, _vp, _i64, _vp, _int, _vp, _vp, _int, _int, _int, _int, _vp]),
     "tb_subdivide": (_st, [_vp, _vp, _i64, _int, _vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64)]),

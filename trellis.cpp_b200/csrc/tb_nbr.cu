@@ -14,6 +14,9 @@
 // nbr[t*N + i] coalesced across the warp for every tap.
 #include "tb_common.cuh"
 
+#include <algorithm>
+#include <mutex>
+
 namespace {
 
 constexpr unsigned long long kEmpty = ~0ull;
@@ -212,4 +215,65 @@ extern "C" tb_status tb_gather_rows(tb_ctx* ctx, const void* src, const int32_t*
         reinterpret_cast<const uint32_t*>(src), rows, m, row_bytes / 4, reinterpret_cast<uint32_t*>(out));
     TB_LAUNCH_CHECK(ctx, "k_gather_rows");
     return TB_OK;
+}
+
+// ---- neighbor map without any device allocation ---------------------------------------------
+// Some callers cannot allocate device memory at the point where they need a neighbor map:
+// for example a host framework that hands out all device memory from its own pool and treats
+// any other allocation as an accounting error, or code that must not call cudaMalloc because
+// that call can synchronise the whole device and stall unrelated work. For them this entry
+// point builds the same map as tb_build_neighbor_map using a hash table that is part of the
+// library image: a static device array that every GPU loading the library holds until the
+// process exits. No context is needed and nothing is allocated or freed.
+namespace {
+
+constexpr int64_t kNoAllocMaxVoxels = TB_NOALLOC_MAX_VOXELS;
+constexpr uint64_t kNoAllocSlots = 2 * (uint64_t)kNoAllocMaxVoxels;      // load factor <= 1/2
+constexpr size_t kNoAllocBytes = kNoAllocSlots * sizeof(Slot) + 256;    // slots + all-ones-key cell + error word
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kMaxDevices = 64;
+void* g_noalloc_addr[kMaxDevices];          // device address of g_noalloc_scratch, per device
+int g_noalloc_sms[kMaxDevices];
+std::once_flag g_noalloc_once[kMaxDevices];
+cudaError_t g_noalloc_setup_err[kMaxDevices];
+
+}  // namespace
+
+extern "C" tb_status tb_build_neighbor_map_noalloc(void* stream, const int32_t* coords, int64_t n,
+                                                   int coord_stride, int32_t* nbr_out) {
+    if (n < 0 || (coord_stride != 3 && coord_stride != 4)) return TB_ERR_INVALID_ARG;
+    if (n > kNoAllocMaxVoxels) return TB_ERR_TOO_LARGE;       // nothing enqueued
+    if (n == 0) return TB_OK;
+    if (!coords || !nbr_out) return TB_ERR_INVALID_ARG;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TB_ERR_CUDA;
+    // one-time set-up per device, with that device current: the host-side name of the array is
+    // only a stand-in, so its device address has to be looked up before a kernel may use it
+    std::call_once(g_noalloc_once[dev], [dev]() {
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        int sms = 0;
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        g_noalloc_setup_err[dev] = e;
+        if (e == cudaSuccess) {
+            g_noalloc_addr[dev] = ptr;
+            g_noalloc_sms[dev] = sms;
+        }
+    });
+    if (g_noalloc_setup_err[dev] != cudaSuccess || !g_noalloc_addr[dev]) return TB_ERR_CUDA;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const uint64_t cap = tb_hash_capacity(n);                   // <= kNoAllocSlots for n <= the maximum
+    Slot* t = reinterpret_cast<Slot*>(g_noalloc_addr[dev]);
+    int* special = reinterpret_cast<int*>(t + cap);
+    int* err = reinterpret_cast<int*>(reinterpret_cast<unsigned char*>(g_noalloc_addr[dev]) + kNoAllocBytes - 4);
+    const int tpb = 256;
+    // every call rebuilds the table from scratch: the previous call's contents are cleared here
+    const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)g_noalloc_sms[dev] * 16);
+    k_hash_clear<<<clear_blocks, tpb, 0, st>>>(t, cap, special);
+    const int64_t blocks = (n + tpb - 1) / tpb;
+    k_hash_insert<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, err);
+    k_nbr_lookup<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, nbr_out, err);
+    return cudaGetLastError() == cudaSuccess ? TB_OK : TB_ERR_CUDA;
 }
