@@ -1,0 +1,165 @@
+"""Multi-GPU z-slab sharding of a voxel set with one-voxel halos over NCCL.
+
+The reference runs on one device and only chunks output rows within it
+(src/sparse.cpp:94-118); this module splits the voxels across ranks (one process per GPU).
+
+* :func:`plan_slabs` cuts the z axis into `world` slabs at voxel-count quantiles (whole z
+  planes, so every voxel belongs to exactly one rank). Rank r owns z in [z_lo, z_hi) and needs
+  the planes z_lo-1 and z_hi of its neighbours as a halo: a 3x3x3 submanifold conv at an owned
+  voxel reads only voxels within one plane.
+* The local row order is [owned rows in global order] + [halo plane z_lo-1] + [halo plane
+  z_hi], so a local neighbor map built over those rows gives every owned row exactly its
+  global neighbors (tests check this against the single-rank oracle).
+* :func:`exchange_halo` sends the boundary planes to the neighbouring ranks with point-to-point
+  send/recv (NCCL over NVLink on GPUs, gloo in the CPU tests) and receives the halo planes
+  straight into their rows. Nothing else is communicated: no all-reduce, no all-gather.
+* :class:`SlabRunner` is the benchmark step on one rank: local neighbor map, halo exchange,
+  conv(SiLU), halo exchange of the intermediate rows, conv.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class SlabPlan:
+    rank: int
+    world: int
+    z_lo: int                  # owned planes: z_lo <= z < z_hi
+    z_hi: int
+    owned: np.ndarray          # global row ids of owned voxels (ascending)
+    halo_lo: np.ndarray        # global row ids of plane z_lo-1 (owned by rank-1)
+    halo_hi: np.ndarray        # global row ids of plane z_hi (owned by rank+1)
+    send_lo: np.ndarray        # local row ids of plane z_lo (sent to rank-1)
+    send_hi: np.ndarray        # local row ids of plane z_hi-1 (sent to rank+1)
+
+    @property
+    def n_owned(self) -> int:
+        return int(self.owned.size)
+
+    @property
+    def n_local(self) -> int:
+        return int(self.owned.size + self.halo_lo.size + self.halo_hi.size)
+
+    def local_rows(self) -> np.ndarray:
+        """Global row id of every local row (owned, then halo_lo, then halo_hi)."""
+        return np.concatenate([self.owned, self.halo_lo, self.halo_hi])
+
+
+def slab_bounds(z: np.ndarray, world: int) -> np.ndarray:
+    """z cut points [world+1] at voxel-count quantiles, on whole planes.
+
+    Every slab gets at least one plane (the voxel sets here span hundreds of planes), so the
+    owner of plane z_lo-1 is always rank-1 and of plane z_hi always rank+1."""
+    z = np.asarray(z, dtype=np.int64)
+    if z.size == 0:
+        return np.arange(world + 1, dtype=np.int64)
+    zmin, zmax = int(z.min()), int(z.max())
+    if zmax - zmin + 1 < world:
+        raise ValueError(f"{zmax - zmin + 1} z planes cannot be split into {world} slabs")
+    csum = np.cumsum(np.bincount(z - zmin, minlength=zmax - zmin + 1))
+    total = int(csum[-1])
+    cuts = np.empty(world + 1, dtype=np.int64)
+    cuts[0] = zmin
+    cuts[world] = zmax + 1
+    for r in range(1, world):
+        k = int(np.searchsorted(csum, total * r / world, side="left"))   # first plane reaching the quantile
+        lo = cuts[r - 1] + 1                                               # at least one plane per slab
+        hi = zmax + 1 - (world - r)                                        # leave a plane for each later slab
+        cuts[r] = min(max(zmin + k + 1, lo), hi)
+    return cuts
+
+
+def plan_slabs(coords: np.ndarray, world: int, rank: int) -> SlabPlan:
+    """Slab of `rank` for coords [N,3] (x,y,z) or [N,4] (b,x,y,z); z is the last column."""
+    z = np.asarray(coords)[:, -1].astype(np.int64)
+    cuts = slab_bounds(z, world)
+    z_lo, z_hi = int(cuts[rank]), int(cuts[rank + 1])
+    owned = np.nonzero((z >= z_lo) & (z < z_hi))[0]
+    halo_lo = np.nonzero(z == z_lo - 1)[0] if rank > 0 else np.zeros(0, np.int64)
+    halo_hi = np.nonzero(z == z_hi)[0] if rank < world - 1 else np.zeros(0, np.int64)
+    zo = z[owned]
+    send_lo = np.nonzero(zo == z_lo)[0] if rank > 0 else np.zeros(0, np.int64)
+    send_hi = np.nonzero(zo == z_hi - 1)[0] if rank < world - 1 else np.zeros(0, np.int64)
+    return SlabPlan(rank, world, z_lo, z_hi, owned, halo_lo, halo_hi, send_lo, send_hi)
+
+
+def exchange_halo(plan: SlabPlan, x: torch.Tensor, gather, send_lo_idx=None, send_hi_idx=None):
+    """Fill the halo rows of the local tensor ``x`` ([n_local, C]) from the neighbouring ranks.
+
+    ``gather(x, idx)`` packs rows ``idx`` of ``x`` into a contiguous tensor (index_select on
+    CPU, the library's tb_gather_rows on GPU). Halo rows are received in place."""
+    n_own, h_lo, h_hi = plan.n_owned, plan.halo_lo.size, plan.halo_hi.size
+    ops = []
+    bufs = []
+    # a plane that is empty on one side is empty on the other (it is the same plane), so both
+    # ranks skip the same transfers
+    if plan.rank > 0 and plan.send_lo.size:
+        sidx = send_lo_idx if send_lo_idx is not None else torch.from_numpy(plan.send_lo).to(x.device)
+        sb = gather(x, sidx)
+        bufs.append(sb)
+        ops.append(dist.P2POp(dist.isend, sb, plan.rank - 1))
+    if plan.rank > 0 and h_lo:
+        ops.append(dist.P2POp(dist.irecv, x[n_own:n_own + h_lo], plan.rank - 1))
+    if plan.rank < plan.world - 1 and plan.send_hi.size:
+        sidx = send_hi_idx if send_hi_idx is not None else torch.from_numpy(plan.send_hi).to(x.device)
+        sb = gather(x, sidx)
+        bufs.append(sb)
+        ops.append(dist.P2POp(dist.isend, sb, plan.rank + 1))
+    if plan.rank < plan.world - 1 and h_hi:
+        ops.append(dist.P2POp(dist.irecv, x[n_own + h_lo:n_own + h_lo + h_hi], plan.rank + 1))
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+    return x
+
+
+class SlabRunner:
+    """The benchmark step on one rank of a NCCL group: map + conv(SiLU) + conv on a z-slab."""
+
+    launches_per_step = 3 + 2 + 2 + 2     # map (3), pack x2 per exchange (2 exchanges), 2 convs
+
+    def __init__(self, coords_np: np.ndarray, ci: int, device, generator):
+        from . import ops
+        self.ops = ops
+        self.rank = dist.get_rank()
+        self.world = dist.get_world_size()
+        self.plan = plan_slabs(coords_np, self.world, self.rank)
+        rows = self.plan.local_rows()
+        self.device = device
+        self.coords = torch.from_numpy(np.ascontiguousarray(coords_np[rows])).to(device)
+        self.n_local = self.plan.n_local
+        self.n_owned = self.plan.n_owned
+        self.ci = ci
+        # features of the owned rows are resident; halo rows arrive by exchange each step
+        self.feats = torch.zeros((self.n_local, ci), dtype=torch.bfloat16, device=device)
+        self.feats[: self.n_owned] = torch.randn((self.n_owned, ci), device=device,
+                                                 generator=generator).bfloat16()
+        self.nbr = torch.empty(27 * self.n_local, dtype=torch.int32, device=device)
+        self.h = torch.zeros((self.n_local, ci), dtype=torch.bfloat16, device=device)
+        self.out = torch.empty((self.n_local, ci), dtype=torch.bfloat16, device=device)
+        self.send_lo = torch.from_numpy(self.plan.send_lo.astype(np.int32)).to(device)
+        self.send_hi = torch.from_numpy(self.plan.send_hi.astype(np.int32)).to(device)
+
+    def _gather(self, x, idx):
+        return self.ops.gather_rows(x, idx)
+
+    def step(self, w1, w2):
+        ops = self.ops
+        ops.build_neighbor_table(self.coords, out=self.nbr)
+        exchange_halo(self.plan, self.feats, self._gather, self.send_lo, self.send_hi)
+        ops.sparse_submconv(self.feats, self.nbr, w1, None, epi="silu", out=self.h)
+        exchange_halo(self.plan, self.h, self._gather, self.send_lo, self.send_hi)
+        ops.sparse_submconv(self.h, self.nbr, w2, None, out=self.out)
+
+    def count_valid_pairs(self) -> int:
+        """Present (voxel, tap) pairs over the owned rows (the algorithmic work of one conv)."""
+        nb = self.nbr.view(27, self.n_local)[:, : self.n_owned]
+        return int((nb != self.n_local).sum().item())
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
