@@ -57,7 +57,7 @@ def _peaks():
 
 def _profile_traffic():
     """DRAM bytes per conv launch from the committed ncu summary, or None."""
-    p = os.path.join(ROOT, "profiles", "submconv_tc_c4.md")
+    p = os.path.join(ROOT, "profiles", "submconv_brick_c4.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
