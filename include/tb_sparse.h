@@ -116,12 +116,15 @@ tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n,
                       const void* feats, int ci, const void* weight, const float* bias,
                       int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
 
-/* Which tensor-core kernel tb_submconv uses for bf16/f16 operands. AUTO picks BRICK when
- * ci is a multiple of 64 (neighbor rows staged per tile in shared memory, A operands built
- * in TMEM) and GATHER otherwise (per-tap row gathers). Forcing a path that does not support
- * the shape makes tb_submconv return TB_ERR_UNSUPPORTED. No reference counterpart (tuning
- * and testing knob). */
-typedef enum tb_conv_path { TB_CONV_AUTO = 0, TB_CONV_GATHER = 1, TB_CONV_BRICK = 2 } tb_conv_path;
+/* Which tensor-core kernel tb_submconv uses for bf16/f16 operands. AUTO picks PAIR when
+ * ci == 64 and co is 32 or 64 (CTA pairs with the weights resident in shared memory), BRICK
+ * when ci is another multiple of 64 (neighbor rows staged per tile in shared memory, A
+ * operands built in TMEM) and GATHER otherwise (per-tap row gathers). Forcing a path that
+ * does not support the shape makes tb_submconv return TB_ERR_UNSUPPORTED. No reference
+ * counterpart (tuning and testing knob). */
+typedef enum tb_conv_path {
+    TB_CONV_AUTO = 0, TB_CONV_GATHER = 1, TB_CONV_BRICK = 2, TB_CONV_PAIR = 3
+} tb_conv_path;
 tb_status tb_ctx_set_conv_path(tb_ctx* ctx, tb_conv_path path);
 
 /* ---- subdivide and channel-to-spatial gather (sparse_c2s, src/sparse.cpp:172-336) -------

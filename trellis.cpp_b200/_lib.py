@@ -16,7 +16,7 @@ STATUS = {0: "TB_OK", 1: "TB_ERR_INVALID_ARG", 2: "TB_ERR_UNSUPPORTED", 3: "TB_E
           4: "TB_ERR_OUT_OF_MEMORY", 5: "TB_ERR_DEVICE", 6: "TB_ERR_TOO_LARGE"}
 TB_F32, TB_F16, TB_BF16 = 0, 1, 2
 TB_EPI_NONE, TB_EPI_SILU = 0, 1
-TB_CONV_AUTO, TB_CONV_GATHER, TB_CONV_BRICK = 0, 1, 2
+TB_CONV_AUTO, TB_CONV_GATHER, TB_CONV_BRICK, TB_CONV_PAIR = 0, 1, 2, 3
 
 # Every symbol include/tb_sparse.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p

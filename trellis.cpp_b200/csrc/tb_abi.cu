@@ -141,6 +141,9 @@ tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* fe
     if (dtype == TB_F32)
         return tb_conv_f32_launch(ctx, nbr, n, reinterpret_cast<const float*>(feats), ci,
                                   reinterpret_cast<const float*>(weight), bias, co, epi, reinterpret_cast<float*>(out));
+    const bool pair = ctx->conv_path == TB_CONV_PAIR ||
+                      (ctx->conv_path == TB_CONV_AUTO && tb_conv_pair_supported(ci, co));
+    if (pair) return tb_conv_pair_launch(ctx, nbr, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
     const bool brick = ctx->conv_path == TB_CONV_BRICK ||
                        (ctx->conv_path == TB_CONV_AUTO && tb_conv_brick_supported(ci, co));
     if (brick) return tb_conv_brick_launch(ctx, nbr, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
@@ -149,7 +152,7 @@ tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* fe
 
 tb_status tb_ctx_set_conv_path(tb_ctx* ctx, tb_conv_path path) {
     if (!ctx) return TB_ERR_INVALID_ARG;
-    if (path != TB_CONV_AUTO && path != TB_CONV_GATHER && path != TB_CONV_BRICK)
+    if (path != TB_CONV_AUTO && path != TB_CONV_GATHER && path != TB_CONV_BRICK && path != TB_CONV_PAIR)
         return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_ctx_set_conv_path: unknown path");
     ctx->conv_path = path;
     return TB_OK;

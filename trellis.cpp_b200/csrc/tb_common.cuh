@@ -78,4 +78,8 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const
                                const void* weight, const float* bias, int co, tb_dtype dtype,
                                tb_dtype out_dtype, tb_epilogue epi, void* out);
 bool tb_conv_brick_supported(int ci, int co);
+tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
+                              const void* weight, const float* bias, int co, tb_dtype dtype,
+                              tb_dtype out_dtype, tb_epilogue epi, void* out);
+bool tb_conv_pair_supported(int ci, int co);
 uint64_t tb_hash_capacity(int64_t n);

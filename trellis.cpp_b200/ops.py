@@ -48,9 +48,10 @@ def context(device=None):
 
 
 def set_conv_path(path: str = "auto", device=None):
-    """Select the tensor-core conv kernel: "auto", "gather" or "brick" (tuning/testing)."""
+    """Select the tensor-core conv kernel: "auto", "gather", "brick" or "pair" (tuning/testing)."""
     ctx = context(device)
-    code = {"auto": _lib.TB_CONV_AUTO, "gather": _lib.TB_CONV_GATHER, "brick": _lib.TB_CONV_BRICK}[path]
+    code = {"auto": _lib.TB_CONV_AUTO, "gather": _lib.TB_CONV_GATHER, "brick": _lib.TB_CONV_BRICK,
+            "pair": _lib.TB_CONV_PAIR}[path]
     check(_lib.load().tb_ctx_set_conv_path(ctx, code), "tb_ctx_set_conv_path", ctx)
 
 
