@@ -32,10 +32,11 @@ namespace {
 using namespace tbtc;
 
 constexpr int kTileM = 128;
+constexpr int kNBuild = 8;           // builder warps: 4 lane quarters x 2 issuers
 constexpr int kWarpBuild0 = 4;       // builders: warps 4-11
-constexpr int kWarpLoader = 12;
-constexpr int kWarpMma0 = 13;        // issuers: warps 13-14 (even CTA)
-constexpr int kThreads = 15 * 32;
+constexpr int kWarpLoader = kWarpBuild0 + kNBuild;
+constexpr int kWarpMma0 = kWarpLoader + 1;   // issuers: two warps (even CTA)
+constexpr int kThreads = (kWarpMma0 + 2) * 32;
 constexpr int kBox = 32;             // rows per TMA box
 constexpr int kNbrRow = kTileM + 4;     // one tap's indices, copied from a 16-byte aligned start
 constexpr int kNbrInts = 27 * kNbrRow;
@@ -123,11 +124,11 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
     if (threadIdx.x == 0) {
         for (int b = 0; b < kNB; ++b) {
             mbar_init(nbrf + 8 * b, 1);
-            mbar_init(nbre + 8 * b, 8);
+            mbar_init(nbre + 8 * b, kNBuild);
         }
         for (int r = 0; r < kNR; ++r) {
             mbar_init(rngf + 8 * r, 1);
-            mbar_init(rnge + 8 * r, 8);
+            mbar_init(rnge + 8 * r, kNBuild);
         }
         for (int a = 0; a < 2 * kNU; ++a) {
             mbar_init(af + 8 * a, 8);        // four builder warps in each CTA (even CTA's copy used)
@@ -304,8 +305,9 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             const long long t0 = clock64();
             while (clock64() - t0 < 4000000ll) __nanosleep(256);
         }
-    } else if (warp >= kWarpBuild0 && warp < kWarpBuild0 + 8) {
+    } else if (warp >= kWarpBuild0 && warp < kWarpBuild0 + kNBuild) {
         // ------------------------------------------------------------------ A builders
+        // warp w writes TMEM lane quarter w % 4 of the units of issuer half
         const int q = warp & 3;
         const int half = (warp - kWarpBuild0) >> 2;
         const int i = q * 32 + lane;
@@ -333,11 +335,13 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                     const bool has2 = t2 < 9 * g + 9;
                     const bool tr0 = leader && half == 0 && q == 0 && lane == 0;
                     if (tr0) TB_STAMP(8, seq0 + t);
+                    // both taps' 32 rows of A in registers before the slot wait: ring row, missing
+                    // (zero) or, for a row outside the held range, global memory
                     uint32_t rv[2][32];
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
-                        const int tt = e == 0 ? t : t2;
                         if (e == 1 && !has2) break;
+                        const int tt = e == 0 ? t : t2;
                         const int32_t v = row_valid ? rows[tt * kNbrRow + ((tt * n4) & 3) + i] : sentinel;
                         if (v == sentinel) {
 #pragma unroll
@@ -378,6 +382,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
 #endif
                     // the unit slot's previous taps have been multiplied
                     if (!mbar_wait_cluster_relaxed(aeh + 8 * u, (uint32_t)(uph ^ 1), s_abort, p.err)) { ok = false; break; }
+                    tc_fence_after();
                     if (tr0) TB_STAMP(9, s1);
                     tmem_st_x32(a_lane + 64u * (uint32_t)u, rv[0]);
                     if (tr0) TB_STAMP(11, s1);

@@ -39,7 +39,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
                  : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     return ok != 0;
 }
-// Bounded wait: false when the CTA aborted or the clock limit ran out (then aborts it).
+// Bounded wait: false when the CTA aborted or the clock limit ran out (then aborts it). The
+// loop re-polls without a sleep: try_wait already suspends the thread in hardware while the phase
+// is open, and a __nanosleep between polls added microseconds to hand-offs that missed the first
+// poll.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
@@ -51,7 +54,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
             atomicCAS(err, 0, TB_DEVERR_WAIT_TIMEOUT);
             return false;
         }
-        __nanosleep(64);
     }
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -234,7 +236,6 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
             atomicCAS(err, 0, TB_DEVERR_WAIT_TIMEOUT);
             return false;
         }
-        __nanosleep(64);
     }
 }
 // Relaxed forms of the cluster-scope wait. Hand-offs that only order tcgen05 operations (TMEM
@@ -261,7 +262,6 @@ __device__ __forceinline__ bool mbar_wait_cluster_relaxed(uint32_t bar, uint32_t
             atomicCAS(err, 0, TB_DEVERR_WAIT_TIMEOUT);
             return false;
         }
-        __nanosleep(64);
     }
 }
 // M=256 MMA over a CTA pair: each CTA supplies 128 rows of A (TMEM) and N/2 rows of B (smem)
