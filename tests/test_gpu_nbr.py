@@ -72,3 +72,44 @@ def test_config_maps_full_size(tb, name):
     from trellis_cpp_b200 import synth
     c = synth.coords_for(name)
     assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+# The map is built in 4x4x4 coordinate blocks when every coordinate is in [0, 2^20 - 2] and every
+# batch index in [0, 15], with buckets for at most N/4 + 64 blocks; otherwise the voxel hash
+# builds it. Both must give the reference's map; these cases sit on either side of each limit.
+@pytest.mark.parametrize("top", [(1 << 20) - 2, (1 << 20) - 1])
+def test_block_layout_coordinate_limit(tb, top):
+    rng = np.random.default_rng(top & 0xFF)
+    c = random_voxels(3000, 16, 31).astype(np.int64)
+    c[:1000] = c[:1000] % 14 + (top - 13)       # a cluster reaching exactly the top of the range
+    c[1000:1500, 0] = top - rng.integers(0, 3, 500)
+    assert c.max() == top or c.max() < top
+    c = np.concatenate([c, [[0, 0, 0], [top, top, top], [top, 0, top], [top - 1, top, top]]]).astype(np.int32)
+    assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+@pytest.mark.parametrize("bmax", [15, 16])
+def test_block_layout_batch_limit(tb, bmax):
+    rng = np.random.default_rng(bmax)
+    c = np.concatenate([rng.integers(0, bmax + 1, (6000, 1)), rng.integers(0, 9, (6000, 3))], 1).astype(np.int32)
+    c[0, 0] = bmax
+    assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+@pytest.mark.parametrize("spacing", [1, 4, 5])
+def test_block_layout_sparse_overflow(tb, spacing):
+    # spacing >= 4 puts every voxel in its own block: more blocks than buckets, so the voxel hash
+    # builds the map (spacing 4 also makes every neighbor absent)
+    g = np.stack(np.meshgrid(*[np.arange(0, 24 * spacing, spacing)] * 3, indexing="ij"), -1).reshape(-1, 3)
+    rng = np.random.default_rng(spacing)
+    c = g[rng.permutation(g.shape[0])].astype(np.int32)
+    assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+def test_block_layout_shuffled_shell_with_duplicates(tb):
+    from trellis_cpp_b200 import synth
+    c = synth.coords_for("c2")
+    rng = np.random.default_rng(4)
+    c = np.concatenate([c, c[rng.integers(0, c.shape[0], 20000)]])
+    c = c[rng.permutation(c.shape[0])]
+    assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))

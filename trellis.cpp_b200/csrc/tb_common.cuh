@@ -66,7 +66,9 @@ inline bool tb_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p)
 
 // Launch helpers implemented in the individual .cu files (all enqueue on ctx->stream).
 tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride,
-                            int32_t* nbr, void* table, uint64_t cap);
+                            int32_t* nbr, void* table, uint64_t cap, const int* gate);
+tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws);
+size_t tb_nbr_workspace_bytes(int64_t n);
 tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
                             const void* weight, const float* bias, int co, tb_dtype dtype,
                             tb_dtype out_dtype, tb_epilogue epi, void* out);

@@ -5,7 +5,19 @@
 // duplicate overwrites) and then does 27 lookups per voxel into a tap-major [27*N] table
 // whose absent entries hold N.
 //
-// GPU design: open addressing with linear probing over 16-byte slots {key, row}. The
+// Block layout (the default): voxels are grouped in 4x4x4 coordinate blocks. A hash table maps
+// each block to a 64-entry bucket of rows indexed by the voxel's position in the block, so a
+// voxel's 27 lookups need at most 8 block probes (mostly its own block) and read buckets that
+// neighbouring voxels read too; in the usual x-major voxel order the table and buckets stay in
+// L1/L2 instead of every probe going to DRAM. It applies when every coordinate is in
+// [0, 2^20 - 2] and every batch index in [0, 15]: there the reference's packed key (20 bits per
+// coordinate, batch in the top 4 bits) is injective, and the keys of the out-of-grid neighbours
+// (a coordinate of -1) cannot equal a voxel's key, so "same key" is "same coordinates" and
+// absent neighbours stay absent. Otherwise, or when there are more than N/4 + 64 blocks (very
+// sparse voxels), a device flag routes the build to the voxel hash below; no host round trip.
+//
+// Voxel hash (fallback, and the allocation-free entry point): open addressing with linear
+// probing over 16-byte slots {key, row}. The
 // capacity is the next power of two >= 2N (load factor <= 1/2), so one 16-byte load per
 // probe. Insert: atomicCAS claims the slot for the key, then atomicMax on the row makes the
 // largest row index win, which is exactly "last writer wins" of the sequential reference.
@@ -33,7 +45,9 @@ __device__ __forceinline__ uint64_t key_of(const int32_t* c, int stride, int dx,
     return tb_key3(c[0] + dx, c[1] + dy, c[2] + dz);
 }
 
-__global__ void k_hash_clear(Slot* __restrict__ t, uint64_t cap, int* __restrict__ special) {
+__global__ void k_hash_clear(Slot* __restrict__ t, uint64_t cap, int* __restrict__ special,
+                             const int* __restrict__ gate) {
+    if (gate && *gate == 0) return;
     uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (; i < cap; i += stride) {
@@ -43,9 +57,12 @@ __global__ void k_hash_clear(Slot* __restrict__ t, uint64_t cap, int* __restrict
     if (blockIdx.x == 0 && threadIdx.x == 0) *special = -1;
 }
 
+// `gate` (may be null): when it points at 0 the block layout built the map and these kernels
+// return at once.
 __global__ void k_hash_insert(const int32_t* __restrict__ coords, int64_t n, int stride,
                               Slot* __restrict__ t, uint64_t mask, int* __restrict__ special,
-                              int* __restrict__ err) {
+                              int* __restrict__ err, const int* __restrict__ gate) {
+    if (gate && *gate == 0) return;
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= n) return;
     const uint64_t k = key_of(coords + i * stride, stride, 0, 0, 0);
@@ -76,7 +93,8 @@ __device__ __forceinline__ int lookup(const Slot* __restrict__ t, uint64_t mask,
 __global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int stride,
                              const Slot* __restrict__ t, uint64_t mask,
                              const int* __restrict__ special_p, int32_t* __restrict__ nbr,
-                             int* __restrict__ err) {
+                             int* __restrict__ err, const int* __restrict__ gate) {
+    if (gate && *gate == 0) return;
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int special = *special_p;
@@ -87,6 +105,124 @@ __global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int 
         const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
         const uint64_t k = key_of(c, stride, kd - 1, kh - 1, kw - 1);
         nbr[(int64_t)tap * n + i] = lookup(t, mask, special, k, (int)n, err);
+    }
+}
+
+// ---- block layout ---------------------------------------------------------------------------
+constexpr int32_t kMaxCoord = (1 << 20) - 2;
+
+struct BlockCtl {
+    unsigned int nblocks;   // buckets handed out
+    int fallback;           // 1: build with the voxel hash instead
+    int pad[2];
+};
+
+__device__ __forceinline__ uint64_t block_key(int32_t b, int32_t bx, int32_t by, int32_t bz) {
+    return tb_key3(bx, by, bz) ^ ((uint64_t)(uint32_t)b << 60);
+}
+
+// Bucket of the block with key k, or -1 when the block holds no voxel.
+__device__ __forceinline__ int block_find(const Slot* __restrict__ t, uint64_t mask, uint64_t k) {
+    uint64_t h = tb_mix64(k) & mask;
+    for (uint64_t probe = 0; probe <= mask; ++probe) {
+        const ulonglong2 s = __ldg(reinterpret_cast<const ulonglong2*>(t) + h);
+        if (s.x == k) return (int)(uint32_t)s.y;
+        if (s.x == kEmpty) return -1;
+        h = (h + 1) & mask;
+    }
+    return -1;
+}
+
+__device__ __forceinline__ void read_coords(const int32_t* c, int stride, int32_t& b, int32_t& x, int32_t& y, int32_t& z) {
+    if (stride == 4) { b = c[0]; x = c[1]; y = c[2]; z = c[3]; }
+    else { b = 0; x = c[0]; y = c[1]; z = c[2]; }
+}
+
+// Claims each voxel's block and hands the block a bucket; flags coordinates outside the range
+// where block lookup equals the reference's key lookup, and bucket overflow.
+__global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int stride, Slot* __restrict__ t,
+                             uint64_t mask, BlockCtl* __restrict__ ctl, unsigned int pool_blocks,
+                             int* __restrict__ err) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int32_t b, x, y, z;
+    read_coords(coords + i * stride, stride, b, x, y, z);
+    if ((uint32_t)x > (uint32_t)kMaxCoord || (uint32_t)y > (uint32_t)kMaxCoord || (uint32_t)z > (uint32_t)kMaxCoord ||
+        (uint32_t)b > 15u) {
+        ctl->fallback = 1;
+        return;
+    }
+    const uint64_t k = block_key(b, x >> 2, y >> 2, z >> 2);
+    uint64_t h = tb_mix64(k) & mask;
+    for (uint64_t probe = 0; probe <= mask; ++probe) {
+        const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
+        if (prev == kEmpty) {
+            const unsigned int id = atomicAdd(&ctl->nblocks, 1u);
+            if (id >= pool_blocks) ctl->fallback = 1;
+            t[h].row = (int)id;
+            return;
+        }
+        if (prev == k) return;
+        h = (h + 1) & mask;
+    }
+    atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
+}
+
+__global__ void k_pool_clear(int32_t* __restrict__ pool, const BlockCtl* __restrict__ ctl) {
+    if (ctl->fallback) return;
+    const uint64_t total = (uint64_t)ctl->nblocks * 16;            // int4 words
+    uint64_t j = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (; j < total; j += stride) reinterpret_cast<int4*>(pool)[j] = make_int4(-1, -1, -1, -1);
+}
+
+// The largest row index of each coordinate wins, as the reference's later insert overwrites.
+__global__ void k_vox_insert(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t,
+                             uint64_t mask, const BlockCtl* __restrict__ ctl, int32_t* __restrict__ pool) {
+    if (ctl->fallback) return;
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int32_t b, x, y, z;
+    read_coords(coords + i * stride, stride, b, x, y, z);
+    const int bucket = block_find(t, mask, block_key(b, x >> 2, y >> 2, z >> 2));
+    if (bucket < 0) return;                                          // cannot happen after k_blk_insert
+    atomicMax(&pool[(int64_t)bucket * 64 + (((x & 3) << 4) | ((y & 3) << 2) | (z & 3))], (int32_t)i);
+}
+
+// 27 lookups per voxel. Per axis the taps reach at most one block besides the voxel's own, so
+// the up to 8 blocks are looked up once and each tap selects among them.
+__global__ void k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t,
+                             uint64_t mask, const BlockCtl* __restrict__ ctl, const int32_t* __restrict__ pool,
+                             int32_t* __restrict__ nbr) {
+    if (ctl->fallback) return;
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int32_t b, x, y, z;
+    read_coords(coords + i * stride, stride, b, x, y, z);
+    const int32_t bx = x >> 2, by = y >> 2, bz = z >> 2;
+    // the other block per axis: -1 at position 0, +1 at position 3, none in between
+    const int ox = (x & 3) == 0 ? -1 : ((x & 3) == 3 ? 1 : 0);
+    const int oy = (y & 3) == 0 ? -1 : ((y & 3) == 3 ? 1 : 0);
+    const int oz = (z & 3) == 0 ? -1 : ((z & 3) == 3 ? 1 : 0);
+    int bk[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const int ax = (m >> 2) & 1, ay = (m >> 1) & 1, az = m & 1;
+        const int32_t cx = bx + (ax ? ox : 0), cy = by + (ay ? oy : 0), cz = bz + (az ? oz : 0);
+        const bool need = (!ax || ox) && (!ay || oy) && (!az || oz);
+        bk[m] = (need && cx >= 0 && cy >= 0 && cz >= 0) ? block_find(t, mask, block_key(b, cx, cy, cz)) : -1;
+    }
+#pragma unroll
+    for (int tap = 0; tap < 27; ++tap) {
+        const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
+        const int32_t nx = x + dx, ny = y + dy, nz = z + dz;
+        const int m = (((nx >> 2) != bx) << 2) | (((ny >> 2) != by) << 1) | ((nz >> 2) != bz);
+        int bucket = bk[0];
+#pragma unroll
+        for (int mm = 1; mm < 8; ++mm) bucket = m == mm ? bk[mm] : bucket;
+        int32_t r = -1;
+        if (bucket >= 0) r = __ldg(&pool[(int64_t)bucket * 64 + (((nx & 3) << 4) | ((ny & 3) << 2) | (nz & 3))]);
+        nbr[(int64_t)tap * n + i] = r >= 0 ? r : (int32_t)n;
     }
 }
 
@@ -136,21 +272,57 @@ uint64_t tb_hash_capacity(int64_t n) {
 }
 
 // `table` holds cap Slots followed by one int (the all-ones key cell); 16*cap + 16 bytes.
+// `gate` (may be null) skips the build when it points at 0.
 tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride,
-                            int32_t* nbr, void* table, uint64_t cap) {
+                            int32_t* nbr, void* table, uint64_t cap, const int* gate) {
     Slot* t = reinterpret_cast<Slot*>(table);
     int* special = reinterpret_cast<int*>(t + cap);
     const uint64_t mask = cap - 1;
     const int tpb = 256;
     const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
-    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap, special);
+    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap, special, gate);
     TB_LAUNCH_CHECK(ctx, "k_hash_clear");
     const int64_t blocks = (n + tpb - 1) / tpb;
-    k_hash_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, ctx->d_err);
+    k_hash_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, ctx->d_err, gate);
     TB_LAUNCH_CHECK(ctx, "k_hash_insert");
-    k_nbr_lookup<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, nbr, ctx->d_err);
+    k_nbr_lookup<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, nbr, ctx->d_err, gate);
     TB_LAUNCH_CHECK(ctx, "k_nbr_lookup");
     return TB_OK;
+}
+
+size_t tb_nbr_workspace_bytes(int64_t n) {
+    const uint64_t cap = tb_hash_capacity(n);
+    const uint64_t pool_blocks = (uint64_t)n / 4 + 64;
+    return cap * sizeof(Slot) + 16 + sizeof(BlockCtl) + pool_blocks * 64 * sizeof(int32_t);
+}
+
+// Block layout first; its kernels and the voxel-hash kernels read BlockCtl::fallback, so
+// exactly one of the two writes the map.
+tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws) {
+    const uint64_t cap = tb_hash_capacity(n);
+    const uint64_t mask = cap - 1;
+    const uint64_t pool_blocks = (uint64_t)n / 4 + 64;
+    Slot* t = reinterpret_cast<Slot*>(ws);
+    unsigned char* after = reinterpret_cast<unsigned char*>(t + cap) + 16;
+    BlockCtl* ctl = reinterpret_cast<BlockCtl*>(after);
+    int32_t* pool = reinterpret_cast<int32_t*>(after + sizeof(BlockCtl));
+    const int tpb = 256;
+    TB_CUDA_TRY(ctx, cudaMemsetAsync(ctl, 0, sizeof(BlockCtl), ctx->stream));
+    const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
+    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap, reinterpret_cast<int*>(t + cap), nullptr);
+    TB_LAUNCH_CHECK(ctx, "k_hash_clear");
+    const int64_t blocks = (n + tpb - 1) / tpb;
+    k_blk_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, (unsigned)pool_blocks,
+                                                             ctx->d_err);
+    TB_LAUNCH_CHECK(ctx, "k_blk_insert");
+    k_pool_clear<<<ctx->num_sms * 8, tpb, 0, ctx->stream>>>(pool, ctl);
+    TB_LAUNCH_CHECK(ctx, "k_pool_clear");
+    k_vox_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool);
+    TB_LAUNCH_CHECK(ctx, "k_vox_insert");
+    k_blk_lookup<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool, nbr);
+    TB_LAUNCH_CHECK(ctx, "k_blk_lookup");
+    // voxel hash, run only when the block layout did not apply
+    return tb_nbr_build_impl(ctx, coords, n, stride, nbr, ws, cap, &ctl->fallback);
 }
 
 extern "C" tb_status tb_build_neighbor_map(tb_ctx* ctx, const int32_t* coords, int64_t n,
@@ -162,10 +334,9 @@ extern "C" tb_status tb_build_neighbor_map(tb_ctx* ctx, const int32_t* coords, i
     if (!coords || !nbr_out) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_build_neighbor_map: null pointer");
     if (n >= (int64_t)INT32_MAX) return tb_fail(ctx, TB_ERR_TOO_LARGE, "tb_build_neighbor_map: n must be < 2^31-1");
     TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
-    const uint64_t cap = tb_hash_capacity(n);
-    tb_status s = tb_ensure(ctx, &ctx->ws, &ctx->ws_bytes, cap * sizeof(Slot) + 16, "hash table");
+    tb_status s = tb_ensure(ctx, &ctx->ws, &ctx->ws_bytes, tb_nbr_workspace_bytes(n), "neighbor-map workspace");
     if (s != TB_OK) return s;
-    return tb_nbr_build_impl(ctx, coords, n, coord_stride, nbr_out, ctx->ws, cap);
+    return tb_nbr_build_blocks(ctx, coords, n, coord_stride, nbr_out, ctx->ws);
 }
 
 extern "C" tb_status tb_count_valid_pairs(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t* pairs) {
@@ -271,9 +442,9 @@ extern "C" tb_status tb_build_neighbor_map_noalloc(void* stream, const int32_t* 
     const int tpb = 256;
     // every call rebuilds the table from scratch: the previous call's contents are cleared here
     const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)g_noalloc_sms[dev] * 16);
-    k_hash_clear<<<clear_blocks, tpb, 0, st>>>(t, cap, special);
+    k_hash_clear<<<clear_blocks, tpb, 0, st>>>(t, cap, special, nullptr);
     const int64_t blocks = (n + tpb - 1) / tpb;
-    k_hash_insert<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, err);
-    k_nbr_lookup<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, nbr_out, err);
+    k_hash_insert<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, err, nullptr);
+    k_nbr_lookup<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, nbr_out, err, nullptr);
     return cudaGetLastError() == cudaSuccess ? TB_OK : TB_ERR_CUDA;
 }
