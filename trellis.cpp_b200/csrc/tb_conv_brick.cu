@@ -437,14 +437,10 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
                     TMEM_LD_X16(d1 + c0, w);
                 }
                 tmem_wait_ld();
-                float f[16];
+                float a[16], f[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int o = cb * p.nb + c0 + j;
-                    float x = __uint_as_float(v[j]) + (p.bias ? __ldg(p.bias + o) : 0.0f);
-                    if (p.niss == 2) x += __uint_as_float(w[j]);
-                    f[j] = apply_epi(x, p.epi);
-                }
+                for (int j = 0; j < 16; ++j) a[j] = __uint_as_float(v[j]) + (p.niss == 2 ? __uint_as_float(w[j]) : 0.0f);
+                epi16(a, p.bias ? p.bias + cb * p.nb + c0 : nullptr, p.epi, f);
                 if (valid) store16(orow + (size_t)c0 * esize, f, p.out_kind);
             }
             tc_fence_before();

@@ -513,11 +513,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 for (int c = 0; c < 4; ++c) {
                     if (16 * c < p.co) {
                         float f[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const float x = accv[16 * c + j] + (p.bias ? __ldg(p.bias + 16 * c + j) : 0.0f);
-                            f[j] = apply_epi(x, p.epi);
-                        }
+                        epi16(accv + 16 * c, p.bias ? p.bias + 16 * c : nullptr, p.epi, f);
                         store16(orow + (size_t)(16 * c) * esize, f, p.out_kind);
                     }
                 }

@@ -103,8 +103,27 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ float apply_epi(float v, int epi) {
-    return epi == TB_EPI_SILU ? v / (1.0f + __expf(-v)) : v;
+// Bias and activation for 16 consecutive channels, each stage over all 16 values so the
+// exponentials and reciprocals of independent channels overlap; one epilogue warp per
+// sub-partition otherwise waits out their latency one channel at a time. SiLU is
+// v * (1 / (1 + e^-v)) with the rounded reciprocal: for large negative v the reciprocal of +inf
+// is 0 and the result is -0, as v / (1 + e^-v) gives.
+__device__ __forceinline__ void epi16(const float* acc, const float* bias, int epi, float* f) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = acc[j];
+    if (bias) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) f[j] += __ldg(bias + j);
+    }
+    if (epi == TB_EPI_SILU) {
+        float e[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) e[j] = __expf(-f[j]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) e[j] = __frcp_rn(1.0f + e[j]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) f[j] *= e[j];
+    }
 }
 
 // Store 16 consecutive output channels of one row.
