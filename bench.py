@@ -57,7 +57,7 @@ def _peaks():
 
 def _profile_traffic():
     """DRAM bytes per conv launch from the committed ncu summary, or None."""
-    p = os.path.join(ROOT, "profiles", "submconv_brick_c4.md")
+    p = os.path.join(ROOT, "profiles", "submconv_pair_c4.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -301,7 +301,7 @@ def run_gpu(args):
         traffic = _profile_traffic()
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                     "frac": achieved / peak_tf, "traffic": traffic,
-                    "peak_source": f"{peak_kind} bf16_tflops (burst)", "kernel": "k_submconv_brick",
+                    "peak_source": f"{peak_kind} bf16_tflops (burst)", "kernel": "k_submconv_pair",
                     "flops_per_launch": flops_launch}
         kernel_stats = {"conv_ms_avg": conv_ms, "conv1_ms": float(np.mean(c1)), "conv2_ms": float(np.mean(c2)),
                         "map_ms_est": ms_step - float(np.mean(c1)) - float(np.mean(c2))}
@@ -340,7 +340,7 @@ def run_gpu(args):
                                   f"{t_map:.2f} s) + both fp32 convs on {sample} rows with {nthreads} threads "
                                   f"({t_conv:.2f} s); per-voxel times summed"}
 
-    launches_per_step = 5   # hash clear, hash insert, neighbor lookup, conv, conv
+    launches_per_step = ops.NBR_MAP_LAUNCHES + 2   # neighbor map, conv, conv
     if world > 1:
         launches_per_step = runner.launches_per_step
     if rank == 0:

@@ -121,11 +121,12 @@ def exchange_halo(plan: SlabPlan, x: torch.Tensor, gather, send_lo_idx=None, sen
 class SlabRunner:
     """The benchmark step on one rank of a NCCL group: map + conv(SiLU) + conv on a z-slab."""
 
-    launches_per_step = 3 + 2 + 2 + 2     # map (3), pack x2 per exchange (2 exchanges), 2 convs
+    launches_per_step = 0                 # set in __init__: map, two packs per exchange (2), 2 convs
 
     def __init__(self, coords_np: np.ndarray, ci: int, device, generator):
         from . import ops
         self.ops = ops
+        self.launches_per_step = ops.NBR_MAP_LAUNCHES + 2 * 2 + 2
         self.rank = dist.get_rank()
         self.world = dist.get_world_size()
         self.plan = plan_slabs(coords_np, self.world, self.rank)

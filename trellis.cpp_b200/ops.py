@@ -27,6 +27,11 @@ _DT = {torch.float32: _lib.TB_F32, torch.float16: _lib.TB_F16, torch.bfloat16: _
 _EPI = {"none": _lib.TB_EPI_NONE, None: _lib.TB_EPI_NONE, "silu": _lib.TB_EPI_SILU}
 _ctxs: dict = {}
 
+# Kernels one tb_build_neighbor_map call launches: the block layout's insert, bucket clear,
+# voxel insert and lookup plus its table clear, and the voxel hash's clear, insert and lookup,
+# which return at once unless the block layout did not apply.
+NBR_MAP_LAUNCHES = 8
+
 
 def _ptr(t) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
