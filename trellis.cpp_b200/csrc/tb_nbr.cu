@@ -13,8 +13,9 @@
 // [0, 2^20 - 2] and every batch index in [0, 15]: there the reference's packed key (20 bits per
 // coordinate, batch in the top 4 bits) is injective, and the keys of the out-of-grid neighbours
 // (a coordinate of -1) cannot equal a voxel's key, so "same key" is "same coordinates" and
-// absent neighbours stay absent. Otherwise, or when there are more than N/4 + 64 blocks (very
-// sparse voxels), a device flag routes the build to the voxel hash below; no host round trip.
+// absent neighbours stay absent. Otherwise, or when there are more than min(N/4 + 64, 2^25 - 64)
+// blocks (very sparse voxels), a device flag routes the build to the voxel hash below; no host
+// round trip.
 //
 // Voxel hash (fallback, and the allocation-free entry point): open addressing with linear
 // probing over 16-byte slots {key, row}. The
@@ -63,17 +64,18 @@ __global__ void k_hash_insert(const int32_t* __restrict__ coords, int64_t n, int
                               Slot* __restrict__ t, uint64_t mask, int* __restrict__ special,
                               int* __restrict__ err, const int* __restrict__ gate) {
     if (gate && *gate == 0) return;
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const uint64_t k = key_of(coords + i * stride, stride, 0, 0, 0);
-    if (k == kEmpty) { atomicMax(special, (int)i); return; }
-    uint64_t h = tb_mix64(k) & mask;
-    for (uint64_t probe = 0; probe <= mask; ++probe) {
-        const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
-        if (prev == kEmpty || prev == k) { atomicMax(&t[h].row, (int)i); return; }
-        h = (h + 1) & mask;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint64_t k = key_of(coords + i * stride, stride, 0, 0, 0);
+        if (k == kEmpty) { atomicMax(special, (int)i); continue; }
+        uint64_t h = tb_mix64(k) & mask;
+        bool done = false;
+        for (uint64_t probe = 0; probe <= mask; ++probe) {
+            const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
+            if (prev == kEmpty || prev == k) { atomicMax(&t[h].row, (int)i); done = true; break; }
+            h = (h + 1) & mask;
+        }
+        if (!done) atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
     }
-    atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
 }
 
 __device__ __forceinline__ int lookup(const Slot* __restrict__ t, uint64_t mask, int special,
@@ -95,16 +97,16 @@ __global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int 
                              const int* __restrict__ special_p, int32_t* __restrict__ nbr,
                              int* __restrict__ err, const int* __restrict__ gate) {
     if (gate && *gate == 0) return;
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= n) return;
     const int special = *special_p;
-    int32_t c[4];
-    for (int d = 0; d < stride; ++d) c[d] = coords[i * stride + d];
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int32_t c[4];
+        for (int d = 0; d < stride; ++d) c[d] = coords[i * stride + d];
 #pragma unroll
-    for (int tap = 0; tap < 27; ++tap) {
-        const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
-        const uint64_t k = key_of(c, stride, kd - 1, kh - 1, kw - 1);
-        nbr[(int64_t)tap * n + i] = lookup(t, mask, special, k, (int)n, err);
+        for (int tap = 0; tap < 27; ++tap) {
+            const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+            const uint64_t k = key_of(c, stride, kd - 1, kh - 1, kw - 1);
+            nbr[(int64_t)tap * n + i] = lookup(t, mask, special, k, (int)n, err);
+        }
     }
 }
 
@@ -121,9 +123,22 @@ __device__ __forceinline__ uint64_t block_key(int32_t b, int32_t bx, int32_t by,
     return tb_key3(bx, by, bz) ^ ((uint64_t)(uint32_t)b << 60);
 }
 
-// Bucket of the block with key k, or -1 when the block holds no voxel.
-__device__ __forceinline__ int block_find(const Slot* __restrict__ t, uint64_t mask, uint64_t k) {
-    uint64_t h = tb_mix64(k) & mask;
+// Slot index of a block: the coordinates, each below 2^18, mixed in 32-bit arithmetic (the
+// comparison is on the full 64-bit key, so the mix only spreads the blocks over the table).
+__device__ __forceinline__ uint64_t block_slot(int32_t b, int32_t bx, int32_t by, int32_t bz, uint64_t mask) {
+    uint32_t h = (uint32_t)bx * 0x9E3779B1u ^ (uint32_t)by * 0x85EBCA77u ^ (uint32_t)bz * 0xC2B2AE3Du ^
+                 (uint32_t)b * 0x27D4EB2Fu;
+    h ^= h >> 15;
+    h *= 0x2C1B3C6Du;
+    h ^= h >> 13;
+    return (uint64_t)h & mask;
+}
+
+// Bucket of the block (b, bx, by, bz), or -1 when the block holds no voxel.
+__device__ __forceinline__ int block_find(const Slot* __restrict__ t, uint64_t mask, int32_t b, int32_t bx,
+                                          int32_t by, int32_t bz) {
+    const uint64_t k = block_key(b, bx, by, bz);
+    uint64_t h = block_slot(b, bx, by, bz, mask);
     for (uint64_t probe = 0; probe <= mask; ++probe) {
         const ulonglong2 s = __ldg(reinterpret_cast<const ulonglong2*>(t) + h);
         if (s.x == k) return (int)(uint32_t)s.y;
@@ -144,16 +159,22 @@ __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int 
                              uint64_t mask, BlockCtl* __restrict__ ctl, unsigned int pool_blocks,
                              int* __restrict__ err) {
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    int32_t b, x, y, z;
-    read_coords(coords + i * stride, stride, b, x, y, z);
-    if ((uint32_t)x > (uint32_t)kMaxCoord || (uint32_t)y > (uint32_t)kMaxCoord || (uint32_t)z > (uint32_t)kMaxCoord ||
-        (uint32_t)b > 15u) {
-        ctl->fallback = 1;
-        return;
+    const int lane = threadIdx.x & 31;
+    int32_t b = 0, x = 0, y = 0, z = 0;
+    bool valid = i < n;
+    if (valid) {
+        read_coords(coords + i * stride, stride, b, x, y, z);
+        if ((uint32_t)x > (uint32_t)kMaxCoord || (uint32_t)y > (uint32_t)kMaxCoord ||
+            (uint32_t)z > (uint32_t)kMaxCoord || (uint32_t)b > 15u) {
+            ctl->fallback = 1;
+            valid = false;
+        }
     }
-    const uint64_t k = block_key(b, x >> 2, y >> 2, z >> 2);
-    uint64_t h = tb_mix64(k) & mask;
+    // consecutive voxels mostly share a block: one lane per distinct block of the warp claims it
+    const uint64_t k = valid ? block_key(b, x >> 2, y >> 2, z >> 2) : (kEmpty - (uint64_t)lane);
+    const unsigned same = __match_any_sync(0xffffffffu, k);
+    if (!valid || (same & ((1u << lane) - 1u)) != 0) return;
+    uint64_t h = block_slot(b, x >> 2, y >> 2, z >> 2, mask);
     for (uint64_t probe = 0; probe <= mask; ++probe) {
         const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
         if (prev == kEmpty) {
@@ -184,13 +205,14 @@ __global__ void k_vox_insert(const int32_t* __restrict__ coords, int64_t n, int 
     if (i >= n) return;
     int32_t b, x, y, z;
     read_coords(coords + i * stride, stride, b, x, y, z);
-    const int bucket = block_find(t, mask, block_key(b, x >> 2, y >> 2, z >> 2));
+    const int bucket = block_find(t, mask, b, x >> 2, y >> 2, z >> 2);
     if (bucket < 0) return;                                          // cannot happen after k_blk_insert
     atomicMax(&pool[(int64_t)bucket * 64 + (((x & 3) << 4) | ((y & 3) << 2) | (z & 3))], (int32_t)i);
 }
 
-// 27 lookups per voxel. Per axis the taps reach at most one block besides the voxel's own, so
-// the up to 8 blocks are looked up once and each tap selects among them.
+// 27 lookups per voxel. Per axis the taps reach at most one block besides the voxel's own (the
+// one below at position 0, above at position 3), so the up to 8 blocks are looked up once and
+// each tap picks one with three predicates fixed per voxel.
 __global__ void k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t,
                              uint64_t mask, const BlockCtl* __restrict__ ctl, const int32_t* __restrict__ pool,
                              int32_t* __restrict__ nbr) {
@@ -200,28 +222,36 @@ __global__ void k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int 
     int32_t b, x, y, z;
     read_coords(coords + i * stride, stride, b, x, y, z);
     const int32_t bx = x >> 2, by = y >> 2, bz = z >> 2;
-    // the other block per axis: -1 at position 0, +1 at position 3, none in between
-    const int ox = (x & 3) == 0 ? -1 : ((x & 3) == 3 ? 1 : 0);
-    const int oy = (y & 3) == 0 ? -1 : ((y & 3) == 3 ? 1 : 0);
-    const int oz = (z & 3) == 0 ? -1 : ((z & 3) == 3 ? 1 : 0);
-    int bk[8];
+    const int lx = x & 3, ly = y & 3, lz = z & 3;
+    const int ox = lx == 0 ? -1 : (lx == 3 ? 1 : 0);
+    const int oy = ly == 0 ? -1 : (ly == 3 ? 1 : 0);
+    const int oz = lz == 0 ? -1 : (lz == 3 ? 1 : 0);
+    // bucket base (bucket * 64) of block own + (ax ? ox : 0, ay ? oy : 0, az ? oz : 0), or -1
+    int base[8];
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
         const int ax = (m >> 2) & 1, ay = (m >> 1) & 1, az = m & 1;
-        const int32_t cx = bx + (ax ? ox : 0), cy = by + (ay ? oy : 0), cz = bz + (az ? oz : 0);
         const bool need = (!ax || ox) && (!ay || oy) && (!az || oz);
-        bk[m] = (need && cx >= 0 && cy >= 0 && cz >= 0) ? block_find(t, mask, block_key(b, cx, cy, cz)) : -1;
+        const int32_t cx = bx + (ax ? ox : 0), cy = by + (ay ? oy : 0), cz = bz + (az ? oz : 0);
+        int bucket = -1;
+        if (need && cx >= 0 && cy >= 0 && cz >= 0) bucket = block_find(t, mask, b, cx, cy, cz);
+        base[m] = bucket >= 0 ? bucket * 64 : -1;
     }
+    // per axis and offset d: does x + d leave the block
+    const bool xm = lx == 0, xp = lx == 3, ym = ly == 0, yp = ly == 3, zm = lz == 0, zp = lz == 3;
 #pragma unroll
     for (int tap = 0; tap < 27; ++tap) {
         const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
-        const int32_t nx = x + dx, ny = y + dy, nz = z + dz;
-        const int m = (((nx >> 2) != bx) << 2) | (((ny >> 2) != by) << 1) | ((nz >> 2) != bz);
-        int bucket = bk[0];
-#pragma unroll
-        for (int mm = 1; mm < 8; ++mm) bucket = m == mm ? bk[mm] : bucket;
+        const bool ax = dx < 0 ? xm : (dx > 0 ? xp : false);
+        const bool ay = dy < 0 ? ym : (dy > 0 ? yp : false);
+        const bool az = dz < 0 ? zm : (dz > 0 ? zp : false);
+        const int b01 = az ? base[1] : base[0], b23 = az ? base[3] : base[2];
+        const int b45 = az ? base[5] : base[4], b67 = az ? base[7] : base[6];
+        const int blo = ay ? b23 : b01, bhi = ay ? b67 : b45;
+        const int bb = ax ? bhi : blo;
+        const int loc = (((lx + dx) & 3) << 4) | (((ly + dy) & 3) << 2) | ((lz + dz) & 3);
         int32_t r = -1;
-        if (bucket >= 0) r = __ldg(&pool[(int64_t)bucket * 64 + (((nx & 3) << 4) | ((ny & 3) << 2) | (nz & 3))]);
+        if (bb >= 0) r = __ldg(pool + bb + loc);
         nbr[(int64_t)tap * n + i] = r >= 0 ? r : (int32_t)n;
     }
 }
@@ -282,7 +312,8 @@ tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int s
     const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
     k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap, special, gate);
     TB_LAUNCH_CHECK(ctx, "k_hash_clear");
-    const int64_t blocks = (n + tpb - 1) / tpb;
+    // grid-stride kernels: a gated launch that returns at once costs a small grid only
+    const int64_t blocks = std::min<int64_t>((n + tpb - 1) / tpb, (int64_t)ctx->num_sms * 16);
     k_hash_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, ctx->d_err, gate);
     TB_LAUNCH_CHECK(ctx, "k_hash_insert");
     k_nbr_lookup<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, nbr, ctx->d_err, gate);
@@ -290,10 +321,15 @@ tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int s
     return TB_OK;
 }
 
+// Buckets for at most N/4 + 64 blocks, and fewer than 2^25 so a bucket's first entry index
+// (bucket * 64) fits an int; more blocks than that send the build to the voxel hash.
+static uint64_t tb_nbr_pool_blocks(int64_t n) {
+    return std::min<uint64_t>((uint64_t)n / 4 + 64, (1ull << 25) - 64);
+}
+
 size_t tb_nbr_workspace_bytes(int64_t n) {
     const uint64_t cap = tb_hash_capacity(n);
-    const uint64_t pool_blocks = (uint64_t)n / 4 + 64;
-    return cap * sizeof(Slot) + 16 + sizeof(BlockCtl) + pool_blocks * 64 * sizeof(int32_t);
+    return cap * sizeof(Slot) + 16 + sizeof(BlockCtl) + tb_nbr_pool_blocks(n) * 64 * sizeof(int32_t);
 }
 
 // Block layout first; its kernels and the voxel-hash kernels read BlockCtl::fallback, so
@@ -301,7 +337,7 @@ size_t tb_nbr_workspace_bytes(int64_t n) {
 tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws) {
     const uint64_t cap = tb_hash_capacity(n);
     const uint64_t mask = cap - 1;
-    const uint64_t pool_blocks = (uint64_t)n / 4 + 64;
+    const uint64_t pool_blocks = tb_nbr_pool_blocks(n);
     Slot* t = reinterpret_cast<Slot*>(ws);
     unsigned char* after = reinterpret_cast<unsigned char*>(t + cap) + 16;
     BlockCtl* ctl = reinterpret_cast<BlockCtl*>(after);
