@@ -13,9 +13,10 @@
 // [0, 2^20 - 2] and every batch index in [0, 15]: there the reference's packed key (20 bits per
 // coordinate, batch in the top 4 bits) is injective, and the keys of the out-of-grid neighbours
 // (a coordinate of -1) cannot equal a voxel's key, so "same key" is "same coordinates" and
-// absent neighbours stay absent. Otherwise, or when there are more than min(N/4 + 64, 2^25 - 64)
-// blocks (very sparse voxels), a device flag routes the build to the voxel hash below; no host
-// round trip.
+// absent neighbours stay absent. The block table has twice as many slots as there are buckets,
+// min(N/4 + 64, 2^25 - 64). Otherwise, or when there are more blocks than buckets (very sparse
+// voxels) or a block insert probes 64 slots without a place, a device flag routes the build to
+// the voxel hash below, which clears and uses its own full-size table; no host round trip.
 //
 // Voxel hash (fallback, and the allocation-free entry point): open addressing with linear
 // probing over 16-byte slots {key, row}. The
@@ -156,8 +157,7 @@ __device__ __forceinline__ void read_coords(const int32_t* c, int stride, int32_
 // Claims each voxel's block and hands the block a bucket; flags coordinates outside the range
 // where block lookup equals the reference's key lookup, and bucket overflow.
 __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int stride, Slot* __restrict__ t,
-                             uint64_t mask, BlockCtl* __restrict__ ctl, unsigned int pool_blocks,
-                             int* __restrict__ err) {
+                             uint64_t mask, BlockCtl* __restrict__ ctl, unsigned int pool_blocks) {
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
     int32_t b = 0, x = 0, y = 0, z = 0;
@@ -174,8 +174,10 @@ __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int 
     const uint64_t k = valid ? block_key(b, x >> 2, y >> 2, z >> 2) : (kEmpty - (uint64_t)lane);
     const unsigned same = __match_any_sync(0xffffffffu, k);
     if (!valid || (same & ((1u << lane) - 1u)) != 0) return;
+    // the table holds twice the buckets; a probe run this long means far more blocks than
+    // buckets (the table filling up), so the voxel hash builds the map
     uint64_t h = block_slot(b, x >> 2, y >> 2, z >> 2, mask);
-    for (uint64_t probe = 0; probe <= mask; ++probe) {
+    for (int probe = 0; probe < 64; ++probe) {
         const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
         if (prev == kEmpty) {
             const unsigned int id = atomicAdd(&ctl->nblocks, 1u);
@@ -186,7 +188,7 @@ __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int 
         if (prev == k) return;
         h = (h + 1) & mask;
     }
-    atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
+    ctl->fallback = 1;
 }
 
 __global__ void k_pool_clear(int32_t* __restrict__ pool, const BlockCtl* __restrict__ ctl) {
@@ -335,21 +337,21 @@ size_t tb_nbr_workspace_bytes(int64_t n) {
 // Block layout first; its kernels and the voxel-hash kernels read BlockCtl::fallback, so
 // exactly one of the two writes the map.
 tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws) {
-    const uint64_t cap = tb_hash_capacity(n);
-    const uint64_t mask = cap - 1;
+    const uint64_t cap = tb_hash_capacity(n);                   // voxel-hash table (fallback)
     const uint64_t pool_blocks = tb_nbr_pool_blocks(n);
+    const uint64_t cap_b = tb_hash_capacity((int64_t)pool_blocks);   // block table, a prefix of it
+    const uint64_t mask = cap_b - 1;
     Slot* t = reinterpret_cast<Slot*>(ws);
     unsigned char* after = reinterpret_cast<unsigned char*>(t + cap) + 16;
     BlockCtl* ctl = reinterpret_cast<BlockCtl*>(after);
     int32_t* pool = reinterpret_cast<int32_t*>(after + sizeof(BlockCtl));
     const int tpb = 256;
     TB_CUDA_TRY(ctx, cudaMemsetAsync(ctl, 0, sizeof(BlockCtl), ctx->stream));
-    const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
-    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap, reinterpret_cast<int*>(t + cap), nullptr);
+    const int clear_blocks = (int)std::min<uint64_t>((cap_b + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
+    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap_b, reinterpret_cast<int*>(t + cap), nullptr);
     TB_LAUNCH_CHECK(ctx, "k_hash_clear");
     const int64_t blocks = (n + tpb - 1) / tpb;
-    k_blk_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, (unsigned)pool_blocks,
-                                                             ctx->d_err);
+    k_blk_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, (unsigned)pool_blocks);
     TB_LAUNCH_CHECK(ctx, "k_blk_insert");
     k_pool_clear<<<ctx->num_sms * 8, tpb, 0, ctx->stream>>>(pool, ctl);
     TB_LAUNCH_CHECK(ctx, "k_pool_clear");
