@@ -62,6 +62,10 @@ __host__ __device__ __forceinline__ uint64_t tb_mix64(uint64_t k) {   // murmur3
 
 inline size_t tb_dtype_size(tb_dtype d) { return d == TB_F32 ? 4 : 2; }
 
+// SiLU v / (1 + e^-v) with the fast exponential and divide (a few ulp); for large negative v the
+// denominator exceeds 2^126 and the result is 0 (the exact value is below 2^-100 in magnitude).
+__device__ __forceinline__ float tb_silu(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+
 inline bool tb_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Launch helpers implemented in the individual .cu files (all enqueue on ctx->stream).

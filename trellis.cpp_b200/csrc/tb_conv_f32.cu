@@ -66,7 +66,7 @@ k_submconv_f32(const int32_t* __restrict__ nbr, int64_t n, const float* __restri
         const int o = o0 + tx + 8 * j;
         if (o >= co) continue;
         float v = acc[j] + (bias ? bias[o] : 0.f);
-        if (epi == TB_EPI_SILU) v = v * __frcp_rn(1.f + __expf(-v));
+        if (epi == TB_EPI_SILU) v = tb_silu(v);
         out[r * co + o] = v;
     }
 }

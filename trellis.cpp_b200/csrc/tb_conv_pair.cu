@@ -329,8 +329,20 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 if (!mbar_wait(rngf + 8 * slot, (k >> 3) & 1, s_abort, p.err)) { ok = false; break; }
                 if (leader && half == 0 && q == 0 && lane == 0) TB_STAMP(5, k);
                 const int rlo = s_rng[slot].lo, rlen = s_rng[slot].len, roff = s_rng[slot].off;
-                // this group's taps with stage parity == half, two at a time
-                for (int t = 9 * g + ((half ^ (seq0 + 9 * g)) & 1); t < 9 * g + 9 && ok; t += 4) {
+                // this group's taps with stage parity == half, two at a time: taps t0, t0 + 2 |
+                // t0 + 4, t0 + 6 | t0 + 8 (those inside the group). The lane's neighbor rows of all
+                // of them are read first, so each unit's row loads wait on one load latency only.
+                const int t0 = 9 * g + ((half ^ (seq0 + 9 * g)) & 1);
+                int32_t vrow[5];
+#pragma unroll
+                for (int e = 0; e < 5; ++e) {
+                    const int tt = t0 + 2 * e;
+                    vrow[e] = (tt < 9 * g + 9 && row_valid) ? rows[tt * kNbrRow + ((tt * n4) & 3) + i] : sentinel;
+                }
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    const int t = t0 + 4 * j;
+                    if (t >= 9 * g + 9 || !ok) break;
                     const int t2 = t + 2;
                     const bool has2 = t2 < 9 * g + 9;
                     const bool tr0 = leader && half == 0 && q == 0 && lane == 0;
@@ -341,8 +353,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         if (e == 1 && !has2) break;
-                        const int tt = e == 0 ? t : t2;
-                        const int32_t v = row_valid ? rows[tt * kNbrRow + ((tt * n4) & 3) + i] : sentinel;
+                        const int32_t v = vrow[2 * j + e];
                         if (v == sentinel) {
 #pragma unroll
                             for (int c = 0; c < 32; ++c) rv[e][c] = 0u;
@@ -512,9 +523,8 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (16 * c < p.co) {
-                        float f[16];
-                        epi16(accv + 16 * c, p.bias ? p.bias + 16 * c : nullptr, p.epi, f);
-                        store16(orow + (size_t)(16 * c) * esize, f, p.out_kind);
+                        epi16(accv + 16 * c, p.bias ? p.bias + 16 * c : nullptr, p.epi, accv + 16 * c);
+                        store16(orow + (size_t)(16 * c) * esize, accv + 16 * c, p.out_kind);
                     }
                 }
             }

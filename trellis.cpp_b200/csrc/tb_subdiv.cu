@@ -168,7 +168,7 @@ __global__ void k_bias_act(T* __restrict__ x, int64_t total, int c, const float*
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (; i < total; i += stride) {
         float v = to_f<T>(x[i]) + (bias ? bias[i % c] : 0.f);
-        if (epi == TB_EPI_SILU) v = v * __frcp_rn(1.f + __expf(-v));
+        if (epi == TB_EPI_SILU) v = tb_silu(v);
         x[i] = from_f<T>(v);
     }
 }
