@@ -36,8 +36,15 @@ def _worker(rank, world, init_file, result_dir):
         tbdist.exchange_halo(plan, x, lambda t, idx: t.index_select(0, idx.long()).contiguous())
         halo_rows = np.concatenate([plan.halo_lo, plan.halo_hi])
         ok_halo = np.array_equal(x[plan.n_owned:].numpy(), feats[halo_rows])
+        # the started-then-finished form the GPU step uses to overlap the map build
+        x2 = torch.zeros_like(x)
+        x2[: plan.n_owned] = 2 * x[: plan.n_owned]
+        handle = tbdist.exchange_halo(plan, x2, lambda t, idx: t.index_select(0, idx.long()).contiguous(),
+                                      wait=False)
         local = coords[plan.local_rows()]
-        nbr_local = oracle.build_neighbor_table(local)
+        nbr_local = oracle.build_neighbor_table(local)          # work done while the transfer runs
+        tbdist.finish_halo(handle)
+        ok_halo = ok_halo and np.array_equal(x2[plan.n_owned:].numpy(), 2 * feats[halo_rows])
         out_local = oracle.submconv(nbr_local, x.numpy(), w)[: plan.n_owned]
         out_global = oracle.submconv(oracle.build_neighbor_table(coords), feats, w)[plan.owned]
         np.savez(os.path.join(result_dir, f"r{rank}.npz"), owned=plan.owned, ok_halo=ok_halo,

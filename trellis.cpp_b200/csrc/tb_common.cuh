@@ -30,6 +30,11 @@ struct tb_ctx {
     std::string last_error;
     void* encode_tiled = nullptr;  // cuTensorMapEncodeTiled, fetched once
     int conv_path = 0;             // tb_conv_path
+    // dynamic shared memory already allowed per conv kernel on this device: the attribute is set
+    // only when a launch needs more, so repeated launches (and launches recorded into a CUDA
+    // graph) make no function-attribute call
+    size_t pair_smem_set = 0;
+    size_t brick_smem_set = 0;
 };
 
 // Record a failure on the context and return the status.

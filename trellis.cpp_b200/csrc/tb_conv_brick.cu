@@ -547,8 +547,12 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const
     }
     const int units = p.ntiles * p.ncb;
     const int grid = std::min(units, ctx->num_sms);
-    cudaError_t e = cudaFuncSetAttribute(k_submconv_brick, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_submconv_brick)");
+    cudaError_t e = cudaSuccess;
+    if (smem > ctx->brick_smem_set) {
+        e = cudaFuncSetAttribute(k_submconv_brick, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_submconv_brick)");
+        ctx->brick_smem_set = smem;
+    }
     k_submconv_brick<<<grid, kThreads, smem, ctx->stream>>>(wmap, fmap, p);
     TB_LAUNCH_CHECK(ctx, "k_submconv_brick");
     return TB_OK;

@@ -51,7 +51,7 @@ constexpr int kNumBars = kNB + kNB + kNR + kNR + 2 * kNU + 2 * kNU + 2 + 2 + 1 +
 // laid out as [role][kTraceCap] (clock64 is per SM, so compare stamps of one CTA only):
 // 0 even loader issued range k, 1 even builder wrote A seq s, 2 MMA seq s inputs ready,
 // 3 odd builder wrote A seq s, 4 even epilogue accumulator ready (it), 5 even builder got
-// range k, 6 odd loader issued range k, 7 issuer accumulator free (2 * it + issuer), 8 even
+// range k, 6 even builder's gathered rows arrived (seq s), 7 issuer accumulator free (2 * it + issuer), 8 even
 // builder starts seq s, 9 even builder's A slot free for seq s, 11 first tcgen05.st issued,
 // 12 tcgen05.wait::st done, 13 before the arrive, 10 even loader starts tile it's neighbor
 // indices ([it]) and their arrival ([2048 + it]), 14 even loader: ranges computed [it], waits for
@@ -391,6 +391,12 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                         if (lane == 0) { TB_COUNT(0, nring); TB_COUNT(1, nglob); TB_COUNT(2, nmiss); }
                     }
 #endif
+#ifdef TB_TRACE
+                    if (tr0) {
+                        asm volatile("" :: "r"(rv[0][31]), "r"(rv[1][31]));   // the gathered rows have arrived
+                        TB_STAMP(6, s1);
+                    }
+#endif
                     // the unit slot's previous taps have been multiplied
                     if (!mbar_wait_cluster_relaxed(aeh + 8 * u, (uint32_t)(uph ^ 1), s_abort, p.err)) { ok = false; break; }
                     tc_fence_after();
@@ -614,8 +620,12 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const 
         if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the feature view");
     }
     const int nclusters = std::max(1, std::min(p.npairs, ctx->num_sms / 2));
-    cudaError_t e = cudaFuncSetAttribute(k_submconv_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_submconv_pair)");
+    cudaError_t e = cudaSuccess;
+    if (smem > ctx->pair_smem_set) {
+        e = cudaFuncSetAttribute(k_submconv_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_submconv_pair)");
+        ctx->pair_smem_set = smem;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * nclusters);
     cfg.blockDim = dim3(kThreads);

@@ -13,8 +13,8 @@ The reference runs on one device and only chunks output rows within it
 * :func:`exchange_halo` sends the boundary planes to the neighbouring ranks with point-to-point
   send/recv (NCCL over NVLink on GPUs, gloo in the CPU tests) and receives the halo planes
   straight into their rows. Nothing else is communicated: no all-reduce, no all-gather.
-* :class:`SlabRunner` is the benchmark step on one rank: local neighbor map, halo exchange,
-  conv(SiLU), halo exchange of the intermediate rows, conv.
+* :class:`SlabRunner` is the benchmark step on one rank: halo exchange of the input rows
+  overlapped with the local neighbor map, conv(SiLU), halo exchange of the intermediate rows, conv.
 """
 from __future__ import annotations
 
@@ -88,11 +88,14 @@ def plan_slabs(coords: np.ndarray, world: int, rank: int) -> SlabPlan:
     return SlabPlan(rank, world, z_lo, z_hi, owned, halo_lo, halo_hi, send_lo, send_hi)
 
 
-def exchange_halo(plan: SlabPlan, x: torch.Tensor, gather, send_lo_idx=None, send_hi_idx=None):
+def exchange_halo(plan: SlabPlan, x: torch.Tensor, gather, send_lo_idx=None, send_hi_idx=None,
+                  wait: bool = True):
     """Fill the halo rows of the local tensor ``x`` ([n_local, C]) from the neighbouring ranks.
 
     ``gather(x, idx)`` packs rows ``idx`` of ``x`` into a contiguous tensor (index_select on
-    CPU, the library's tb_gather_rows on GPU). Halo rows are received in place."""
+    CPU, the library's tb_gather_rows on GPU). Halo rows are received in place. With
+    ``wait=False`` the transfers are only started and a handle is returned; pass it to
+    :func:`finish_halo` before reading the halo rows (work enqueued in between overlaps them)."""
     n_own, h_lo, h_hi = plan.n_owned, plan.halo_lo.size, plan.halo_hi.size
     ops = []
     bufs = []
@@ -112,10 +115,18 @@ def exchange_halo(plan: SlabPlan, x: torch.Tensor, gather, send_lo_idx=None, sen
         ops.append(dist.P2POp(dist.isend, sb, plan.rank + 1))
     if plan.rank < plan.world - 1 and h_hi:
         ops.append(dist.P2POp(dist.irecv, x[n_own + h_lo:n_own + h_lo + h_hi], plan.rank + 1))
-    if ops:
-        for w in dist.batch_isend_irecv(ops):
-            w.wait()
+    works = dist.batch_isend_irecv(ops) if ops else []
+    if not wait:
+        return (works, bufs)
+    finish_halo((works, bufs))
     return x
+
+
+def finish_halo(handle) -> None:
+    """Wait for the transfers of an ``exchange_halo(..., wait=False)`` call."""
+    works, _bufs = handle          # the send buffers stay alive until the sends complete
+    for w in works:
+        w.wait()
 
 
 class SlabRunner:
@@ -145,17 +156,46 @@ class SlabRunner:
         self.out = torch.empty((self.n_local, ci), dtype=torch.bfloat16, device=device)
         self.send_lo = torch.from_numpy(self.plan.send_lo.astype(np.int32)).to(device)
         self.send_hi = torch.from_numpy(self.plan.send_hi.astype(np.int32)).to(device)
+        self.graph = None
 
     def _gather(self, x, idx):
         return self.ops.gather_rows(x, idx)
 
     def step(self, w1, w2):
         ops = self.ops
+        # the feature halo does not depend on the map: its transfer overlaps the map build
+        pending = exchange_halo(self.plan, self.feats, self._gather, self.send_lo, self.send_hi, wait=False)
         ops.build_neighbor_table(self.coords, out=self.nbr)
-        exchange_halo(self.plan, self.feats, self._gather, self.send_lo, self.send_hi)
+        finish_halo(pending)
         ops.sparse_submconv(self.feats, self.nbr, w1, None, epi="silu", out=self.h)
         exchange_halo(self.plan, self.h, self._gather, self.send_lo, self.send_hi)
         ops.sparse_submconv(self.h, self.nbr, w2, None, out=self.out)
+
+    def capture(self, w1, w2, warmup: int = 3) -> None:
+        """Record one step, both halo exchanges included, into a CUDA graph.
+
+        With fewer voxels per rank the device work of a step shrinks to a few hundred
+        microseconds while issuing it from Python (about fourteen launches and two NCCL
+        exchanges per rank, with every rank's process on the same host) takes longer; replaying
+        the graph issues the whole step at once. The warm-up steps run on a side stream first so
+        that every buffer and NCCL connection exists before recording; the graph keeps the
+        buffers it records, so later replays reuse the same tensors."""
+        cur = torch.cuda.current_stream(self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(w1, w2)
+        cur.wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.step(w1, w2)
+        torch.cuda.synchronize(self.device)
+
+    def replay(self) -> None:
+        """One step from the recorded graph (see :meth:`capture`)."""
+        self.graph.replay()
 
     def count_valid_pairs(self) -> int:
         """Present (voxel, tap) pairs over the owned rows (the algorithmic work of one conv)."""
@@ -163,4 +203,7 @@ class SlabRunner:
         return int((nb != self.n_local).sum().item())
 
     def close(self):
+        """Finish the device work and release the recorded graph; a graph that holds NCCL
+        calls must be gone before the process group is destroyed."""
         torch.cuda.synchronize(self.device)
+        self.graph = None
