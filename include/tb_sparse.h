@@ -116,6 +116,33 @@ tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n,
                       const void* feats, int ci, const void* weight, const float* bias,
                       int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
 
+/* ---- ConvNeXt block --------------------------------------------------------------------
+ * Replaces the per-voxel tail of sparse_convnext (include/sparse.h:23-25,
+ * src/sparse.cpp:124-133) after its conv:
+ *   out[i] = x[i] + W2 . silu( W1 . LN(h[i]) + b1 ) + b2
+ * LN = LayerNorm over the c channels, eps 1e-6, scaled by norm_w and shifted by norm_b
+ * (ggml_norm + affine); W1 = mlp.0.weight [4c][c], b1 [4c]; W2 = mlp.2.weight [c][4c], b2 [c].
+ * h is the block's conv output [n][c] in TB_F32 or the operand dtype; x is the block input
+ * [n][c] in the operand dtype; norm_w, norm_b, b1, b2 are float32.
+ *   dtype TB_BF16 / TB_F16: x, W1, W2 in that type, tcgen05 tensor cores with fp32
+ *        accumulation; the normalised row and the SiLU activations are rounded to the operand
+ *        type before their products (ggml rounds activations to the weight type likewise).
+ *        Needs c in {64, 128, 256}.
+ *   dtype TB_F32: fp32 throughout on CUDA cores (h and out fp32), any c <= 1024; one block per
+ *        row, meant for the precision mode and small n.
+ *   out_dtype: TB_F32 or the operand dtype. `out` must not alias h or x. */
+tb_status tb_convnext_tail(tb_ctx* ctx, int64_t n, int c, const void* h, tb_dtype h_dtype, const void* x,
+                           const float* norm_w, const float* norm_b, const void* w1, const float* b1,
+                           const void* w2, const float* b2, tb_dtype dtype, tb_dtype out_dtype, void* out);
+
+/* The whole block, replacing sparse_convnext (include/sparse.h:23-25, src/sparse.cpp:101-137):
+ * h = tb_submconv(feats; conv_w, conv_b) into context workspace (fp32), then
+ * tb_convnext_tail(h, x = feats). Same dtype rules as the two calls; `out` must not alias feats. */
+tb_status tb_sparse_convnext(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int c,
+                             const void* conv_w, const float* conv_b, const float* norm_w, const float* norm_b,
+                             const void* w1, const float* b1, const void* w2, const float* b2, tb_dtype dtype,
+                             tb_dtype out_dtype, void* out);
+
 /* Which tensor-core kernel tb_submconv uses for bf16/f16 operands. AUTO picks PAIR when
  * ci == 64 and co is 32 or 64 (CTA pairs with the weights resident in shared memory), BRICK
  * when ci is another multiple of 64 (neighbor rows staged per tile in shared memory, A

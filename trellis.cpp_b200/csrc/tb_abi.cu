@@ -91,6 +91,7 @@ tb_status tb_ctx_destroy(tb_ctx* ctx) {
     cudaStreamSynchronize(ctx->stream);
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->host_stage) cudaFree(ctx->host_stage);
+    if (ctx->block_h) cudaFree(ctx->block_h);
     if (ctx->d_err) cudaFree(ctx->d_err);
     delete ctx;
     return TB_OK;
@@ -148,6 +149,43 @@ tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* fe
                        (ctx->conv_path == TB_CONV_AUTO && tb_conv_brick_supported(ci, co));
     if (brick) return tb_conv_brick_launch(ctx, nbr, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
     return tb_conv_tc_launch(ctx, nbr, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
+}
+
+tb_status tb_convnext_tail(tb_ctx* ctx, int64_t n, int c, const void* h, tb_dtype h_dtype, const void* x,
+                           const float* norm_w, const float* norm_b, const void* w1, const float* b1,
+                           const void* w2, const float* b2, tb_dtype dtype, tb_dtype out_dtype, void* out) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (n < 0 || c <= 0) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_convnext_tail: n < 0 or c <= 0");
+    if ((dtype != TB_F32 && dtype != TB_F16 && dtype != TB_BF16) || (h_dtype != TB_F32 && h_dtype != dtype))
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_convnext_tail: bad dtype (h must be TB_F32 or the operand dtype)");
+    if (out_dtype != TB_F32 && out_dtype != dtype)
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "tb_convnext_tail: out_dtype must be TB_F32 or the operand dtype");
+    if (n == 0) return TB_OK;
+    if (!h || !x || !norm_w || !norm_b || !w1 || !b1 || !w2 || !b2 || !out)
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_convnext_tail: null pointer");
+    if (n >= (int64_t)INT32_MAX) return tb_fail(ctx, TB_ERR_TOO_LARGE, "tb_convnext_tail: n must be < 2^31-1");
+    if (!tb_aligned16(h) || !tb_aligned16(x) || !tb_aligned16(w1) || !tb_aligned16(w2) || !tb_aligned16(out))
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_convnext_tail: h/x/w1/w2/out must be 16-byte aligned");
+    if (out == h || out == x) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_convnext_tail: out must not alias h or x");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    return tb_convnext_tail_launch(ctx, n, c, h, h_dtype, x, norm_w, norm_b, w1, b1, w2, b2, dtype, out_dtype, out);
+}
+
+tb_status tb_sparse_convnext(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int c,
+                             const void* conv_w, const float* conv_b, const float* norm_w, const float* norm_b,
+                             const void* w1, const float* b1, const void* w2, const float* b2, tb_dtype dtype,
+                             tb_dtype out_dtype, void* out) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (n < 0 || c <= 0) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_sparse_convnext: n < 0 or c <= 0");
+    if (n == 0) return TB_OK;
+    if (dtype != TB_F32 && !tb_convnext_tc_supported(c))
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "tb_sparse_convnext: 16-bit operands need c in {64, 128, 256}");
+    tb_status s = tb_ensure(ctx, &ctx->block_h, &ctx->block_h_bytes, (size_t)n * c * sizeof(float), "convnext conv output");
+    if (s != TB_OK) return s;
+    s = tb_submconv(ctx, nbr, n, feats, c, conv_w, conv_b, c, dtype, TB_F32, TB_EPI_NONE, ctx->block_h);
+    if (s != TB_OK) return s;
+    return tb_convnext_tail(ctx, n, c, ctx->block_h, TB_F32, feats, norm_w, norm_b, w1, b1, w2, b2, dtype, out_dtype,
+                            out);
 }
 
 tb_status tb_ctx_set_conv_path(tb_ctx* ctx, tb_conv_path path) {

@@ -35,6 +35,8 @@ struct tb_ctx {
     // graph) make no function-attribute call
     size_t pair_smem_set = 0;
     size_t brick_smem_set = 0;
+    void* block_h = nullptr;       // fp32 conv output of tb_sparse_convnext
+    size_t block_h_bytes = 0;
 };
 
 // Record a failure on the context and return the status.
@@ -93,4 +95,8 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const 
                               const void* weight, const float* bias, int co, tb_dtype dtype,
                               tb_dtype out_dtype, tb_epilogue epi, void* out);
 bool tb_conv_pair_supported(int ci, int co);
+tb_status tb_convnext_tail_launch(tb_ctx* ctx, int64_t n, int c, const void* h, tb_dtype h_dtype, const void* x,
+                                  const float* nw, const float* nb, const void* w1, const float* b1, const void* w2,
+                                  const float* b2, tb_dtype dtype, tb_dtype out_dtype, void* out);
+bool tb_convnext_tc_supported(int c);
 uint64_t tb_hash_capacity(int64_t n);

@@ -119,6 +119,62 @@ def sparse_submconv(feats: torch.Tensor, nbr: torch.Tensor, weight: torch.Tensor
     return out
 
 
+def _f32_vec(t, n, name):
+    if t is None or not t.is_cuda or t.dtype != torch.float32 or t.numel() != n or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous float32 CUDA tensor of {n} values")
+
+
+def convnext_tail(h: torch.Tensor, x: torch.Tensor, norm_w, norm_b, w1, b1, w2, b2, out_dtype=None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """The per-voxel tail of ``sparse_convnext`` (src/sparse.cpp:124-133):
+    ``x + W2 . silu(W1 . LN(h) + b1) + b2`` with LN over channels (eps 1e-6, affine).
+
+    h [N,C] float32 or x's dtype; x [N,C]; w1 [4C,C] and w2 [C,4C] in x's dtype; norm_w, norm_b,
+    b1, b2 float32."""
+    _need_cuda(h, x, w1, w2)
+    if x.dtype not in _DT or w1.dtype != x.dtype or w2.dtype != x.dtype:
+        raise ValueError("x, w1 and w2 must share a dtype among float32/float16/bfloat16")
+    if h.dtype not in (torch.float32, x.dtype) or h.shape != x.shape:
+        raise ValueError("h must be [N,C] float32 or x's dtype")
+    n, c = x.shape
+    if w1.numel() != 4 * c * c or w2.numel() != 4 * c * c:
+        raise ValueError("w1 must be [4C,C] and w2 [C,4C]")
+    for t, m, name in ((norm_w, c, "norm_w"), (norm_b, c, "norm_b"), (b1, 4 * c, "b1"), (b2, c, "b2")):
+        _f32_vec(t, m, name)
+    od = x.dtype if out_dtype is None else out_dtype
+    if out is None:
+        out = torch.empty((n, c), dtype=od, device=x.device)
+    ctx = context(x.device)
+    check(_lib.load().tb_convnext_tail(ctx, n, c, _ptr(h), _DT[h.dtype], _ptr(x), _ptr(norm_w), _ptr(norm_b),
+                                       _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _DT[x.dtype], _DT[od], _ptr(out)),
+          "tb_convnext_tail", ctx)
+    return out
+
+
+def sparse_convnext(feats: torch.Tensor, nbr: torch.Tensor, conv_w, conv_b, norm_w, norm_b, w1, b1, w2, b2,
+                    out_dtype=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``trellis::sparse_convnext`` (include/sparse.h:23-25): conv (weight [C,27,C], bias [C]),
+    then :func:`convnext_tail` with the block input ``feats`` as the residual."""
+    _need_cuda(feats, nbr, conv_w, w1, w2)
+    n, c = feats.shape
+    if conv_w.dtype != feats.dtype or w1.dtype != feats.dtype or w2.dtype != feats.dtype:
+        raise ValueError("weights must share feats' dtype")
+    if conv_w.numel() != c * 27 * c or nbr.numel() != 27 * n:
+        raise ValueError("conv weight must be [C,27,C] and nbr 27*N")
+    if conv_b is not None:
+        _f32_vec(conv_b, c, "conv_b")
+    for t, m, name in ((norm_w, c, "norm_w"), (norm_b, c, "norm_b"), (b1, 4 * c, "b1"), (b2, c, "b2")):
+        _f32_vec(t, m, name)
+    od = feats.dtype if out_dtype is None else out_dtype
+    if out is None:
+        out = torch.empty((n, c), dtype=od, device=feats.device)
+    ctx = context(feats.device)
+    check(_lib.load().tb_sparse_convnext(ctx, _ptr(nbr), n, _ptr(feats), c, _ptr(conv_w), _ptr(conv_b),
+                                         _ptr(norm_w), _ptr(norm_b), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2),
+                                         _DT[feats.dtype], _DT[od], _ptr(out)), "tb_sparse_convnext", ctx)
+    return out
+
+
 def subdivide(coords: torch.Tensor, mask: torch.Tensor, max_children: int | None = None):
     """(child coords [M,s], gidx [M], mstart [N+1]) for uint8/bool mask [N,8]."""
     _need_cuda(coords, mask)
