@@ -15,6 +15,10 @@ fixed as N grows ("scaling": "strong").
 
 `--impl reference` times the reference algorithm's CPU implementation (the oracle port in
 oracle/, all host threads) on a bounded sample of the same workload.
+
+`--op convnext` measures one sparse ConvNeXt block instead (src/sparse.cpp:94-137 on the same
+shell): the conv into an fp32 h, then the fused LayerNorm + Linear C->4C + SiLU + Linear 4C->C +
+residual tail; metric voxels/s of the block, roofline of the tail kernel (HBM-bound).
 """
 from __future__ import annotations
 
@@ -55,9 +59,9 @@ def _peaks():
     return 1590.0, 6650.0, "fallback"
 
 
-def _profile_traffic():
-    """DRAM bytes per conv launch from the committed ncu summary, or None."""
-    p = os.path.join(ROOT, "profiles", "submconv_pair_c4.md")
+def _profile_traffic(name="submconv_pair_c4.md"):
+    """DRAM bytes per launch at full size from a committed ncu summary, or None."""
+    p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -372,6 +376,127 @@ def run_gpu(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- ConvNeXt block
+CNX_METRIC = ("voxels/s through one sparse ConvNeXt block (3^3 conv + LayerNorm + Linear C->4C + SiLU + "
+              "Linear 4C->C + residual), ~4.9M voxels C=64 (config 4 shell)")
+
+
+def cpu_convnext_step(nbr_full, feats, cw, cb, nw, nb, w1, b1, w2, b2, sample, nthreads):
+    """The block on `sample` output rows with the oracle port (C conv, numpy tail); s/voxel."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    n = feats.shape[0]
+    row0 = (n - sample) // 2
+    t0 = time.perf_counter()
+    h = oracle.submconv_f32_mt_range(nbr_full, feats, oracle.weight_tap_major(cw), row0, sample, bias=cb,
+                                     nthreads=nthreads)
+    h = h[row0:row0 + sample] if h.shape[0] == n else h
+    y = oracle.layer_norm(h, nw, nb)
+    a = oracle.silu(y @ w1.T + b1)
+    out = a @ w2.T + b2 + feats[row0:row0 + sample]
+    dt = time.perf_counter() - t0
+    assert out.shape == (sample, feats.shape[1])
+    return dt / sample, dt
+
+
+def run_convnext(args):
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _load_package()
+    from trellis_cpp_b200 import ops, synth
+
+    c = CI
+    coords_np = synth.coords_for(args.workload)
+    n = coords_np.shape[0]
+    g = torch.Generator(device=dev).manual_seed(4321)
+    bf = torch.bfloat16
+    feats = torch.randn((n, c), device=dev, generator=g).to(bf)
+    cw = (torch.randn((c, 27, c), device=dev, generator=g) / np.sqrt(27 * c)).to(bf)
+    cb = 0.1 * torch.randn(c, device=dev, generator=g)
+    nw = 1 + 0.1 * torch.randn(c, device=dev, generator=g)
+    nb = 0.1 * torch.randn(c, device=dev, generator=g)
+    w1 = (torch.randn((4 * c, c), device=dev, generator=g) / np.sqrt(c)).to(bf)
+    b1 = 0.1 * torch.randn(4 * c, device=dev, generator=g)
+    w2 = (torch.randn((c, 4 * c), device=dev, generator=g) / np.sqrt(4 * c)).to(bf)
+    b2 = 0.1 * torch.randn(c, device=dev, generator=g)
+    nbr = ops.build_neighbor_table(torch.from_numpy(coords_np).to(dev))
+    h = torch.empty((n, c), dtype=torch.float32, device=dev)
+    out = torch.empty((n, c), dtype=bf, device=dev)
+    events = []
+
+    def step(record=False):
+        # the two launches of tb_sparse_convnext: conv (fp32 h), then the tail
+        if record:
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record()
+        ops.sparse_submconv(feats, nbr, cw, cb, out=h)
+        if record:
+            e[1].record()
+        ops.convnext_tail(h, feats, nw, nb, w1, b1, w2, b2, out=out)
+        if record:
+            e[2].record()
+            events.append(e)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    pairs = ops.count_valid_pairs(nbr, n)
+    ops.check_device()
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    sampler.start()
+    time.sleep(0.8)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step(record=True)
+    t1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    ops.check_device()
+    ms_step = t0.elapsed_time(t1) / args.steps
+    conv_ms = float(np.mean([a.elapsed_time(b) for a, b, _ in events]))
+    tail_ms = float(np.mean([b.elapsed_time(e) for _, b, e in events]))
+    peak_tf, peak_bw, peak_kind = _peaks()
+    tail_bytes = n * c * (4 + 2 + 2) + 2 * (4 * c * c) * 2     # h f32 + x + out bf16, weights
+    tail_flops = 2.0 * 2 * 4 * c * c * n
+    achieved = tail_bytes / (tail_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak_bw, "unit": "GB/s", "frac": achieved / peak_bw,
+                "traffic": _profile_traffic("convnext_tail_c4.md"), "peak_source": f"{peak_kind} hbm_gbs",
+                "kernel": "k_convnext_tail", "bytes_per_launch": tail_bytes,
+                "tail_tflops": tail_flops / (tail_ms / 1e3) / 1e12}
+    cpu = None
+    if not args.no_cpu:
+        rng = np.random.default_rng(3)
+        f_np = rng.standard_normal((n, c)).astype(np.float32)
+        mk = lambda *shape, s=1.0: (rng.standard_normal(shape) * s).astype(np.float32)  # noqa: E731
+        sample = min(n, 1 << 16)
+        nthreads = os.cpu_count() or 1
+        spv, dt = cpu_convnext_step(nbr.cpu().numpy(), f_np, mk(c, 27, c, s=1 / np.sqrt(27 * c)), mk(c, s=0.1),
+                                    1 + mk(c, s=0.1), mk(c, s=0.1), mk(4 * c, c, s=1 / np.sqrt(c)), mk(4 * c, s=0.1),
+                                    mk(c, 4 * c, s=1 / np.sqrt(4 * c)), mk(c, s=0.1), sample, nthreads)
+        cpu = {"value": 1.0 / spv, "unit": "voxels/s", "cores": nthreads, "kind": "port",
+               "sample": f"oracle port: fp32 conv ({nthreads} threads) + numpy LayerNorm/MLP on {sample} rows "
+                         f"({dt:.2f} s)"}
+    line = {
+        "metric": CNX_METRIC, "value": n / (ms_step / 1e3), "unit": "voxels/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded noisy shell, random N(0,1) features, random weights of the block's shapes)",
+        "config": {"workload": f"{args.workload}: res-1024 noisy shell, ConvNeXt block C=64 bf16 operands, "
+                               "fp32 h and accumulate, neighbor map prebuilt", "voxels": n, "valid_pairs": pairs,
+                   "l2": "inputs larger than L2 (h 1.25 GB per step)"},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": None,
+        "gpu_launches": 2 * args.steps, "clocks": sampler.summary(),
+        "kernels": {"conv_ms": conv_ms, "tail_ms": tail_ms,
+                    "conv_tflops": 2.0 * c * c * pairs / (conv_ms / 1e3) / 1e12},
+    }
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -382,7 +507,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--workload", default=WORKLOAD, choices=["c4", "c4s"],
                     help="c4 (default, the benchmark) or c4s (half scale, for profiler captures)")
+    ap.add_argument("--op", default="stack", choices=["stack", "convnext"],
+                    help="stack (default, the benchmark: map + conv x2) or convnext (one ConvNeXt block)")
     args = ap.parse_args()
+    if args.op == "convnext":
+        if args.impl == "reference" or args.gpus != 1:
+            print(json.dumps({"impl": args.impl, "unavailable": "--op convnext is a single-GPU measurement of "
+                              "our kernels; its CPU baseline is in the line's cpu_baseline"}))
+            return 0
+        return run_convnext(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_gpu(args)
