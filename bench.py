@@ -16,6 +16,10 @@ fixed as N grows ("scaling": "strong").
 `--impl reference` times the reference algorithm's CPU implementation (the oracle port in
 oracle/, all host threads) on a bounded sample of the same workload.
 
+`--op c2s` measures one SparseResBlockC2S3d up-block (src/sparse.cpp:172-336) on the config-3
+parents (res-256 noisy shell) with its seeded child mask, Cin=256 -> Cout=128 bf16; metric
+children/s, roofline of conv1 (256 -> 8*128 channels, the block's dominant kernel).
+
 `--op convnext` measures one sparse ConvNeXt block instead (src/sparse.cpp:94-137 on the same
 shell): the conv into an fp32 h, then the fused LayerNorm + Linear C->4C + SiLU + Linear 4C->C +
 residual tail; metric voxels/s of the block, roofline of the tail kernel (HBM-bound).
@@ -497,6 +501,126 @@ def run_convnext(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- C2S up-block
+C2S_METRIC = ("children/s through one SparseResBlockC2S3d up-block (norm1+SiLU, conv1 Cin->8*Cout, subdivide, "
+              "channel-to-spatial + norm2 + SiLU, child map, conv2, skip), config-3 shell Cin=256 Cout=128")
+
+
+def cpu_c2s_step(coords, mask, feats, w, cout, planes=4):
+    """The oracle block on the parents of `planes` x-planes of the shell; seconds per child."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    xs = coords[:, -3]
+    x0 = int(np.median(xs))
+    sel = (xs >= x0) & (xs < x0 + planes)
+    c = np.ascontiguousarray(coords[sel][:, -3:])
+    t0 = time.perf_counter()
+    out, child, _ = oracle.c2s_block(c, feats[sel], w, cout, ext_mask=mask[sel])
+    dt = time.perf_counter() - t0
+    return dt / max(1, child.shape[0]), dt, int(sel.sum()), int(child.shape[0])
+
+
+def run_c2s(args):
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _load_package()
+    from trellis_cpp_b200 import ops, synth
+
+    cin, cout = 256, 128
+    parents = synth.coords_for("c3")
+    mask_np = synth.c3_mask(parents)
+    n = parents.shape[0]
+    rng = np.random.default_rng(33)
+    bf = torch.bfloat16
+
+    def t(a, dt=torch.float32):
+        return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev).to(dt)
+    w = {
+        "norm1.weight": (1 + 0.1 * rng.standard_normal(cin)).astype(np.float32),
+        "norm1.bias": (0.1 * rng.standard_normal(cin)).astype(np.float32),
+        "conv1.weight": (rng.standard_normal((8 * cout, 27, cin)) / np.sqrt(27 * cin)).astype(np.float32),
+        "conv1.bias": (0.1 * rng.standard_normal(8 * cout)).astype(np.float32),
+        "conv2.weight": (rng.standard_normal((cout, 27, cout)) / np.sqrt(27 * cout)).astype(np.float32),
+        "conv2.bias": (0.1 * rng.standard_normal(cout)).astype(np.float32),
+    }
+    feats_np = rng.standard_normal((n, cin)).astype(np.float32)
+    prm = {k: t(v, bf if k.endswith("conv1.weight") or k.endswith("conv2.weight") else torch.float32)
+           for k, v in w.items()}
+    coords = torch.from_numpy(parents).to(dev)
+    feats = t(feats_np, bf)
+    mask = torch.from_numpy(mask_np).to(dev)
+    m_children = int(mask_np.sum())
+
+    def step():
+        return ops.sparse_c2s(coords, feats, prm, cout, ext_mask=mask, max_children=m_children)
+
+    for _ in range(max(3, args.warmup)):
+        out, child, _ = step()
+    torch.cuda.synchronize()
+    ops.check_device()
+    m = child.shape[0]
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    sampler.start()
+    time.sleep(0.8)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    ops.check_device()
+    ms_step = e0.elapsed_time(e1) / args.steps
+
+    # conv1 alone (the block's dominant kernel) for the roofline
+    nbr = ops.build_neighbor_table(coords)
+    h = torch.empty((n, cin), dtype=bf, device=dev)
+    h.copy_(feats)
+    h1 = torch.empty((n, 8 * cout), dtype=torch.float32, device=dev)
+    for _ in range(3):
+        ops.sparse_submconv(h, nbr, prm["conv1.weight"], prm["conv1.bias"], out=h1)
+    torch.cuda.synchronize()
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    reps = 10
+    c0.record()
+    for _ in range(reps):
+        ops.sparse_submconv(h, nbr, prm["conv1.weight"], prm["conv1.bias"], out=h1)
+    c1.record()
+    torch.cuda.synchronize()
+    conv1_ms = c0.elapsed_time(c1) / reps
+    pairs = ops.count_valid_pairs(nbr, n)
+    peak_tf, peak_bw, peak_kind = _peaks()
+    flops1 = 2.0 * cin * 8 * cout * pairs
+    achieved = flops1 / (conv1_ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                "traffic": None, "peak_source": f"{peak_kind} bf16_tflops (burst)", "kernel": "k_submconv_brick (conv1)",
+                "flops_per_launch": flops1, "conv1_ms": conv1_ms}
+    cpu = None
+    if not args.no_cpu:
+        spc, dt, np_, nc_ = cpu_c2s_step(parents, mask_np, feats_np, w, cout)
+        cpu = {"value": 1.0 / spc, "unit": "children/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"oracle port (numpy fp64) c2s_block on {np_} parents of 4 x-planes -> {nc_} children "
+                         f"({dt:.2f} s)"}
+    line = {
+        "metric": C2S_METRIC, "value": m / (ms_step / 1e3), "unit": "children/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded res-256 noisy shell, seeded thickness mask, random weights of the block's shapes)",
+        "config": {"workload": "c3: res-256 shell parents -> res-512 children, external (texture-decoder style) mask, "
+                               "Cin=256 Cout=128 bf16 operands, fp32 conv outputs and skip",
+                   "parents": n, "children": m, "parent_valid_pairs": pairs,
+                   "l2": "conv1 output 1.0 GB per step (larger than L2)"},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": None,
+        "gpu_launches": (2 * ops.NBR_MAP_LAUNCHES + 9) * args.steps, "clocks": sampler.summary(),
+    }
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -507,15 +631,16 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--workload", default=WORKLOAD, choices=["c4", "c4s"],
                     help="c4 (default, the benchmark) or c4s (half scale, for profiler captures)")
-    ap.add_argument("--op", default="stack", choices=["stack", "convnext"],
-                    help="stack (default, the benchmark: map + conv x2) or convnext (one ConvNeXt block)")
+    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s"],
+                    help="stack (default, the benchmark: map + conv x2), convnext (one ConvNeXt block) or c2s "
+                         "(one C2S up-block)")
     args = ap.parse_args()
-    if args.op == "convnext":
+    if args.op in ("convnext", "c2s"):
         if args.impl == "reference" or args.gpus != 1:
-            print(json.dumps({"impl": args.impl, "unavailable": "--op convnext is a single-GPU measurement of "
+            print(json.dumps({"impl": args.impl, "unavailable": f"--op {args.op} is a single-GPU measurement of "
                               "our kernels; its CPU baseline is in the line's cpu_baseline"}))
             return 0
-        return run_convnext(args)
+        return run_convnext(args) if args.op == "convnext" else run_c2s(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_gpu(args)

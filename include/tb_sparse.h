@@ -179,6 +179,39 @@ tb_status tb_c2s_gather(tb_ctx* ctx, const void* src, const int32_t* gidx, int64
 tb_status tb_bias_act(tb_ctx* ctx, void* x, int64_t n, int c, const float* bias,
                       tb_dtype dtype, tb_epilogue epi);
 
+/* ---- SparseResBlockC2S3d ------------------------------------------------------------------
+ * Parameters of one C2S up-block, device pointers named after the reference's tensors under
+ * the block prefix (src/sparse.cpp:186-187,259-261,279,316). */
+typedef struct tb_c2s_params {
+    const float* to_subdiv_w;   /* [8][cin] float32; NULL when an external mask is given */
+    const float* to_subdiv_b;   /* [8] float32 or NULL */
+    const float* norm1_w;       /* [cin] float32 */
+    const float* norm1_b;       /* [cin] float32 */
+    const void* conv1_w;        /* [8*cout][27][cin] of dtype */
+    const float* conv1_b;       /* [8*cout] float32 or NULL */
+    const void* conv2_w;        /* [cout][27][cout] of dtype */
+    const float* conv2_b;       /* [cout] float32 or NULL */
+} tb_c2s_params;
+
+/* tb_sparse_c2s replaces trellis::sparse_c2s (include/sparse.h:27-35, src/sparse.cpp:172-336)
+ * with every step on the device: the to_subdiv logits and their > 0 mask (or ext_mask, uint8
+ * [8n], the texture decoder's external mask), the octant subdivide, norm1 (LayerNorm eps 1e-6,
+ * affine) + SiLU, conv1 to 8*cout channels (fp32), the channel-to-spatial gather fused with
+ * norm2 (no affine) + SiLU, conv2 on the children's neighbor map (fp32), and the skip (x viewed
+ * [8n][cin/8], gathered per child and each value repeated cout/(cin/8) times) added in fp32.
+ * feats: [n][cin] of dtype (device). Outputs (device): child_coords [max_children][coord_stride]
+ * in the reference's order, out [max_children][cout] of out_dtype, mask_out [8n] (may be NULL);
+ * *m_out (host) = M, the child count. The call reads M back from the device (one
+ * synchronisation between conv1 and the child half). M > max_children returns
+ * TB_ERR_TOO_LARGE with *m_out = M (outputs incomplete; 8n always suffices).
+ * Needs cin % 8 == 0, cout a multiple of cin/8 and of 8, cin, cout <= 2048, and both convs
+ * supported by tb_submconv for dtype. */
+tb_status tb_sparse_c2s(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord_stride,
+                        const void* feats, int cin, int cout, const tb_c2s_params* params,
+                        const uint8_t* ext_mask, tb_dtype dtype, tb_dtype out_dtype,
+                        int64_t max_children, int32_t* child_coords, void* out, uint8_t* mask_out,
+                        int64_t* m_out);
+
 /* ---- host-buffer end-to-end call --------------------------------------------------------
  * Mirrors one decoder stage graph run (run1 / GraphRun::run: upload inputs, compute, read
  * back; src/shape_decoder.cpp:34-51, src/sparse.cpp:145-169), without the LayerNorm/MLP

@@ -6,7 +6,12 @@
 //   sparse_submconv        include/sparse.h:19-22   (src/sparse.cpp:64-92), on host vectors:
 //                          the ggml graph builder takes a Model + name prefix, this one takes
 //                          the conv's device weights (ConvWeights)
+//   sparse_convnext        include/sparse.h:23-25 (src/sparse.cpp:94-137), on host vectors,
+//                          with the block's device weights (ConvNeXtWeights)
 //   subdivide              the octant loop of sparse_c2s (src/sparse.cpp:205-222)
+//   sparse_c2s             include/sparse.h:27-35 (src/sparse.cpp:172-336), the whole
+//                          SparseResBlockC2S3d; the block's device weights (C2SWeights) take
+//                          the place of Model + prefix
 //
 // All calls run on device `trellis::set_device()` (default 0) and the legacy stream, and
 // return after the result is back on the host.
@@ -43,6 +48,23 @@ std::vector<float> sparse_submconv(const ConvWeights& w, const std::vector<float
                                    const std::vector<int32_t>& nbr, int N,
                                    tb_epilogue epi = TB_EPI_NONE);
 
+// One ConvNeXt block's parameters on the device: the conv, norm (LayerNorm affine, float32
+// [C]), mlp.0 ([4C][C] of conv.dtype, bias float32 [4C]) and mlp.2 ([C][4C], bias [C]).
+struct ConvNeXtWeights {
+    ConvWeights conv;
+    const float* norm_w = nullptr;
+    const float* norm_b = nullptr;
+    const void* mlp0_w = nullptr;
+    const float* mlp0_b = nullptr;
+    const void* mlp2_w = nullptr;
+    const float* mlp2_b = nullptr;
+};
+
+// feats: [N][C] float32 (rounded to conv.dtype when that is bf16/f16); returns [N][C] float32:
+// conv -> LayerNorm (eps 1e-6) -> Linear C->4C -> SiLU -> Linear 4C->C -> + feats.
+std::vector<float> sparse_convnext(const ConvNeXtWeights& w, const std::vector<float>& feats,
+                                   const std::vector<int32_t>& nbr, int N);
+
 struct SubdivideResult {
     std::vector<std::array<int, 3>> coords;   // children, parent-major, octant ascending
     std::vector<int32_t> gidx;                // o + 8*i: row of the [8N, C] view of conv1
@@ -50,5 +72,28 @@ struct SubdivideResult {
 };
 // mask: uint8 [8*N], mask[o + 8*i] != 0 keeps octant o of parent i.
 SubdivideResult subdivide(const std::vector<std::array<int, 3>>& coords, const std::vector<uint8_t>& mask);
+
+// The reference's C2SResult (include/sparse.h:31): feats [M][C] float32 (ggml's [C, M]),
+// the children's coordinates, C, and the [8N] mask actually used.
+struct C2SResult {
+    std::vector<float> feats;
+    std::vector<std::array<int, 3>> coords;
+    int C = 0;
+    std::vector<uint8_t> subdiv;
+};
+
+// One C2S block's parameters, resident on the device (tb_c2s_params: to_subdiv, norm1, conv1,
+// conv2 under the block prefix); conv weights of `dtype`.
+struct C2SWeights {
+    tb_c2s_params p{};
+    tb_dtype dtype = TB_BF16;
+};
+
+// feats_in: [N][Cin] float32. ext_subdiv: a [8N] mask (the texture decoder's guide), or
+// nullptr to predict it with to_subdiv. With a bf16/f16 `w.dtype` the input is rounded to that
+// type first. Output features are float32.
+C2SResult sparse_c2s(const C2SWeights& w, const std::vector<float>& feats_in, int Cin,
+                     const std::vector<std::array<int, 3>>& coords, int Cout,
+                     const std::vector<uint8_t>* ext_subdiv = nullptr);
 
 }  // namespace trellis

@@ -17,7 +17,8 @@ def _declared_symbols():
 def test_header_declares_entry_points():
     syms = _declared_symbols()
     for s in ("tb_build_neighbor_map", "tb_submconv", "tb_subdivide", "tb_c2s_gather", "tb_bias_act",
-              "tb_submconv_stack_host", "tb_ctx_create", "tb_ctx_destroy"):
+              "tb_submconv_stack_host", "tb_ctx_create", "tb_ctx_destroy", "tb_convnext_tail",
+              "tb_sparse_convnext", "tb_sparse_c2s"):
         assert s in syms
 
 

@@ -31,6 +31,12 @@ class ConvLayer(ctypes.Structure):
     _fields_ = [("weight", _vp), ("bias", _vp), ("ci", _int), ("co", _int), ("epi", _int)]
 
 
+class C2SParams(ctypes.Structure):
+    """tb_c2s_params (include/tb_sparse.h)."""
+    _fields_ = [("to_subdiv_w", _vp), ("to_subdiv_b", _vp), ("norm1_w", _vp), ("norm1_b", _vp),
+                ("conv1_w", _vp), ("conv1_b", _vp), ("conv2_w", _vp), ("conv2_b", _vp)]
+
+
 SIGNATURES = {
     "tb_status_string": (ctypes.c_char_p, [_st]),
     "tb_version": (ctypes.c_char_p, []),
@@ -54,6 +60,8 @@ SIGNATURES = {
     "tb_convnext_tail": (_st, [_vp, _i64, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
     "tb_sparse_convnext": (_st, [_vp, _vp, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int,
                                  _vp]),
+    "tb_sparse_c2s": (_st, [_vp, _vp, _i64, _int, _vp, _int, _int, ctypes.POINTER(C2SParams), _vp, _int, _int,
+                            _i64, _vp, _vp, _vp, ctypes.POINTER(_i64)]),
 }
 
 _lib = None

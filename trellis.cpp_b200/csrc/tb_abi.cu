@@ -92,6 +92,8 @@ tb_status tb_ctx_destroy(tb_ctx* ctx) {
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->host_stage) cudaFree(ctx->host_stage);
     if (ctx->block_h) cudaFree(ctx->block_h);
+    if (ctx->c2s_ws1) cudaFree(ctx->c2s_ws1);
+    if (ctx->c2s_ws2) cudaFree(ctx->c2s_ws2);
     if (ctx->d_err) cudaFree(ctx->d_err);
     delete ctx;
     return TB_OK;

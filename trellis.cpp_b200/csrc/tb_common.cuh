@@ -37,6 +37,10 @@ struct tb_ctx {
     size_t brick_smem_set = 0;
     void* block_h = nullptr;       // fp32 conv output of tb_sparse_convnext
     size_t block_h_bytes = 0;
+    void* c2s_ws1 = nullptr;       // tb_sparse_c2s: parent map, mask, norm1 output, conv1 output, gidx
+    size_t c2s_ws1_bytes = 0;
+    void* c2s_ws2 = nullptr;       // tb_sparse_c2s: child map, norm2 output, conv2 output
+    size_t c2s_ws2_bytes = 0;
 };
 
 // Record a failure on the context and return the status.

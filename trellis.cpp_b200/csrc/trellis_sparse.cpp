@@ -128,6 +128,34 @@ std::vector<float> sparse_submconv(const ConvWeights& w, const std::vector<float
     return out;
 }
 
+std::vector<float> sparse_convnext(const ConvNeXtWeights& w, const std::vector<float>& feats,
+                                   const std::vector<int32_t>& nbr, int N) {
+    const int c = w.conv.ci;
+    if (w.conv.co != c) throw std::runtime_error("trellis: sparse_convnext: the conv must keep the width");
+    if ((int64_t)feats.size() != (int64_t)N * c || (int64_t)nbr.size() != (int64_t)27 * N)
+        throw std::runtime_error("trellis: sparse_convnext: feats/nbr size mismatch");
+    std::vector<float> out((size_t)N * c);
+    if (N == 0) return out;
+    cuda_ok(cudaSetDevice(g_device), "cudaSetDevice");
+    const size_t es = w.conv.dtype == TB_F32 ? 4 : 2;
+    DBuf df((size_t)N * c * es), dn((size_t)N * 27 * 4), dout((size_t)N * c * 4);
+    if (w.conv.dtype == TB_F32) {
+        cuda_ok(cudaMemcpy(df.p, feats.data(), feats.size() * 4, cudaMemcpyHostToDevice), "upload feats");
+    } else {
+        std::vector<uint16_t> h(feats.size());
+        for (size_t k = 0; k < feats.size(); ++k)
+            h[k] = w.conv.dtype == TB_BF16 ? f32_to_bf16_rne(feats[k]) : f32_to_f16_rne(feats[k]);
+        cuda_ok(cudaMemcpy(df.p, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "upload feats");
+    }
+    cuda_ok(cudaMemcpy(dn.p, nbr.data(), nbr.size() * 4, cudaMemcpyHostToDevice), "upload nbr");
+    ok(tb_sparse_convnext(ctx(), dn.as<int32_t>(), N, df.p, c, w.conv.weight, w.conv.bias, w.norm_w, w.norm_b,
+                          w.mlp0_w, w.mlp0_b, w.mlp2_w, w.mlp2_b, w.conv.dtype, TB_F32, dout.p),
+       "tb_sparse_convnext");
+    cuda_ok(cudaMemcpy(out.data(), dout.p, out.size() * 4, cudaMemcpyDeviceToHost), "download out");
+    ok(tb_ctx_check_device(ctx()), "convnext device check");
+    return out;
+}
+
 SubdivideResult subdivide(const std::vector<std::array<int, 3>>& coords, const std::vector<uint8_t>& mask) {
     const int64_t n = (int64_t)coords.size();
     if ((int64_t)mask.size() != 8 * n) throw std::runtime_error("trellis: subdivide: mask must have 8*N entries");
@@ -148,6 +176,50 @@ SubdivideResult subdivide(const std::vector<std::array<int, 3>>& coords, const s
     cuda_ok(cudaMemcpy(r.coords.data(), dch.p, (size_t)m * 12, cudaMemcpyDeviceToHost), "download children");
     cuda_ok(cudaMemcpy(r.gidx.data(), dg.p, (size_t)m * 4, cudaMemcpyDeviceToHost), "download gidx");
     cuda_ok(cudaMemcpy(r.mstart.data(), ds.p, (size_t)(n + 1) * 4, cudaMemcpyDeviceToHost), "download mstart");
+    return r;
+}
+
+C2SResult sparse_c2s(const C2SWeights& w, const std::vector<float>& feats_in, int Cin,
+                     const std::vector<std::array<int, 3>>& coords, int Cout,
+                     const std::vector<uint8_t>* ext_subdiv) {
+    const int64_t n = (int64_t)coords.size();
+    if ((int64_t)feats_in.size() != n * Cin) throw std::runtime_error("trellis: sparse_c2s: feats_in size mismatch");
+    if (ext_subdiv && (int64_t)ext_subdiv->size() != 8 * n)
+        throw std::runtime_error("trellis: sparse_c2s: ext_subdiv must have 8*N entries");
+    C2SResult r;
+    r.C = Cout;
+    r.subdiv.assign((size_t)(8 * n), 0);
+    if (n == 0) return r;
+    int64_t cap = 8 * n;
+    if (ext_subdiv) {
+        cap = 0;
+        for (uint8_t v : *ext_subdiv) cap += v != 0;
+    }
+    cuda_ok(cudaSetDevice(g_device), "cudaSetDevice");
+    const size_t es = w.dtype == TB_F32 ? 4 : 2;
+    DBuf dc((size_t)n * 12), df((size_t)n * Cin * es), dm((size_t)n * 8), dch((size_t)cap * 12),
+        dout((size_t)cap * Cout * 4), dmo((size_t)n * 8);
+    cuda_ok(cudaMemcpy(dc.p, coords.data(), (size_t)n * 12, cudaMemcpyHostToDevice), "upload coords");
+    if (w.dtype == TB_F32) {
+        cuda_ok(cudaMemcpy(df.p, feats_in.data(), feats_in.size() * 4, cudaMemcpyHostToDevice), "upload feats");
+    } else {
+        std::vector<uint16_t> h(feats_in.size());
+        for (size_t k = 0; k < feats_in.size(); ++k)
+            h[k] = w.dtype == TB_BF16 ? f32_to_bf16_rne(feats_in[k]) : f32_to_f16_rne(feats_in[k]);
+        cuda_ok(cudaMemcpy(df.p, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "upload feats");
+    }
+    if (ext_subdiv)
+        cuda_ok(cudaMemcpy(dm.p, ext_subdiv->data(), (size_t)n * 8, cudaMemcpyHostToDevice), "upload mask");
+    int64_t m = 0;
+    ok(tb_sparse_c2s(ctx(), dc.as<int32_t>(), n, 3, df.p, Cin, Cout, &w.p, ext_subdiv ? dm.as<uint8_t>() : nullptr,
+                     w.dtype, TB_F32, cap, dch.as<int32_t>(), dout.p, dmo.as<uint8_t>(), &m),
+       "tb_sparse_c2s");
+    r.coords.resize((size_t)m);
+    r.feats.resize((size_t)m * Cout);
+    cuda_ok(cudaMemcpy(r.coords.data(), dch.p, (size_t)m * 12, cudaMemcpyDeviceToHost), "download children");
+    cuda_ok(cudaMemcpy(r.feats.data(), dout.p, r.feats.size() * 4, cudaMemcpyDeviceToHost), "download feats");
+    cuda_ok(cudaMemcpy(r.subdiv.data(), dmo.p, (size_t)n * 8, cudaMemcpyDeviceToHost), "download mask");
+    ok(tb_ctx_check_device(ctx()), "c2s device check");
     return r;
 }
 

@@ -7,6 +7,9 @@ Names and argument meanings follow pwilkin/trellis.cpp's ``include/sparse.h``:
   weight / bias tensors in place of a Model + name prefix
 * :func:`subdivide` / :func:`c2s_gather` -- the subdivide and channel-to-spatial steps of
   ``trellis::sparse_c2s`` (src/sparse.cpp:205-222, 263-266, 288, 307)
+* :func:`sparse_convnext` / :func:`convnext_tail` -- ``trellis::sparse_convnext``
+  (sparse.h:23-25) and its LayerNorm / MLP / residual tail
+* :func:`sparse_c2s` -- ``trellis::sparse_c2s`` (sparse.h:27-35), the whole C2S up-block
 * :func:`submconv_stack_host` -- a host-buffer stage run (upload, map, convs, read back), the
   shape of ``run1`` / ``GraphRun::run`` (src/shape_decoder.cpp:34-51)
 
@@ -190,6 +193,58 @@ def subdivide(coords: torch.Tensor, mask: torch.Tensor, max_children: int | None
     check(_lib.load().tb_subdivide(ctx, _ptr(coords), n, s, _ptr(m8), _ptr(child), _ptr(gidx), _ptr(mstart),
                                    max_children, ctypes.byref(m)), "tb_subdivide", ctx)
     return child[: m.value], gidx[: m.value], mstart
+
+
+def sparse_c2s(coords: torch.Tensor, feats: torch.Tensor, params: dict, cout: int, ext_mask=None,
+               out_dtype=None, max_children: int | None = None):
+    """``trellis::sparse_c2s`` (include/sparse.h:27-35, src/sparse.cpp:172-336) on the device.
+
+    ``params`` maps the reference's tensor names under the block prefix to CUDA tensors:
+    ``to_subdiv.weight`` [8,Cin] / ``to_subdiv.bias`` [8] (float32; unused with ``ext_mask``),
+    ``norm1.weight`` / ``norm1.bias`` [Cin] (float32), ``conv1.weight`` [8*Cout,27,Cin] and
+    ``conv2.weight`` [Cout,27,Cout] (feats' dtype), ``conv1.bias`` / ``conv2.bias`` (float32 or
+    absent). Returns ``(out [M,Cout], child coords [M,s], mask [N,8] uint8)`` -- the fields of
+    the reference's ``C2SResult``."""
+    _need_cuda(coords, feats)
+    n, s = coords.shape
+    cin = feats.shape[1]
+    dt = feats.dtype
+    w1, w2 = params["conv1.weight"], params["conv2.weight"]
+    if w1.dtype != dt or w2.dtype != dt:
+        raise ValueError("conv weights must share feats' dtype")
+    if w1.numel() != 8 * cout * 27 * cin or w2.numel() != cout * 27 * cout:
+        raise ValueError("conv1.weight must be [8*Cout,27,Cin] and conv2.weight [Cout,27,Cout]")
+    _f32_vec(params["norm1.weight"], cin, "norm1.weight")
+    _f32_vec(params["norm1.bias"], cin, "norm1.bias")
+    for name, m in (("conv1.bias", 8 * cout), ("conv2.bias", cout)):
+        if params.get(name) is not None:
+            _f32_vec(params[name], m, name)
+    sw, sb = params.get("to_subdiv.weight"), params.get("to_subdiv.bias")
+    if ext_mask is None:
+        if sw is None or sw.dtype != torch.float32 or sw.numel() != 8 * cin or not sw.is_contiguous():
+            raise ValueError("to_subdiv.weight must be a contiguous float32 [8, Cin] tensor")
+        if sb is not None:
+            _f32_vec(sb, 8, "to_subdiv.bias")
+        em = None
+    else:
+        em = ext_mask.to(torch.uint8).contiguous()
+        if em.numel() != 8 * n:
+            raise ValueError("ext_mask must have 8*N entries")
+    if max_children is None:
+        max_children = 8 * n
+    od = dt if out_dtype is None else out_dtype
+    child = torch.empty((max_children, s), dtype=torch.int32, device=coords.device)
+    out = torch.empty((max_children, cout), dtype=od, device=coords.device)
+    mask = torch.empty((n, 8), dtype=torch.uint8, device=coords.device)
+    prm = _lib.C2SParams(_ptr(sw if em is None else None).value, _ptr(sb if em is None else None).value,
+                         _ptr(params["norm1.weight"]).value, _ptr(params["norm1.bias"]).value, _ptr(w1).value,
+                         _ptr(params.get("conv1.bias")).value, _ptr(w2).value, _ptr(params.get("conv2.bias")).value)
+    m = ctypes.c_int64()
+    ctx = context(coords.device)
+    check(_lib.load().tb_sparse_c2s(ctx, _ptr(coords.contiguous()), n, s, _ptr(feats), cin, cout, ctypes.byref(prm),
+                                    _ptr(em), _DT[dt], _DT[od], max_children, _ptr(child), _ptr(out), _ptr(mask),
+                                    ctypes.byref(m)), "tb_sparse_c2s", ctx)
+    return out[: m.value], child[: m.value], mask
 
 
 def c2s_gather(src: torch.Tensor, gidx: torch.Tensor, c: int) -> torch.Tensor:
