@@ -116,6 +116,14 @@ tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n,
                       const void* feats, int ci, const void* weight, const float* bias,
                       int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
 
+/* tb_submconv_range: the output rows [row0, row0 + nrows) of tb_submconv, the reference's
+ * submconv_range(r0, nr) (src/sparse.cpp:64-79) used to chunk a conv over voxels. nbr, feats
+ * and out are the whole n-row arrays (out [n][co]); only the range's rows of out are written,
+ * and its inputs may be any rows of feats. row0 must be a multiple of 256. */
+tb_status tb_submconv_range(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                            const void* feats, int ci, const void* weight, const float* bias,
+                            int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
+
 /* ---- ConvNeXt block --------------------------------------------------------------------
  * Replaces the per-voxel tail of sparse_convnext (include/sparse.h:23-25,
  * src/sparse.cpp:124-133) after its conv:
@@ -220,7 +228,11 @@ tb_status tb_sparse_c2s(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord
  * last output to out_host. Weights and biases are DEVICE pointers: they are resident
  * model parameters, as in the reference's backend buffer. Intermediate outputs use
  * `dtype`; the last layer writes `out_dtype`. Synchronises before returning. Host
- * buffers may be pageable; pinned buffers copy faster. */
+ * buffers may be pageable; pinned buffers copy faster, and with pinned buffers the call
+ * overlaps its transfers with the convs: after the coordinates and the map, the features go
+ * up in row chunks on a copy stream, each chunk's conv of each layer starts once the input
+ * rows it reads (found from the map) are on the device, and each finished chunk of the last
+ * layer goes down on a second copy stream while later chunks still compute or upload. */
 typedef struct tb_conv_layer {
     const void* weight;   /* [co][27][ci] of dtype, device */
     const float* bias;    /* [co] float32, device, or NULL */

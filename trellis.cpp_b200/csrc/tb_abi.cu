@@ -94,6 +94,11 @@ tb_status tb_ctx_destroy(tb_ctx* ctx) {
     if (ctx->block_h) cudaFree(ctx->block_h);
     if (ctx->c2s_ws1) cudaFree(ctx->c2s_ws1);
     if (ctx->c2s_ws2) cudaFree(ctx->c2s_ws2);
+    if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
+    if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
+    if (ctx->stage_ev_made)
+        for (cudaEvent_t e : ctx->stage_ev) cudaEventDestroy(e);
+    if (ctx->chunk_hi_host) cudaFreeHost(ctx->chunk_hi_host);
     if (ctx->d_err) cudaFree(ctx->d_err);
     delete ctx;
     return TB_OK;
@@ -124,17 +129,19 @@ tb_status tb_ctx_check_device(tb_ctx* ctx) {
     return TB_OK;
 }
 
-tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
-                      const void* weight, const float* bias, int co, tb_dtype dtype, tb_dtype out_dtype,
-                      tb_epilogue epi, void* out) {
+tb_status tb_submconv_range(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                            const void* feats, int ci, const void* weight, const float* bias, int co,
+                            tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
     if (!ctx) return TB_ERR_INVALID_ARG;
     if (n < 0 || ci <= 0 || co <= 0) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: n < 0 or channels <= 0");
+    if (row0 < 0 || nrows < 0 || row0 + nrows > n || row0 % 256 != 0)
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_range: need 0 <= row0, row0 % 256 == 0, row0 + nrows <= n");
     if (epi != TB_EPI_NONE && epi != TB_EPI_SILU) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: bad epilogue");
     if (dtype != TB_F32 && dtype != TB_F16 && dtype != TB_BF16)
         return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: bad dtype");
     if (out_dtype != TB_F32 && out_dtype != dtype)
         return tb_fail(ctx, TB_ERR_UNSUPPORTED, "tb_submconv: out_dtype must be TB_F32 or the operand dtype");
-    if (n == 0) return TB_OK;
+    if (nrows == 0) return TB_OK;
     if (!nbr || !feats || !weight || !out) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: null pointer");
     if (n >= (int64_t)INT32_MAX) return tb_fail(ctx, TB_ERR_TOO_LARGE, "tb_submconv: n must be < 2^31-1");
     if (!tb_aligned16(feats) || !tb_aligned16(weight) || !tb_aligned16(out) || (bias && !tb_aligned16(bias)))
@@ -142,15 +149,23 @@ tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* fe
     if (feats == out) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: out must not alias feats");
     TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     if (dtype == TB_F32)
-        return tb_conv_f32_launch(ctx, nbr, n, reinterpret_cast<const float*>(feats), ci,
+        return tb_conv_f32_launch(ctx, nbr, n, row0, nrows, reinterpret_cast<const float*>(feats), ci,
                                   reinterpret_cast<const float*>(weight), bias, co, epi, reinterpret_cast<float*>(out));
     const bool pair = ctx->conv_path == TB_CONV_PAIR ||
                       (ctx->conv_path == TB_CONV_AUTO && tb_conv_pair_supported(ci, co));
-    if (pair) return tb_conv_pair_launch(ctx, nbr, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
+    if (pair)
+        return tb_conv_pair_launch(ctx, nbr, n, row0, nrows, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
     const bool brick = ctx->conv_path == TB_CONV_BRICK ||
                        (ctx->conv_path == TB_CONV_AUTO && tb_conv_brick_supported(ci, co));
-    if (brick) return tb_conv_brick_launch(ctx, nbr, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
-    return tb_conv_tc_launch(ctx, nbr, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
+    if (brick)
+        return tb_conv_brick_launch(ctx, nbr, n, row0, nrows, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
+    return tb_conv_tc_launch(ctx, nbr, n, row0, nrows, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
+}
+
+tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
+                      const void* weight, const float* bias, int co, tb_dtype dtype, tb_dtype out_dtype,
+                      tb_epilogue epi, void* out) {
+    return tb_submconv_range(ctx, nbr, n, 0, n, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
 }
 
 tb_status tb_convnext_tail(tb_ctx* ctx, int64_t n, int c, const void* h, tb_dtype h_dtype, const void* x,
@@ -196,53 +211,6 @@ tb_status tb_ctx_set_conv_path(tb_ctx* ctx, tb_conv_path path) {
         return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_ctx_set_conv_path: unknown path");
     ctx->conv_path = path;
     return TB_OK;
-}
-
-tb_status tb_submconv_stack_host(tb_ctx* ctx, const int32_t* coords_host, int64_t n, int coord_stride,
-                                 const void* feats_host, const tb_conv_layer* layers, int nlayers,
-                                 tb_dtype dtype, tb_dtype out_dtype, void* out_host) {
-    if (!ctx) return TB_ERR_INVALID_ARG;
-    if (n < 0 || nlayers <= 0 || !layers || (coord_stride != 3 && coord_stride != 4))
-        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_stack_host: bad arguments");
-    for (int l = 0; l < nlayers; ++l) {
-        if (layers[l].ci <= 0 || layers[l].co <= 0 || !layers[l].weight)
-            return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_stack_host: bad layer");
-        if (l > 0 && layers[l].ci != layers[l - 1].co)
-            return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_stack_host: layer ci != previous co");
-    }
-    if (n == 0) return TB_OK;
-    if (!coords_host || !feats_host || !out_host)
-        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_stack_host: null pointer");
-    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
-    const size_t es = tb_dtype_size(dtype);
-    int cmax = layers[0].ci;
-    for (int l = 0; l < nlayers; ++l) cmax = std::max(cmax, layers[l].co);
-    auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
-    const size_t coords_b = al((size_t)n * coord_stride * 4);
-    const size_t nbr_b = al((size_t)n * 27 * 4);
-    const size_t feat_b = al((size_t)n * cmax * std::max<size_t>(es, tb_dtype_size(out_dtype)));
-    tb_status s = tb_ensure(ctx, &ctx->host_stage, &ctx->host_stage_bytes, coords_b + nbr_b + 2 * feat_b, "host-call staging");
-    if (s != TB_OK) return s;
-    uint8_t* base = reinterpret_cast<uint8_t*>(ctx->host_stage);
-    int32_t* d_coords = reinterpret_cast<int32_t*>(base);
-    int32_t* d_nbr = reinterpret_cast<int32_t*>(base + coords_b);
-    uint8_t* buf[2] = {base + coords_b + nbr_b, base + coords_b + nbr_b + feat_b};
-    TB_CUDA_TRY(ctx, cudaMemcpyAsync(d_coords, coords_host, (size_t)n * coord_stride * 4, cudaMemcpyHostToDevice, ctx->stream));
-    TB_CUDA_TRY(ctx, cudaMemcpyAsync(buf[0], feats_host, (size_t)n * layers[0].ci * es, cudaMemcpyHostToDevice, ctx->stream));
-    s = tb_build_neighbor_map(ctx, d_coords, n, coord_stride, d_nbr);
-    if (s != TB_OK) return s;
-    int cur = 0;
-    for (int l = 0; l < nlayers; ++l) {
-        const tb_dtype od = (l == nlayers - 1) ? out_dtype : dtype;
-        s = tb_submconv(ctx, d_nbr, n, buf[cur], layers[l].ci, layers[l].weight, layers[l].bias, layers[l].co,
-                        dtype, od, layers[l].epi, buf[cur ^ 1]);
-        if (s != TB_OK) return s;
-        cur ^= 1;
-    }
-    TB_CUDA_TRY(ctx, cudaMemcpyAsync(out_host, buf[cur], (size_t)n * layers[nlayers - 1].co * tb_dtype_size(out_dtype),
-                                     cudaMemcpyDeviceToHost, ctx->stream));
-    TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-    return tb_ctx_check_device(ctx);
 }
 
 }  // extern "C"

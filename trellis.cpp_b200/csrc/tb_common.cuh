@@ -41,6 +41,12 @@ struct tb_ctx {
     size_t c2s_ws1_bytes = 0;
     void* c2s_ws2 = nullptr;       // tb_sparse_c2s: child map, norm2 output, conv2 output
     size_t c2s_ws2_bytes = 0;
+    // tb_submconv_stack_host's pipeline: copy streams, chunk events, pinned chunk bounds
+    cudaStream_t copy_in = nullptr;
+    cudaStream_t copy_out = nullptr;
+    cudaEvent_t stage_ev[2 + 2 * 32] = {};
+    bool stage_ev_made = false;
+    int32_t* chunk_hi_host = nullptr;
 };
 
 // Record a failure on the context and return the status.
@@ -84,20 +90,22 @@ tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int s
                             int32_t* nbr, void* table, uint64_t cap, const int* gate);
 tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws);
 size_t tb_nbr_workspace_bytes(int64_t n);
-tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
-                            const void* weight, const float* bias, int co, tb_dtype dtype,
-                            tb_dtype out_dtype, tb_epilogue epi, void* out);
-tb_status tb_conv_f32_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const float* feats, int ci,
-                             const float* weight, const float* bias, int co, tb_epilogue epi,
-                             float* out);
+tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                            const void* feats, int ci, const void* weight, const float* bias, int co,
+                            tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
+// The conv kernels compute output rows [row0, row0 + nrows) of an n-row map (tap stride and
+// sentinel n); row0 is a multiple of 256.
+tb_status tb_conv_f32_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                             const float* feats, int ci, const float* weight, const float* bias, int co,
+                             tb_epilogue epi, float* out);
 bool tb_conv_tc_supported(int ci, int co);
-tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
-                               const void* weight, const float* bias, int co, tb_dtype dtype,
-                               tb_dtype out_dtype, tb_epilogue epi, void* out);
+tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                               const void* feats, int ci, const void* weight, const float* bias, int co,
+                               tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
 bool tb_conv_brick_supported(int ci, int co);
-tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
-                              const void* weight, const float* bias, int co, tb_dtype dtype,
-                              tb_dtype out_dtype, tb_epilogue epi, void* out);
+tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                              const void* feats, int ci, const void* weight, const float* bias, int co,
+                              tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
 bool tb_conv_pair_supported(int ci, int co);
 tb_status tb_convnext_tail_launch(tb_ctx* ctx, int64_t n, int c, const void* h, tb_dtype h_dtype, const void* x,
                                   const float* nw, const float* nb, const void* w1, const float* b1, const void* w2,

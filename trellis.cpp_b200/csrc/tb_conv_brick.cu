@@ -93,7 +93,9 @@ struct BrickParams {
     int64_t n;
     int ci, co;
     int out_kind, epi;
-    int ntiles, ncb, nkc, nb;
+    int ntiles, ncb, nkc, nb;  // ntiles: tiles of the range
+    int tile0;                 // first tile of the range
+    int64_t row_end;           // rows at or past it are not stored
     int nbst, nbst_log2;   // weight stages (2, 4 or 8)
     int brick_cap;         // rows per brick buffer (multiple of kBox)
     uint32_t b_bytes;      // nb * 128
@@ -207,7 +209,7 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         int it = 0, bseq = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++it) {
-            const int tile = u / p.ncb;
+            const int tile = p.tile0 + u / p.ncb;
             const int buf = it & 1;
             if (!mbar_wait(nbre + 8 * buf, ((it >> 1) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
             const int64_t r0 = (int64_t)tile * kTileM;
@@ -416,7 +418,7 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
         int it = 0;
         const size_t esize = p.out_kind == 0 ? 4 : 2;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
-            const int tile = u / p.ncb, cb = u % p.ncb;
+            const int tile = p.tile0 + u / p.ncb, cb = u % p.ncb;
             const int d = p.nd == 2 ? (it & 1) : 0;
             const uint32_t dph = p.nd == 2 ? ((it >> 1) & 1) : (it & 1);
             bool ok = mbar_wait(df + 8 * d, dph, s_abort, p.err);
@@ -425,7 +427,7 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
             if (threadIdx.x == 0) { TB_STAMP(4, it); TB_PROGRESS(6, it + 1); }
             tc_fence_after();
             const int64_t row = (int64_t)tile * kTileM + q * 32 + lane;
-            const bool valid = row < p.n;
+            const bool valid = row < p.row_end;
             uint8_t* orow = p.out + ((size_t)row * p.co + (size_t)cb * p.nb) * esize;
             const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
             const uint32_t d0 = lane_base + (uint32_t)(d * p.nb);
@@ -466,9 +468,9 @@ bool tb_conv_brick_supported(int ci, int co) {
     return ci > 0 && ci % 64 == 0 && co > 0 && co % 16 == 0 && (co <= 256 || co % 256 == 0);
 }
 
-tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
-                               const void* weight, const float* bias, int co, tb_dtype dtype,
-                               tb_dtype out_dtype, tb_epilogue epi, void* out) {
+tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                               const void* feats, int ci, const void* weight, const float* bias, int co,
+                               tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
     if (!tb_conv_brick_supported(ci, co))
         return tb_fail(ctx, TB_ERR_UNSUPPORTED, "brick conv needs ci%64==0 and co%16==0 (<=256 or 256k)");
     if (!ctx->encode_tiled) {
@@ -495,7 +497,9 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const
     p.co = co;
     p.out_kind = out_dtype == TB_F32 ? 0 : (out_dtype == TB_F16 ? 1 : 2);
     p.epi = epi;
-    p.ntiles = (int)((n + kTileM - 1) / kTileM);
+    p.tile0 = (int)(row0 / kTileM);
+    p.row_end = row0 + nrows;
+    p.ntiles = (int)((row0 + nrows + kTileM - 1) / kTileM) - p.tile0;
     p.ncb = co / nb;
     p.nkc = ci / 64;
     p.nb = nb;

@@ -17,7 +17,8 @@ constexpr int BC = 64;   // output channels per block
 constexpr int BK = 32;   // input channels per step
 
 __global__ void __launch_bounds__(256)
-k_submconv_f32(const int32_t* __restrict__ nbr, int64_t n, const float* __restrict__ feats, int ci,
+k_submconv_f32(const int32_t* __restrict__ nbr, int64_t n, int64_t row0, int64_t row_end,
+               const float* __restrict__ feats, int ci,
                const float* __restrict__ w, const float* __restrict__ bias, int co, int epi,
                float* __restrict__ out) {
     __shared__ float xs[BR][BK + 1];
@@ -25,7 +26,7 @@ k_submconv_f32(const int32_t* __restrict__ nbr, int64_t n, const float* __restri
     __shared__ int32_t rows[BR];
     const int tx = threadIdx.x & 7;          // channel group: o = o0 + tx + 8*j
     const int ty = threadIdx.x >> 3;         // row within block
-    const int64_t r0 = (int64_t)blockIdx.x * BR;
+    const int64_t r0 = row0 + (int64_t)blockIdx.x * BR;
     const int o0 = blockIdx.y * BC;
     float acc[8];
 #pragma unroll
@@ -60,7 +61,7 @@ k_submconv_f32(const int32_t* __restrict__ nbr, int64_t n, const float* __restri
         }
     }
     const int64_t r = r0 + ty;
-    if (r >= n) return;
+    if (r >= row_end) return;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int o = o0 + tx + 8 * j;
@@ -73,10 +74,11 @@ k_submconv_f32(const int32_t* __restrict__ nbr, int64_t n, const float* __restri
 
 }  // namespace
 
-tb_status tb_conv_f32_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const float* feats, int ci,
-                             const float* weight, const float* bias, int co, tb_epilogue epi, float* out) {
-    dim3 grid((unsigned)((n + BR - 1) / BR), (unsigned)((co + BC - 1) / BC));
-    k_submconv_f32<<<grid, 256, 0, ctx->stream>>>(nbr, n, feats, ci, weight, bias, co, (int)epi, out);
+tb_status tb_conv_f32_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                             const float* feats, int ci, const float* weight, const float* bias, int co,
+                             tb_epilogue epi, float* out) {
+    dim3 grid((unsigned)((nrows + BR - 1) / BR), (unsigned)((co + BC - 1) / BC));
+    k_submconv_f32<<<grid, 256, 0, ctx->stream>>>(nbr, n, row0, row0 + nrows, feats, ci, weight, bias, co, (int)epi, out);
     TB_LAUNCH_CHECK(ctx, "k_submconv_f32");
     return TB_OK;
 }

@@ -88,7 +88,9 @@ struct PairParams {
     int64_t n;
     int co;
     int out_kind, epi;
-    int ntiles, npairs;
+    int ntiles, npairs;    // npairs: end of the pair range (absolute)
+    int pr0;               // first pair of the range (rows 256 * pr0 ...)
+    int64_t row_end;       // rows at or past it are computed (whole pairs) but not stored
     int ring_rows;               // multiple of kBox
     int nbr_bulk;                // map pointer 16-byte aligned: tiles fetch indices with bulk copies
     uint32_t w_tap_bytes;        // (co/2) rows x 128 B, rounded up to 1024
@@ -202,13 +204,13 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         // the first kNB - 1 tiles' indices
         {
             int j = 0;
-            for (int prj = cid; prj < p.npairs && j < kNB - 1; prj += ncl, ++j) fetch_nbr(prj, j);
+            for (int prj = p.pr0 + cid; prj < p.npairs && j < kNB - 1; prj += ncl, ++j) fetch_nbr(prj, j);
         }
         int it = 0, k = 0, koldest = 0, head = 0, used = 0;
         int buf = 0, ph = 0;                     // consumer side of the index buffers
         int fbuf = kNB - 1, fph = 0;             // next fetch: tile it + kNB - 1
         bool ok = true;
-        for (int pr = cid; pr < p.npairs && ok; pr += ncl, ++it) {
+        for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
             const int64_t r0 = (int64_t)(2 * pr + (int)rank) * kTileM;
             const int nvalid = p.n - r0 < kTileM ? (int)(p.n - r0) : kTileM;
             if (leader && lane == 0) TB_STAMP(10, it);
@@ -317,7 +319,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         int u = 0, uph = 0;                 // unit slot and its phase
         bool ok = mbar_wait(wbar, 0, s_abort, p.err);   // this CTA's weight half has landed
         int it = 0, k = 0, buf = 0, ph = 0;
-        for (int pr = cid; pr < p.npairs && ok; pr += ncl, ++it) {
+        for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
             if (!mbar_wait(nbrf + 8 * buf, (uint32_t)ph, s_abort, p.err)) { ok = false; break; }
             const int32_t* rows = s_nbr + buf * kNbrInts;
             const int64_t r0 = (int64_t)(2 * pr + (int)rank) * kTileM;
@@ -443,7 +445,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             const uint32_t dt = tmem_base + 64u * (uint32_t)mi;
             const uint32_t a_base = tmem_base + kACol0 + 64u * kNU * (uint32_t)mi;
             const uint32_t afh = af + 8 * kNU * mi, aeh = ae + 8 * kNU * mi;
-            for (int pr = cid; pr < p.npairs && ok; pr += ncl, ++it) {
+            for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
                 // the epilogue has read this issuer's accumulator for the previous tile
                 ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(de + 8 * mi, (uint32_t)((it & 1) ^ 1), s_abort, p.err));
                 if (!ok) break;
@@ -495,7 +497,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         const int q = warp;
         int it = 0;
         const size_t esize = p.out_kind == 0 ? 4 : 2;
-        for (int pr = cid; pr < p.npairs; pr += ncl, ++it) {
+        for (int pr = p.pr0 + cid; pr < p.npairs; pr += ncl, ++it) {
             const uint32_t dph = (uint32_t)(it & 1);
             bool ok = mbar_wait_cluster_relaxed(df, dph, s_abort, p.err);
             if (ok) ok = mbar_wait_cluster_relaxed(df + 8, dph, s_abort, p.err);
@@ -524,7 +526,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 mbar_arrive_cluster_relaxed(de + 8, 0);
             }
             const int64_t row = (int64_t)(2 * pr + (int)rank) * kTileM + q * 32 + lane;
-            if (row < p.n) {
+            if (row < p.row_end) {
                 uint8_t* orow = p.out + (size_t)row * p.co * esize;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -553,9 +555,9 @@ extern long long* g_trace_buffer;
 
 bool tb_conv_pair_supported(int ci, int co) { return ci == 64 && (co == 64 || co == 32); }
 
-tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
-                              const void* weight, const float* bias, int co, tb_dtype dtype,
-                              tb_dtype out_dtype, tb_epilogue epi, void* out) {
+tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                              const void* feats, int ci, const void* weight, const float* bias, int co,
+                              tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
     if (!tb_conv_pair_supported(ci, co))
         return tb_fail(ctx, TB_ERR_UNSUPPORTED, "pair conv needs ci == 64 and co in {32, 64}");
     if (!ctx->encode_tiled) {
@@ -581,7 +583,10 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const 
     p.out_kind = out_dtype == TB_F32 ? 0 : (out_dtype == TB_F16 ? 1 : 2);
     p.epi = epi;
     p.ntiles = (int)((n + kTileM - 1) / kTileM);
-    p.npairs = (p.ntiles + 1) / 2;
+    // output rows [row0, row0 + nrows): row0 is a multiple of 256 (one pair of tiles)
+    p.pr0 = (int)(row0 / (2 * kTileM));
+    p.npairs = (int)((row0 + nrows + 2 * kTileM - 1) / (2 * kTileM));
+    p.row_end = row0 + nrows;
     const int nhalf = co / 2;
     p.w_tap_bytes = ((uint32_t)nhalf * 128u + 1023u) & ~1023u;
     const uint32_t fmt = dtype == TB_BF16 ? 1u : 0u;
@@ -619,7 +624,7 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const 
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the feature view");
     }
-    const int nclusters = std::max(1, std::min(p.npairs, ctx->num_sms / 2));
+    const int nclusters = std::max(1, std::min(p.npairs - p.pr0, ctx->num_sms / 2));
     cudaError_t e = cudaSuccess;
     if (smem > ctx->pair_smem_set) {
         e = cudaFuncSetAttribute(k_submconv_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -55,7 +55,9 @@ struct ConvParams {
     int ci, co;
     int out_kind;       // 0 f32, 1 f16, 2 bf16
     int epi;
-    int ntiles, ncb, nkc;
+    int ntiles, ncb, nkc;  // ntiles: tiles of the range
+    int tile0;             // first tile of the range
+    int64_t row_end;       // rows at or past it are not stored
     int kc;             // channels per chunk (16, 32 or 64)
     int nb;             // accumulator columns per work unit
     int stages;
@@ -139,7 +141,7 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ 
         // ------------------------------------------------------------------ neighbor loader
         int it = 0;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
-            const int tile = u / p.ncb;
+            const int tile = p.tile0 + u / p.ncb;
             const int buf = it & 1;
             const uint32_t ph = (it >> 1) & 1;
             if (!mbar_wait(nbre_bar(buf), ph ^ 1, s_abort, p.err)) break;
@@ -258,14 +260,14 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ 
         int it = 0;
         const size_t esize = p.out_kind == 0 ? 4 : 2;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++it) {
-            const int tile = u / p.ncb, cb = u % p.ncb;
+            const int tile = p.tile0 + u / p.ncb, cb = u % p.ncb;
             const int ab = it & 1;
             const uint32_t aph = (it >> 1) & 1;
             if (!mbar_wait(accf_bar(ab), aph, s_abort, p.err)) break;
             if (threadIdx.x == 0) TB_STAMP(2, it);
             tc_fence_after();
             const int64_t pos = (int64_t)tile * kTileM + q * 32 + lane;
-            const bool valid = pos < p.n;
+            const bool valid = pos < p.row_end;
             const int64_t row = (valid && p.perm) ? (int64_t)__ldg(p.perm + pos) : pos;
             uint8_t* orow = p.out + ((size_t)row * p.co + (size_t)cb * p.nb) * esize;
             for (int c0 = 0; c0 < p.nb; c0 += 16) {
@@ -305,9 +307,9 @@ bool tb_conv_tc_supported(int ci, int co) {
     return ci_ok && co_ok;
 }
 
-tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const void* feats, int ci,
-                            const void* weight, const float* bias, int co, tb_dtype dtype,
-                            tb_dtype out_dtype, tb_epilogue epi, void* out) {
+tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
+                            const void* feats, int ci, const void* weight, const float* bias, int co,
+                            tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
     if (!tb_conv_tc_supported(ci, co))
         return tb_fail(ctx, TB_ERR_UNSUPPORTED, "tb_submconv: tensor-core path needs ci in {16,32,64k} and co%16==0 (<=256 or 256k)");
     if (!ctx->encode_tiled) {
@@ -337,7 +339,9 @@ tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, const vo
     p.co = co;
     p.out_kind = out_dtype == TB_F32 ? 0 : (out_dtype == TB_F16 ? 1 : 2);
     p.epi = epi;
-    p.ntiles = (int)((n + kTileM - 1) / kTileM);
+    p.tile0 = (int)(row0 / kTileM);
+    p.row_end = row0 + nrows;
+    p.ntiles = (int)((row0 + nrows + kTileM - 1) / kTileM) - p.tile0;
     p.ncb = co / nb;
     p.nkc = ci / kc;
     p.kc = kc;

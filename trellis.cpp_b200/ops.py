@@ -122,6 +122,24 @@ def sparse_submconv(feats: torch.Tensor, nbr: torch.Tensor, weight: torch.Tensor
     return out
 
 
+def sparse_submconv_range(feats: torch.Tensor, nbr: torch.Tensor, weight: torch.Tensor, bias, row0: int, nrows: int,
+                          out: torch.Tensor, epi: str = "none") -> torch.Tensor:
+    """Rows [row0, row0 + nrows) of :func:`sparse_submconv` written into ``out`` [N,Co] (the
+    reference's ``submconv_range``, src/sparse.cpp:64-79); row0 a multiple of 256."""
+    _need_cuda(feats, nbr, weight, bias, out)
+    n, ci = feats.shape
+    co = weight.shape[0]
+    if weight.dtype != feats.dtype or weight.numel() != co * 27 * ci or nbr.numel() != 27 * n:
+        raise ValueError("weight must be [Co,27,Ci] of feats' dtype and nbr 27*N")
+    if out.shape != (n, co):
+        raise ValueError("out must be [N, Co]")
+    ctx = context(feats.device)
+    check(_lib.load().tb_submconv_range(ctx, _ptr(nbr), n, row0, nrows, _ptr(feats), ci, _ptr(weight), _ptr(bias), co,
+                                        _DT[feats.dtype], _DT[out.dtype], _EPI[epi], _ptr(out)),
+          "tb_submconv_range", ctx)
+    return out
+
+
 def _f32_vec(t, n, name):
     if t is None or not t.is_cuda or t.dtype != torch.float32 or t.numel() != n or not t.is_contiguous():
         raise ValueError(f"{name} must be a contiguous float32 CUDA tensor of {n} values")
