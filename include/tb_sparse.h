@@ -252,11 +252,14 @@ tb_status tb_submconv_stack_host(tb_ctx* ctx, const int32_t* coords_host, int64_
  * [z_min, z_min + nz); voxels outside the range are ignored. counts is int64 [nz], zeroed by
  * the call.
  * tb_gather_rows: out[k] = src[rows[k]] for k < m, row_bytes per row (halo packing and
- * owned-row extraction). row_bytes must be a multiple of 4. */
+ * owned-row extraction). tb_scatter_rows: out[rows[k]] = src[k] (received halo rows into
+ * their local positions). row_bytes must be a multiple of 4. */
 tb_status tb_zslab_counts(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord_stride,
                           int32_t z_min, int32_t nz, int64_t* counts);
 tb_status tb_gather_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t m,
                          int64_t row_bytes, void* out);
+tb_status tb_scatter_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t m,
+                          int64_t row_bytes, void* out);
 
 #ifdef __cplusplus
 }

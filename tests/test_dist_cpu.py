@@ -31,21 +31,27 @@ def _worker(rank, world, init_file, result_dir):
         feats = rng.standard_normal((n, 16)).astype(np.float32)
         w = (rng.standard_normal((8, 27, 16)) / 20).astype(np.float32)
         plan = tbdist.plan_slabs(coords, world, rank)
-        x = torch.zeros((plan.n_local, 16), dtype=torch.float32)
-        x[: plan.n_owned] = torch.from_numpy(feats[plan.owned])
-        tbdist.exchange_halo(plan, x, lambda t, idx: t.index_select(0, idx.long()).contiguous())
-        halo_rows = np.concatenate([plan.halo_lo, plan.halo_hi])
-        ok_halo = np.array_equal(x[plan.n_owned:].numpy(), feats[halo_rows])
+        gather = lambda t, idx: t.index_select(0, idx.long()).contiguous()   # noqa: E731
+        scatter = lambda t, idx, src: t.index_copy_(0, idx.long(), src)       # noqa: E731
+        own = torch.from_numpy(plan.own_local)
+        assert np.array_equal(plan.local_rows()[plan.own_local], plan.owned)
+        assert np.all(np.diff(plan.local_rows()) > 0)           # local rows in global order
+        x = torch.full((plan.n_local, 16), float("nan"), dtype=torch.float32)
+        x[own] = torch.from_numpy(feats[plan.owned])
+        tbdist.exchange_halo(plan, x, gather, scatter)
+        halo = np.concatenate([plan.recv_lo, plan.recv_hi])
+        halo_rows = plan.local_rows()[halo]
+        ok_halo = np.array_equal(np.sort(halo_rows), np.sort(np.concatenate([plan.halo_lo, plan.halo_hi])))
+        ok_halo = ok_halo and np.array_equal(x.numpy(), feats[plan.local_rows()])   # every local row filled
         # the started-then-finished form the GPU step uses to overlap the map build
-        x2 = torch.zeros_like(x)
-        x2[: plan.n_owned] = 2 * x[: plan.n_owned]
-        handle = tbdist.exchange_halo(plan, x2, lambda t, idx: t.index_select(0, idx.long()).contiguous(),
-                                      wait=False)
+        x2 = torch.full_like(x, float("nan"))
+        x2[own] = 2 * x[own]
+        handle = tbdist.exchange_halo(plan, x2, gather, scatter, wait=False)
         local = coords[plan.local_rows()]
         nbr_local = oracle.build_neighbor_table(local)          # work done while the transfer runs
         tbdist.finish_halo(handle)
-        ok_halo = ok_halo and np.array_equal(x2[plan.n_owned:].numpy(), 2 * feats[halo_rows])
-        out_local = oracle.submconv(nbr_local, x.numpy(), w)[: plan.n_owned]
+        ok_halo = ok_halo and np.array_equal(x2.numpy(), 2 * feats[plan.local_rows()])
+        out_local = oracle.submconv(nbr_local, x.numpy(), w)[plan.own_local]
         out_global = oracle.submconv(oracle.build_neighbor_table(coords), feats, w)[plan.owned]
         np.savez(os.path.join(result_dir, f"r{rank}.npz"), owned=plan.owned, ok_halo=ok_halo,
                  ok_conv=np.array_equal(out_local, out_global), n_halo=halo_rows.size)

@@ -58,6 +58,7 @@ SIGNATURES = {
                                      _int, _vp]),
     "tb_zslab_counts": (_st, [_vp, _vp, _i64, _int, _i32, _i32, _vp]),
     "tb_gather_rows": (_st, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "tb_scatter_rows": (_st, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "tb_convnext_tail": (_st, [_vp, _i64, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
     "tb_sparse_convnext": (_st, [_vp, _vp, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int,
                                  _vp]),

@@ -295,6 +295,25 @@ __global__ void k_gather_rows(const uint32_t* __restrict__ src, const int32_t* _
     }
 }
 
+// out[rows[k]] = src[k]: the inverse of k_gather_rows (halo rows received into a contiguous
+// buffer land at their positions in the local row order).
+__global__ void k_scatter_rows(const uint32_t* __restrict__ src, const int32_t* __restrict__ rows,
+                               int64_t m, int64_t words, uint32_t* __restrict__ out) {
+    const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= m) return;
+    const int64_t r = rows[warp];
+    const uint32_t* s = src + warp * words;
+    uint32_t* d = out + r * words;
+    if ((words & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+        const int64_t v = words >> 2;
+        for (int64_t k = lane; k < v; k += 32)
+            reinterpret_cast<uint4*>(d)[k] = reinterpret_cast<const uint4*>(s)[k];
+    } else {
+        for (int64_t k = lane; k < words; k += 32) d[k] = s[k];
+    }
+}
+
 }  // namespace
 
 uint64_t tb_hash_capacity(int64_t n) {
@@ -423,6 +442,21 @@ extern "C" tb_status tb_gather_rows(tb_ctx* ctx, const void* src, const int32_t*
     k_gather_rows<<<(unsigned)((threads + 255) / 256), 256, 0, ctx->stream>>>(
         reinterpret_cast<const uint32_t*>(src), rows, m, row_bytes / 4, reinterpret_cast<uint32_t*>(out));
     TB_LAUNCH_CHECK(ctx, "k_gather_rows");
+    return TB_OK;
+}
+
+extern "C" tb_status tb_scatter_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t m,
+                                     int64_t row_bytes, void* out) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (m < 0 || row_bytes <= 0 || (row_bytes & 3))
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_scatter_rows: m < 0 or row_bytes not a positive multiple of 4");
+    if (m == 0) return TB_OK;
+    if (!src || !rows || !out) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_scatter_rows: null pointer");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    const int64_t threads = m * 32;
+    k_scatter_rows<<<(unsigned)((threads + 255) / 256), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const uint32_t*>(src), rows, m, row_bytes / 4, reinterpret_cast<uint32_t*>(out));
+    TB_LAUNCH_CHECK(ctx, "k_scatter_rows");
     return TB_OK;
 }
 

@@ -7,12 +7,17 @@ The reference runs on one device and only chunks output rows within it
   planes, so every voxel belongs to exactly one rank). Rank r owns z in [z_lo, z_hi) and needs
   the planes z_lo-1 and z_hi of its neighbours as a halo: a 3x3x3 submanifold conv at an owned
   voxel reads only voxels within one plane.
-* The local row order is [owned rows in global order] + [halo plane z_lo-1] + [halo plane
-  z_hi], so a local neighbor map built over those rows gives every owned row exactly its
-  global neighbors (tests check this against the single-rank oracle).
+* The local rows are the owned rows and the two halo planes in ascending global order, so a
+  local neighbor map built over them gives every owned row exactly its global neighbors (tests
+  check this against the single-rank oracle), and a row's neighbors stay as close in the local
+  order as they are in the global one. (Halo rows appended after the owned rows put the
+  neighbors of every slab-boundary voxel at the far end of the array; the conv kernel streams
+  each tile's neighbor rows as contiguous ranges, and those stretched ranges made a rank's conv
+  up to 1.5x slower at 8 ranks.)
 * :func:`exchange_halo` sends the boundary planes to the neighbouring ranks with point-to-point
-  send/recv (NCCL over NVLink on GPUs, gloo in the CPU tests) and receives the halo planes
-  straight into their rows. Nothing else is communicated: no all-reduce, no all-gather.
+  send/recv (NCCL over NVLink on GPUs, gloo in the CPU tests) into contiguous buffers and
+  scatters them to the halo rows' local positions. Nothing else is communicated: no all-reduce,
+  no all-gather.
 * :class:`SlabRunner` is the benchmark step on one rank: halo exchange of the input rows
   overlapped with the local neighbor map, conv(SiLU), halo exchange of the intermediate rows, conv.
 """
@@ -32,10 +37,14 @@ class SlabPlan:
     z_lo: int                  # owned planes: z_lo <= z < z_hi
     z_hi: int
     owned: np.ndarray          # global row ids of owned voxels (ascending)
-    halo_lo: np.ndarray        # global row ids of plane z_lo-1 (owned by rank-1)
-    halo_hi: np.ndarray        # global row ids of plane z_hi (owned by rank+1)
-    send_lo: np.ndarray        # local row ids of plane z_lo (sent to rank-1)
-    send_hi: np.ndarray        # local row ids of plane z_hi-1 (sent to rank+1)
+    halo_lo: np.ndarray        # global row ids of plane z_lo-1 (owned by rank-1), ascending
+    halo_hi: np.ndarray        # global row ids of plane z_hi (owned by rank+1), ascending
+    local: np.ndarray          # global row ids of the local rows: owned + halo, ascending
+    own_local: np.ndarray      # local positions of the owned rows
+    send_lo: np.ndarray        # local positions of plane z_lo (sent to rank-1), ascending
+    send_hi: np.ndarray        # local positions of plane z_hi-1 (sent to rank+1), ascending
+    recv_lo: np.ndarray        # local positions of plane z_lo-1 (received from rank-1)
+    recv_hi: np.ndarray        # local positions of plane z_hi (received from rank+1)
 
     @property
     def n_owned(self) -> int:
@@ -43,11 +52,11 @@ class SlabPlan:
 
     @property
     def n_local(self) -> int:
-        return int(self.owned.size + self.halo_lo.size + self.halo_hi.size)
+        return int(self.local.size)
 
     def local_rows(self) -> np.ndarray:
-        """Global row id of every local row (owned, then halo_lo, then halo_hi)."""
-        return np.concatenate([self.owned, self.halo_lo, self.halo_hi])
+        """Global row id of every local row (ascending)."""
+        return self.local
 
 
 def slab_bounds(z: np.ndarray, world: int) -> np.ndarray:
@@ -82,93 +91,116 @@ def plan_slabs(coords: np.ndarray, world: int, rank: int) -> SlabPlan:
     owned = np.nonzero((z >= z_lo) & (z < z_hi))[0]
     halo_lo = np.nonzero(z == z_lo - 1)[0] if rank > 0 else np.zeros(0, np.int64)
     halo_hi = np.nonzero(z == z_hi)[0] if rank < world - 1 else np.zeros(0, np.int64)
-    zo = z[owned]
-    send_lo = np.nonzero(zo == z_lo)[0] if rank > 0 else np.zeros(0, np.int64)
-    send_hi = np.nonzero(zo == z_hi - 1)[0] if rank < world - 1 else np.zeros(0, np.int64)
-    return SlabPlan(rank, world, z_lo, z_hi, owned, halo_lo, halo_hi, send_lo, send_hi)
+    local = np.sort(np.concatenate([owned, halo_lo, halo_hi]))
+    zl = z[local]
+    # a sender packs its boundary plane in ascending global order, which is the order of the
+    # receiver's halo positions for the same plane
+    none = np.zeros(0, np.int64)
+    send_lo = np.nonzero(zl == z_lo)[0] if rank > 0 else none
+    send_hi = np.nonzero(zl == z_hi - 1)[0] if rank < world - 1 else none
+    recv_lo = np.nonzero(zl == z_lo - 1)[0] if rank > 0 else none
+    recv_hi = np.nonzero(zl == z_hi)[0] if rank < world - 1 else none
+    own_local = np.nonzero((zl >= z_lo) & (zl < z_hi))[0]
+    return SlabPlan(rank, world, z_lo, z_hi, owned, halo_lo, halo_hi, local, own_local, send_lo, send_hi,
+                    recv_lo, recv_hi)
 
 
-def exchange_halo(plan: SlabPlan, x: torch.Tensor, gather, send_lo_idx=None, send_hi_idx=None,
-                  wait: bool = True):
+def exchange_halo(plan: SlabPlan, x: torch.Tensor, gather, scatter, idx=None, wait: bool = True):
     """Fill the halo rows of the local tensor ``x`` ([n_local, C]) from the neighbouring ranks.
 
-    ``gather(x, idx)`` packs rows ``idx`` of ``x`` into a contiguous tensor (index_select on
-    CPU, the library's tb_gather_rows on GPU). Halo rows are received in place. With
-    ``wait=False`` the transfers are only started and a handle is returned; pass it to
-    :func:`finish_halo` before reading the halo rows (work enqueued in between overlaps them)."""
-    n_own, h_lo, h_hi = plan.n_owned, plan.halo_lo.size, plan.halo_hi.size
+    ``gather(x, idx)`` packs rows ``idx`` of ``x`` into a contiguous tensor and
+    ``scatter(x, idx, src)`` writes the rows of ``src`` to rows ``idx`` of ``x`` (index_select /
+    index_copy_ on CPU, the library's tb_gather_rows / tb_scatter_rows on GPU). ``idx`` holds
+    the plan's send_lo, send_hi, recv_lo, recv_hi positions on ``x``'s device (made here when
+    absent). With ``wait=False`` the transfers are only started and a handle is returned; pass it
+    to :func:`finish_halo` before reading the halo rows (work enqueued in between overlaps them)."""
+    if idx is None:
+        idx = [torch.from_numpy(a.astype(np.int32)).to(x.device)
+               for a in (plan.send_lo, plan.send_hi, plan.recv_lo, plan.recv_hi)]
+    s_lo, s_hi, r_lo, r_hi = idx
     ops = []
     bufs = []
+    recvs = []
     # a plane that is empty on one side is empty on the other (it is the same plane), so both
     # ranks skip the same transfers
     if plan.rank > 0 and plan.send_lo.size:
-        sidx = send_lo_idx if send_lo_idx is not None else torch.from_numpy(plan.send_lo).to(x.device)
-        sb = gather(x, sidx)
+        sb = gather(x, s_lo)
         bufs.append(sb)
         ops.append(dist.P2POp(dist.isend, sb, plan.rank - 1))
-    if plan.rank > 0 and h_lo:
-        ops.append(dist.P2POp(dist.irecv, x[n_own:n_own + h_lo], plan.rank - 1))
+    if plan.rank > 0 and plan.recv_lo.size:
+        rb = x.new_empty((plan.recv_lo.size,) + tuple(x.shape[1:]))
+        recvs.append((r_lo, rb))
+        ops.append(dist.P2POp(dist.irecv, rb, plan.rank - 1))
     if plan.rank < plan.world - 1 and plan.send_hi.size:
-        sidx = send_hi_idx if send_hi_idx is not None else torch.from_numpy(plan.send_hi).to(x.device)
-        sb = gather(x, sidx)
+        sb = gather(x, s_hi)
         bufs.append(sb)
         ops.append(dist.P2POp(dist.isend, sb, plan.rank + 1))
-    if plan.rank < plan.world - 1 and h_hi:
-        ops.append(dist.P2POp(dist.irecv, x[n_own + h_lo:n_own + h_lo + h_hi], plan.rank + 1))
+    if plan.rank < plan.world - 1 and plan.recv_hi.size:
+        rb = x.new_empty((plan.recv_hi.size,) + tuple(x.shape[1:]))
+        recvs.append((r_hi, rb))
+        ops.append(dist.P2POp(dist.irecv, rb, plan.rank + 1))
     works = dist.batch_isend_irecv(ops) if ops else []
+    handle = (works, bufs, recvs, x, scatter)
     if not wait:
-        return (works, bufs)
-    finish_halo((works, bufs))
+        return handle
+    finish_halo(handle)
     return x
 
 
 def finish_halo(handle) -> None:
-    """Wait for the transfers of an ``exchange_halo(..., wait=False)`` call."""
-    works, _bufs = handle          # the send buffers stay alive until the sends complete
+    """Wait for the transfers of an ``exchange_halo(..., wait=False)`` call and place the
+    received rows."""
+    works, _bufs, recvs, x, scatter = handle   # the send buffers stay alive until the sends complete
     for w in works:
         w.wait()
+    for pos, rb in recvs:
+        scatter(x, pos, rb)
 
 
 class SlabRunner:
     """The benchmark step on one rank of a NCCL group: map + conv(SiLU) + conv on a z-slab."""
 
-    launches_per_step = 0                 # set in __init__: map, two packs per exchange (2), 2 convs
+    launches_per_step = 0                 # set in __init__: map, packs and unpacks of 2 exchanges, 2 convs
 
     def __init__(self, coords_np: np.ndarray, ci: int, device, generator):
         from . import ops
         self.ops = ops
-        self.launches_per_step = ops.NBR_MAP_LAUNCHES + 2 * 2 + 2
         self.rank = dist.get_rank()
         self.world = dist.get_world_size()
         self.plan = plan_slabs(coords_np, self.world, self.rank)
+        moves = sum(int(a.size > 0) for a in (self.plan.send_lo, self.plan.send_hi, self.plan.recv_lo,
+                                              self.plan.recv_hi))
+        self.launches_per_step = ops.NBR_MAP_LAUNCHES + 2 * moves + 2
         rows = self.plan.local_rows()
         self.device = device
         self.coords = torch.from_numpy(np.ascontiguousarray(coords_np[rows])).to(device)
         self.n_local = self.plan.n_local
         self.n_owned = self.plan.n_owned
         self.ci = ci
-        # features of the owned rows are resident; halo rows arrive by exchange each step
-        self.feats = torch.zeros((self.n_local, ci), dtype=torch.bfloat16, device=device)
-        self.feats[: self.n_owned] = torch.randn((self.n_owned, ci), device=device,
-                                                 generator=generator).bfloat16()
+        # features of the owned rows are resident; halo rows are overwritten by the exchange each step
+        self.feats = torch.randn((self.n_local, ci), device=device, generator=generator).bfloat16()
         self.nbr = torch.empty(27 * self.n_local, dtype=torch.int32, device=device)
         self.h = torch.zeros((self.n_local, ci), dtype=torch.bfloat16, device=device)
         self.out = torch.empty((self.n_local, ci), dtype=torch.bfloat16, device=device)
-        self.send_lo = torch.from_numpy(self.plan.send_lo.astype(np.int32)).to(device)
-        self.send_hi = torch.from_numpy(self.plan.send_hi.astype(np.int32)).to(device)
+        self.idx = [torch.from_numpy(a.astype(np.int32)).to(device)
+                    for a in (self.plan.send_lo, self.plan.send_hi, self.plan.recv_lo, self.plan.recv_hi)]
+        self.own_local = torch.from_numpy(self.plan.own_local).to(device)
         self.graph = None
 
     def _gather(self, x, idx):
         return self.ops.gather_rows(x, idx)
 
+    def _scatter(self, x, idx, src):
+        return self.ops.scatter_rows(x, idx, src)
+
     def step(self, w1, w2):
         ops = self.ops
         # the feature halo does not depend on the map: its transfer overlaps the map build
-        pending = exchange_halo(self.plan, self.feats, self._gather, self.send_lo, self.send_hi, wait=False)
+        pending = exchange_halo(self.plan, self.feats, self._gather, self._scatter, self.idx, wait=False)
         ops.build_neighbor_table(self.coords, out=self.nbr)
         finish_halo(pending)
         ops.sparse_submconv(self.feats, self.nbr, w1, None, epi="silu", out=self.h)
-        exchange_halo(self.plan, self.h, self._gather, self.send_lo, self.send_hi)
+        exchange_halo(self.plan, self.h, self._gather, self._scatter, self.idx)
         ops.sparse_submconv(self.h, self.nbr, w2, None, out=self.out)
 
     def capture(self, w1, w2, warmup: int = 3) -> None:
@@ -199,7 +231,7 @@ class SlabRunner:
 
     def count_valid_pairs(self) -> int:
         """Present (voxel, tap) pairs over the owned rows (the algorithmic work of one conv)."""
-        nb = self.nbr.view(27, self.n_local)[:, : self.n_owned]
+        nb = self.nbr.view(27, self.n_local)[:, self.own_local]
         return int((nb != self.n_local).sum().item())
 
     def close(self):

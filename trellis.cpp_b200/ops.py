@@ -294,6 +294,16 @@ def gather_rows(src: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def scatter_rows(dst: torch.Tensor, rows: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """dst[rows[k]] = src[k] (rows int32)."""
+    _need_cuda(dst, rows, src)
+    m = rows.numel()
+    row_bytes = dst[0].numel() * dst.element_size() if dst.shape[0] else 4
+    ctx = context(dst.device)
+    check(_lib.load().tb_scatter_rows(ctx, _ptr(src), _ptr(rows), m, row_bytes, _ptr(dst)), "tb_scatter_rows", ctx)
+    return dst
+
+
 def zslab_counts(coords: torch.Tensor, z_min: int, nz: int) -> torch.Tensor:
     _need_cuda(coords)
     counts = torch.empty(nz, dtype=torch.int64, device=coords.device)
