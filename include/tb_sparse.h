@@ -261,6 +261,36 @@ tb_status tb_gather_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int6
 tb_status tb_scatter_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t m,
                           int64_t row_bytes, void* out);
 
+/* ---- model and input files, read without ggml --------------------------------------------
+ * GGUF checkpoints as the reference's tools/convert.py writes them and src/trellis_model.cpp:96-137
+ * loads them (conv / linear weights F16, 1-D parameters F32, names kept verbatim; a sparse conv
+ * weight has ne = (Ci, 27, Co), the bytes of the [Co][27][Ci] layout tb_submconv takes), and the
+ * hr_slat.bin decode input of src/decode_replay.cpp:19-28. Host-only calls report failures
+ * through tb_io_last_error() (per thread); tb_gguf_upload_tensor reports on its context.
+ *   tb_gguf_open / tb_gguf_close: parse the header, metadata and tensor infos (GGUF v2/v3).
+ *   tb_gguf_find_tensor: index of a tensor by name, or -1.
+ *   tb_gguf_tensor_info: name, ggml type (0 F32, 1 F16, 30 BF16, others listed but not read),
+ *     n_dims, ne[4] (innermost first, unused dims 1) and byte size (0 for unreadable types).
+ *   tb_gguf_get_string: a string metadata value (e.g. "general.architecture",
+ *     "trellis.config_json"), or NULL.
+ *   tb_gguf_read_tensor: the raw bytes into a host buffer of exactly `nbytes`.
+ *   tb_gguf_upload_tensor: into device memory as `dtype` (F32/F16/BF16 converted on the device,
+ *     rounding to nearest even). Synchronises.
+ *   tb_slat_read: N and res, then (when the pointers are non-NULL) coords int32 [N][3] and
+ *     feats float32 [N][32]; call once with NULL buffers to learn N. */
+typedef struct tb_gguf tb_gguf;
+tb_status tb_gguf_open(const char* path, tb_gguf** out);
+void tb_gguf_close(tb_gguf* g);
+int64_t tb_gguf_n_tensors(const tb_gguf* g);
+int64_t tb_gguf_find_tensor(const tb_gguf* g, const char* name);
+tb_status tb_gguf_tensor_info(const tb_gguf* g, int64_t i, const char** name, int32_t* ggml_type,
+                              int32_t* n_dims, int64_t* ne, uint64_t* nbytes);
+const char* tb_gguf_get_string(const tb_gguf* g, const char* key);
+tb_status tb_gguf_read_tensor(const tb_gguf* g, int64_t i, void* dst, uint64_t nbytes);
+tb_status tb_gguf_upload_tensor(tb_ctx* ctx, const tb_gguf* g, int64_t i, tb_dtype dtype, void* dst);
+tb_status tb_slat_read(const char* path, int64_t* n, int32_t* res, int32_t* coords, float* feats);
+const char* tb_io_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif

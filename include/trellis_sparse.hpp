@@ -9,6 +9,10 @@
 //   sparse_convnext        include/sparse.h:23-25 (src/sparse.cpp:94-137), on host vectors,
 //                          with the block's device weights (ConvNeXtWeights)
 //   subdivide              the octant loop of sparse_c2s (src/sparse.cpp:205-222)
+//   GgufModel              the Model of src/trellis_model.cpp:96-137: a GGUF checkpoint's
+//                          tensors on the device, looked up by the reference's names; its
+//                          conv(), convnext() and c2s() give the weights of a block prefix
+//   read_slat              the hr_slat.bin decode input of src/decode_replay.cpp:19-28
 //   sparse_c2s             include/sparse.h:27-35 (src/sparse.cpp:172-336), the whole
 //                          SparseResBlockC2S3d; the block's device weights (C2SWeights) take
 //                          the place of Model + prefix
@@ -19,6 +23,8 @@
 
 #include <array>
 #include <cstdint>
+#include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "tb_sparse.h"
@@ -95,5 +101,51 @@ struct C2SWeights {
 C2SResult sparse_c2s(const C2SWeights& w, const std::vector<float>& feats_in, int Cin,
                      const std::vector<std::array<int, 3>>& coords, int Cout,
                      const std::vector<uint8_t>* ext_subdiv = nullptr);
+
+// A GGUF checkpoint (tools/convert.py's output) on device `device`. Every F32/F16/BF16 tensor is
+// uploaded: tensors of two or more dims (conv and linear weights) as `weight_dtype`, 1-D tensors
+// and the C2S `to_subdiv.weight` as float32, the types the kernels take. Move-only; frees its
+// device memory when destroyed.
+class GgufModel {
+public:
+    static GgufModel load(const std::string& path, int device = 0, tb_dtype weight_dtype = TB_BF16);
+    GgufModel() = default;
+    GgufModel(GgufModel&& o) noexcept;
+    GgufModel& operator=(GgufModel&& o) noexcept;
+    GgufModel(const GgufModel&) = delete;
+    GgufModel& operator=(const GgufModel&) = delete;
+    ~GgufModel();
+
+    bool has(const std::string& name) const { return t_.count(name) != 0; }
+    const void* get(const std::string& name) const;                 // throws if absent
+    std::vector<int64_t> shape(const std::string& name) const;      // torch order
+    // prefix.weight [Co,27,Ci] + prefix.bias (src/sparse.cpp:87-92)
+    ConvWeights conv(const std::string& prefix) const;
+    // prefix.conv, prefix.norm, prefix.mlp.0, prefix.mlp.2 (src/sparse.cpp:104-133)
+    ConvNeXtWeights convnext(const std::string& prefix) const;
+    // prefix.to_subdiv (absent in the texture decoder), norm1, conv1, conv2 (src/sparse.cpp:186-316)
+    C2SWeights c2s(const std::string& prefix) const;
+
+    std::string arch;           // general.architecture
+    std::string config_json;    // trellis.config_json
+    tb_dtype weight_dtype = TB_BF16;
+
+private:
+    struct Tensor {
+        void* dev = nullptr;
+        tb_dtype dtype = TB_F32;
+        std::vector<int64_t> shape;
+    };
+    std::unordered_map<std::string, Tensor> t_;
+    int device_ = 0;
+};
+
+// The hr_slat.bin dump (src/decode_replay.cpp:19-28): coords, feats [N][32] and the resolution.
+struct SlatInput {
+    std::vector<std::array<int, 3>> coords;
+    std::vector<float> feats;
+    int res = 0;
+};
+SlatInput read_slat(const std::string& path);
 
 }  // namespace trellis

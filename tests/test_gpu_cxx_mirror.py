@@ -1,7 +1,9 @@
 """The C++ host mirror (include/trellis_sparse.hpp: the reference's include/sparse.h names) on the
 GPU: a small C++ program built against the header and libtb_sparse.so runs
 build_neighbor_table, sparse_submconv, sparse_convnext and sparse_c2s on the golden inputs of
-the reference's torch restatements (fp32 mode); the outputs are compared here (maps and child
+the reference's torch restatements (fp32 mode), once with weights it uploads itself and once
+with weights loaded by GgufModel from GGUF files written by gguf-py (the reference's converter's
+writer), and reads an hr_slat.bin dump; the outputs are compared here (maps and child
 coordinates exactly, features at max|d|/max|ref| < 1e-4)."""
 import os
 import shutil
@@ -96,6 +98,26 @@ int main(int argc, char** argv) {
         wr("c2s_mask.out", r.subdiv.data(), r.subdiv.size());
         auto r2 = trellis::sparse_c2s(w, feats2, cin, coords2, cout, nullptr);   // mask from to_subdiv
         wr("c2s_mask2.out", r2.subdiv.data(), r2.subdiv.size());
+        // ---- the same blocks with weights from GGUF checkpoints, looked up by prefix
+        {
+            auto m = trellis::GgufModel::load(g_dir + "/model.gguf", 0, TB_F32);
+            if (m.arch != "trellis2-shape-dec" || m.config_json.empty()) return 5;
+            auto blk2 = trellis::sparse_convnext(m.convnext("blk"), feats, nbr, n);
+            wr("block_gguf.out", blk2.data(), blk2.size());
+            auto r3 = trellis::sparse_c2s(m.c2s("up"), feats2, cin, coords2, cout, &mask);
+            wr("c2s_gguf.out", r3.feats.data(), r3.feats.size());
+            bool threw2 = false;
+            try {
+                m.conv("no.such.block");
+            } catch (const std::runtime_error&) {
+                threw2 = true;
+            }
+            if (!threw2) return 6;
+        }
+        auto slat = trellis::read_slat(g_dir + "/hr_slat.bin");
+        wr("slat_coords.out", reinterpret_cast<const int*>(slat.coords.data()), slat.coords.size() * 3);
+        wr("slat_feats.out", slat.feats.data(), slat.feats.size());
+        if (slat.res != 512) return 7;
         // errors throw like the reference
         bool threw = false;
         try {
@@ -140,6 +162,30 @@ def test_cxx_mirror_on_golden_cases(tb, golden, tmp_path):
     }
     for name, a in files.items():
         np.ascontiguousarray(a).tofile(tmp_path / name)
+    # a GGUF checkpoint holding both blocks under the reference's tensor names (fp32 throughout,
+    # as tools/convert.py writes with FORCE_F32=1)
+    gguf = pytest.importorskip("gguf")
+    gw = gguf.GGUFWriter(str(tmp_path / "model.gguf"), "trellis2-shape-dec")
+    gw.add_string("trellis.config_json", "{}")
+    c2 = lambda a: np.ascontiguousarray(a.reshape(a.shape[0], 27, -1), dtype=np.float32)  # noqa: E731
+    for name, a in (("blk.conv.weight", c2(g["weight"])), ("blk.conv.bias", g["bias"]),
+                    ("blk.norm.weight", g["norm.weight"]), ("blk.norm.bias", g["norm.bias"]),
+                    ("blk.mlp.0.weight", g["mlp.0.weight"]), ("blk.mlp.0.bias", g["mlp.0.bias"]),
+                    ("blk.mlp.2.weight", g["mlp.2.weight"]), ("blk.mlp.2.bias", g["mlp.2.bias"]),
+                    ("up.to_subdiv.weight", g2["to_subdiv.weight"]), ("up.to_subdiv.bias", g2["to_subdiv.bias"]),
+                    ("up.norm1.weight", g2["norm1.weight"]), ("up.norm1.bias", g2["norm1.bias"]),
+                    ("up.conv1.weight", c2(g2["conv1.weight"])), ("up.conv1.bias", g2["conv1.bias"]),
+                    ("up.conv2.weight", c2(g2["conv2.weight"])), ("up.conv2.bias", g2["conv2.bias"])):
+        gw.add_tensor(name, np.ascontiguousarray(a, dtype=np.float32))
+    gw.write_header_to_file()
+    gw.write_kv_data_to_file()
+    gw.write_tensors_to_file()
+    gw.close()
+    rng = np.random.default_rng(5)
+    slat_c = rng.integers(0, 512, (300, 3)).astype(np.int32)
+    slat_f = rng.standard_normal((300, 32)).astype(np.float32)
+    with open(tmp_path / "hr_slat.bin", "wb") as fh:
+        fh.write(np.array([300, 512], dtype=np.int32).tobytes() + slat_c.tobytes() + slat_f.tobytes())
     src = tmp_path / "mirror.cpp"
     src.write_text(PROGRAM)
     exe = tmp_path / "mirror"
@@ -163,6 +209,11 @@ def test_cxx_mirror_on_golden_cases(tb, golden, tmp_path):
     out = np.fromfile(tmp_path / "c2s_feats.out", dtype=np.float32).reshape(-1, cout)
     assert max_rel(out, g2["out"]) < 1e-4
     assert np.array_equal(np.fromfile(tmp_path / "c2s_mask.out", dtype=np.uint8).reshape(n2, 8), g2["mask"])
+    assert max_rel(np.fromfile(tmp_path / "block_gguf.out", dtype=np.float32).reshape(n, c), g["block_out"]) < 1e-4
+    out_g = np.fromfile(tmp_path / "c2s_gguf.out", dtype=np.float32).reshape(-1, cout)
+    assert max_rel(out_g, g2["out"]) < 1e-4
+    assert np.array_equal(np.fromfile(tmp_path / "slat_coords.out", dtype=np.int32).reshape(-1, 3), slat_c)
+    assert np.array_equal(np.fromfile(tmp_path / "slat_feats.out", dtype=np.float32).reshape(-1, 32), slat_f)
     sure = np.abs(g2["subdiv"]) > 1e-5
     mask2 = np.fromfile(tmp_path / "c2s_mask2.out", dtype=np.uint8).reshape(n2, 8)
     assert np.array_equal(mask2[sure], g2["mask"][sure])

@@ -1,0 +1,110 @@
+"""GGUF checkpoints and the hr_slat.bin dump, read through the C ABI without a GPU.
+
+The GGUF files are written by gguf-py's GGUFWriter, the writer the reference's tools/convert.py
+uses (conv weights [Co,27,Ci] as F16, 1-D parameters as F32, the config JSON as
+`trellis.config_json`); the reader must return the same names, shapes, types, strings and
+bytes. The slat file follows src/decode_replay.cpp:19-28."""
+import json
+
+import numpy as np
+import pytest
+
+gguf = pytest.importorskip("gguf")
+
+
+def _write_model(path, alignment=None, extra=True):
+    rng = np.random.default_rng(0)
+    t = {
+        "blocks.0.conv.weight": rng.standard_normal((16, 27, 8)).astype(np.float16),   # [Co,27,Ci]
+        "blocks.0.conv.bias": rng.standard_normal(16).astype(np.float32),
+        "blocks.0.mlp.0.weight": rng.standard_normal((64, 16)).astype(np.float16),
+        "blocks.0.norm.weight": rng.standard_normal(16).astype(np.float32),
+        "up.to_subdiv.weight": rng.standard_normal((8, 16)).astype(np.float32),
+    }
+    w = gguf.GGUFWriter(str(path), "trellis2-shape-dec")
+    if alignment:
+        w.add_custom_alignment(alignment)
+    w.add_string("trellis.config_json", json.dumps({"channels": [16, 8]}))
+    w.add_string("general.name", "shape_dec")
+    if extra:
+        w.add_array("test.int_array", [1, 2, 3])
+        w.add_array("test.str_array", ["a", "bc"])
+        w.add_uint32("test.u32", 7)
+        w.add_float32("test.f32", 0.5)
+        w.add_bool("test.bool", True)
+    for name, a in t.items():
+        w.add_tensor(name, a)
+    bf = (rng.standard_normal((4, 6)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    w.add_tensor("raw.bf16", bf, raw_dtype=gguf.GGMLQuantizationType.BF16)
+    t["raw.bf16"] = bf
+    q = np.zeros((2, 34), dtype=np.uint8)      # two Q8_0 blocks of 32 values: listed, not readable
+    w.add_tensor("raw.q8", q, raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return t
+
+
+@pytest.mark.parametrize("alignment", [None, 64])
+def test_gguf_round_trip(tb, tmp_path, alignment):
+    from trellis_cpp_b200 import ops
+    path = tmp_path / "m.gguf"
+    t = _write_model(path, alignment)
+    f = ops.GgufFile(path)
+    assert f.string("general.architecture") == "trellis2-shape-dec"
+    assert json.loads(f.string("trellis.config_json")) == {"channels": [16, 8]}
+    assert f.string("no.such.key") is None
+    assert set(f.tensors) == set(t) | {"raw.q8"}
+    for name, a in t.items():
+        _, typ, shape, nbytes = f.tensors[name]
+        assert shape == a.shape, name
+        assert typ == {np.float16: ops.GGUF_F16, np.float32: ops.GGUF_F32, np.uint16: ops.GGUF_BF16}[a.dtype.type]
+        assert nbytes == a.nbytes
+        got = f.numpy(name)
+        assert got.dtype == a.dtype and np.array_equal(got, a), name
+    # the conv weight's bytes are the [Co][27][Ci] layout the conv kernels take
+    assert f.numpy("blocks.0.conv.weight").shape == (16, 27, 8)
+    _, typ, shape, nbytes = f.tensors["raw.q8"]
+    assert typ == 8 and nbytes == 0
+    with pytest.raises(ops.TBError):
+        f.numpy("raw.q8")
+    f.close()
+
+
+def test_gguf_rejects_bad_files(tb, tmp_path):
+    from trellis_cpp_b200 import ops
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"NOTAGGUF" + bytes(64))
+    with pytest.raises(ops.TBError) as e:
+        ops.GgufFile(bad)
+    assert "not a GGUF" in str(e.value)
+    good = tmp_path / "m.gguf"
+    _write_model(good, extra=False)
+    data = good.read_bytes()
+    for cut in (6, 40, len(data) - 160):     # the last cut truncates readable tensor data
+        part = tmp_path / f"cut{cut}.gguf"
+        part.write_bytes(data[:cut])
+        with pytest.raises(ops.TBError):
+            ops.GgufFile(part)
+    with pytest.raises(ops.TBError):
+        ops.GgufFile(tmp_path / "missing.gguf")
+
+
+def test_slat_dump(tb, tmp_path):
+    from trellis_cpp_b200 import ops
+    rng = np.random.default_rng(2)
+    n, res = 500, 64
+    coords = rng.integers(0, res, (n, 3)).astype(np.int32)
+    feats = rng.standard_normal((n, 32)).astype(np.float32)
+    p = tmp_path / "hr_slat.bin"
+    with open(p, "wb") as f:
+        f.write(np.array([n, res], dtype=np.int32).tobytes())
+        f.write(coords.tobytes())
+        f.write(feats.tobytes())
+    c, x, r = ops.read_slat(p)
+    assert r == res and np.array_equal(c, coords) and np.array_equal(x, feats)
+    p.write_bytes(p.read_bytes()[:-4])
+    with pytest.raises(ops.TBError) as e:
+        ops.read_slat(p)
+    assert "size does not match" in str(e.value)

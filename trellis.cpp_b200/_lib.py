@@ -62,6 +62,17 @@ SIGNATURES = {
     "tb_convnext_tail": (_st, [_vp, _i64, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
     "tb_sparse_convnext": (_st, [_vp, _vp, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int,
                                  _vp]),
+    "tb_gguf_open": (_st, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "tb_gguf_close": (None, [_vp]),
+    "tb_gguf_n_tensors": (_i64, [_vp]),
+    "tb_gguf_find_tensor": (_i64, [_vp, ctypes.c_char_p]),
+    "tb_gguf_tensor_info": (_st, [_vp, _i64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_i32),
+                                  ctypes.POINTER(_i32), ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_uint64)]),
+    "tb_gguf_get_string": (ctypes.c_char_p, [_vp, ctypes.c_char_p]),
+    "tb_gguf_read_tensor": (_st, [_vp, _i64, _vp, ctypes.c_uint64]),
+    "tb_gguf_upload_tensor": (_st, [_vp, _vp, _i64, _int, _vp]),
+    "tb_slat_read": (_st, [ctypes.c_char_p, ctypes.POINTER(_i64), ctypes.POINTER(_i32), _vp, _vp]),
+    "tb_io_last_error": (ctypes.c_char_p, []),
     "tb_sparse_c2s": (_st, [_vp, _vp, _i64, _int, _vp, _int, _int, ctypes.POINTER(C2SParams), _vp, _int, _int,
                             _i64, _vp, _vp, _vp, ctypes.POINTER(_i64)]),
 }

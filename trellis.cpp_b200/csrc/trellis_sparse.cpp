@@ -223,4 +223,137 @@ C2SResult sparse_c2s(const C2SWeights& w, const std::vector<float>& feats_in, in
     return r;
 }
 
+// ---- GGUF checkpoints and the slat dump ---------------------------------------------------------
+GgufModel GgufModel::load(const std::string& path, int device, tb_dtype weight_dtype) {
+    tb_gguf* g = nullptr;
+    if (tb_gguf_open(path.c_str(), &g) != TB_OK) throw std::runtime_error(std::string("trellis: ") + tb_io_last_error());
+    struct Closer {
+        tb_gguf* g;
+        ~Closer() { tb_gguf_close(g); }
+    } closer{g};
+    set_device(device);
+    cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+    GgufModel m;
+    m.device_ = device;
+    m.weight_dtype = weight_dtype;
+    if (const char* a = tb_gguf_get_string(g, "general.architecture")) m.arch = a;
+    if (const char* c = tb_gguf_get_string(g, "trellis.config_json")) m.config_json = c;
+    const int64_t n = tb_gguf_n_tensors(g);
+    for (int64_t i = 0; i < n; ++i) {
+        const char* name = nullptr;
+        int32_t type = 0, nd = 0;
+        int64_t ne[4];
+        uint64_t nbytes = 0;
+        ok(tb_gguf_tensor_info(g, i, &name, &type, &nd, ne, &nbytes), "tb_gguf_tensor_info");
+        if (!nbytes) continue;                      // quantised types are not used on this path
+        const std::string nm = name;
+        static const std::string kSubdiv = ".to_subdiv.weight";    // read by tb_sparse_c2s as float32
+        const bool subdiv = nm.size() >= kSubdiv.size() &&
+                            nm.compare(nm.size() - kSubdiv.size(), kSubdiv.size(), kSubdiv) == 0;
+        Tensor t;
+        t.dtype = nd >= 2 && !subdiv ? weight_dtype : TB_F32;
+        int64_t elems = 1;
+        for (int d = nd - 1; d >= 0; --d) {
+            t.shape.push_back(ne[d]);
+            elems *= ne[d];
+        }
+        cuda_ok(cudaMalloc(&t.dev, (size_t)elems * (t.dtype == TB_F32 ? 4 : 2) + 16), "cudaMalloc");
+        m.t_[nm] = t;   // owned by m from here on (freed by its destructor on an error below)
+        ok(tb_gguf_upload_tensor(ctx(), g, i, t.dtype, t.dev), "tb_gguf_upload_tensor");
+    }
+    return m;
+}
+
+GgufModel::GgufModel(GgufModel&& o) noexcept
+    : arch(std::move(o.arch)), config_json(std::move(o.config_json)), weight_dtype(o.weight_dtype),
+      t_(std::move(o.t_)), device_(o.device_) {
+    o.t_.clear();
+}
+
+GgufModel& GgufModel::operator=(GgufModel&& o) noexcept {
+    if (this != &o) {
+        for (auto& kv : t_) cudaFree(kv.second.dev);
+        t_ = std::move(o.t_);
+        o.t_.clear();
+        arch = std::move(o.arch);
+        config_json = std::move(o.config_json);
+        weight_dtype = o.weight_dtype;
+        device_ = o.device_;
+    }
+    return *this;
+}
+
+GgufModel::~GgufModel() {
+    if (t_.empty()) return;
+    cudaSetDevice(device_);
+    for (auto& kv : t_) cudaFree(kv.second.dev);
+}
+
+const void* GgufModel::get(const std::string& name) const {
+    auto it = t_.find(name);
+    if (it == t_.end()) throw std::runtime_error("trellis: missing tensor " + name);
+    return it->second.dev;
+}
+
+std::vector<int64_t> GgufModel::shape(const std::string& name) const {
+    auto it = t_.find(name);
+    if (it == t_.end()) throw std::runtime_error("trellis: missing tensor " + name);
+    return it->second.shape;
+}
+
+ConvWeights GgufModel::conv(const std::string& prefix) const {
+    const auto s = shape(prefix + ".weight");
+    if (s.size() != 3 || s[1] != 27) throw std::runtime_error("trellis: " + prefix + ".weight is not [Co,27,Ci]");
+    ConvWeights w;
+    w.weight = get(prefix + ".weight");
+    w.bias = has(prefix + ".bias") ? static_cast<const float*>(get(prefix + ".bias")) : nullptr;
+    w.co = (int)s[0];
+    w.ci = (int)s[2];
+    w.dtype = weight_dtype;
+    return w;
+}
+
+ConvNeXtWeights GgufModel::convnext(const std::string& prefix) const {
+    ConvNeXtWeights w;
+    w.conv = conv(prefix + ".conv");
+    w.norm_w = static_cast<const float*>(get(prefix + ".norm.weight"));
+    w.norm_b = static_cast<const float*>(get(prefix + ".norm.bias"));
+    w.mlp0_w = get(prefix + ".mlp.0.weight");
+    w.mlp0_b = static_cast<const float*>(get(prefix + ".mlp.0.bias"));
+    w.mlp2_w = get(prefix + ".mlp.2.weight");
+    w.mlp2_b = static_cast<const float*>(get(prefix + ".mlp.2.bias"));
+    return w;
+}
+
+C2SWeights GgufModel::c2s(const std::string& prefix) const {
+    C2SWeights w;
+    w.dtype = weight_dtype;
+    if (has(prefix + ".to_subdiv.weight")) {
+        w.p.to_subdiv_w = static_cast<const float*>(get(prefix + ".to_subdiv.weight"));
+        w.p.to_subdiv_b = has(prefix + ".to_subdiv.bias") ? static_cast<const float*>(get(prefix + ".to_subdiv.bias"))
+                                                          : nullptr;
+    }
+    w.p.norm1_w = static_cast<const float*>(get(prefix + ".norm1.weight"));
+    w.p.norm1_b = static_cast<const float*>(get(prefix + ".norm1.bias"));
+    w.p.conv1_w = get(prefix + ".conv1.weight");
+    w.p.conv1_b = has(prefix + ".conv1.bias") ? static_cast<const float*>(get(prefix + ".conv1.bias")) : nullptr;
+    w.p.conv2_w = get(prefix + ".conv2.weight");
+    w.p.conv2_b = has(prefix + ".conv2.bias") ? static_cast<const float*>(get(prefix + ".conv2.bias")) : nullptr;
+    return w;
+}
+
+SlatInput read_slat(const std::string& path) {
+    int64_t n = 0;
+    int32_t res = 0;
+    if (tb_slat_read(path.c_str(), &n, &res, nullptr, nullptr) != TB_OK)
+        throw std::runtime_error(std::string("trellis: ") + tb_io_last_error());
+    SlatInput s;
+    s.res = res;
+    s.coords.resize((size_t)n);
+    s.feats.resize((size_t)n * 32);
+    if (tb_slat_read(path.c_str(), &n, &res, reinterpret_cast<int32_t*>(s.coords.data()), s.feats.data()) != TB_OK)
+        throw std::runtime_error(std::string("trellis: ") + tb_io_last_error());
+    return s;
+}
+
 }  // namespace trellis

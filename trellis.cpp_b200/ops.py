@@ -337,3 +337,82 @@ def submconv_stack_host(coords: np.ndarray, feats: np.ndarray, layers, dtype: to
         len(layers), _DT[dtype], _DT[out_dtype], out.ctypes.data_as(ctypes.c_void_p)),
         "tb_submconv_stack_host", ctx)
     return out
+
+
+# ---- model and input files ----------------------------------------------------------------
+_GGUF_NP = {0: np.float32, 1: np.float16, 30: np.uint16}   # BF16 read as its raw 16-bit words
+GGUF_F32, GGUF_F16, GGUF_BF16 = 0, 1, 30
+
+
+def _io_check(status: int, call: str):
+    if status != _lib.TB_OK:
+        d = _lib.load().tb_io_last_error()
+        raise TBError(status, call, d.decode() if d else "")
+
+
+class GgufFile:
+    """A GGUF checkpoint (the reference's Model file, src/trellis_model.cpp:96-137), parsed by
+    tb_gguf_open. Shapes are given in torch order (ggml's ne reversed): a sparse conv weight
+    is [Co, 27, Ci]."""
+
+    def __init__(self, path: str):
+        self._g = ctypes.c_void_p()
+        _io_check(_lib.load().tb_gguf_open(str(path).encode(), ctypes.byref(self._g)), "tb_gguf_open")
+        self.tensors = {}
+        lib = _lib.load()
+        for i in range(lib.tb_gguf_n_tensors(self._g)):
+            name = ctypes.c_char_p()
+            typ, nd = _lib._i32(), _lib._i32()
+            ne = (_lib._i64 * 4)()
+            nb = ctypes.c_uint64()
+            _io_check(lib.tb_gguf_tensor_info(self._g, i, ctypes.byref(name), ctypes.byref(typ), ctypes.byref(nd), ne,
+                                              ctypes.byref(nb)), "tb_gguf_tensor_info")
+            shape = tuple(int(ne[d]) for d in range(nd.value))[::-1]
+            self.tensors[name.value.decode()] = (i, int(typ.value), shape, int(nb.value))
+
+    def close(self):
+        if self._g:
+            _lib.load().tb_gguf_close(self._g)
+            self._g = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001  (interpreter shutdown)
+            pass
+
+    def string(self, key: str):
+        v = _lib.load().tb_gguf_get_string(self._g, key.encode())
+        return v.decode() if v is not None else None
+
+    def numpy(self, name: str) -> np.ndarray:
+        i, typ, shape, nb = self.tensors[name]
+        if typ not in _GGUF_NP:
+            raise TBError(2, "GgufFile.numpy", f"{name}: ggml type {typ} is not F32/F16/BF16")
+        out = np.empty(shape, dtype=_GGUF_NP[typ])
+        _io_check(_lib.load().tb_gguf_read_tensor(self._g, i, out.ctypes.data_as(ctypes.c_void_p), nb),
+                  "tb_gguf_read_tensor")
+        return out
+
+    def to_device(self, name: str, dtype: torch.dtype, device=None) -> torch.Tensor:
+        i, typ, shape, nb = self.tensors[name]
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        out = torch.empty(shape, dtype=dtype, device=dev)
+        ctx = context(dev)
+        check(_lib.load().tb_gguf_upload_tensor(ctx, self._g, i, _DT[dtype], _ptr(out)), "tb_gguf_upload_tensor", ctx)
+        return out
+
+
+def read_slat(path: str):
+    """The hr_slat.bin decode input (src/decode_replay.cpp:19-28): (coords int32 [N,3],
+    feats float32 [N,32], res)."""
+    lib = _lib.load()
+    n = ctypes.c_int64()
+    res = _lib._i32()
+    _io_check(lib.tb_slat_read(str(path).encode(), ctypes.byref(n), ctypes.byref(res), None, None), "tb_slat_read")
+    coords = np.empty((n.value, 3), dtype=np.int32)
+    feats = np.empty((n.value, 32), dtype=np.float32)
+    _io_check(lib.tb_slat_read(str(path).encode(), ctypes.byref(n), ctypes.byref(res),
+                               coords.ctypes.data_as(ctypes.c_void_p), feats.ctypes.data_as(ctypes.c_void_p)),
+              "tb_slat_read")
+    return coords, feats, int(res.value)
