@@ -135,7 +135,10 @@ tb_status tb_submconv_range(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t 
  *   dtype TB_BF16 / TB_F16: x, W1, W2 in that type, tcgen05 tensor cores with fp32
  *        accumulation; the normalised row and the SiLU activations are rounded to the operand
  *        type before their products (ggml rounds activations to the weight type likewise).
- *        Needs c in {64, 128, 256}.
+ *        c in {64, 128, 256}: one fused kernel, nothing but x, h and out leaves the SM. Other
+ *        c in {16, 32} or a multiple of 64 up to 2048 (the 512 and 1024 of decode_unet): the
+ *        same arithmetic as three passes (LayerNorm, mlp.0 + SiLU, mlp.2 + bias + residual; see
+ *        tb_layer_norm and tb_linear) with a [n][4c] activation buffer in context workspace.
  *   dtype TB_F32: fp32 throughout on CUDA cores (h and out fp32), any c <= 1024; one block per
  *        row, meant for the precision mode and small n.
  *   out_dtype: TB_F32 or the operand dtype. `out` must not alias h or x. */
@@ -186,6 +189,24 @@ tb_status tb_c2s_gather(tb_ctx* ctx, const void* src, const int32_t* gidx, int64
  * SiLU of src/sparse.cpp:127 as a standalone pass). bias may be NULL. */
 tb_status tb_bias_act(tb_ctx* ctx, void* x, int64_t n, int c, const float* bias,
                       tb_dtype dtype, tb_epilogue epi);
+
+/* ---- per-voxel dense layers ---------------------------------------------------------------
+ * tb_linear: out[i][j] = act(bias[j] + sum_k a[i][k] * w[j][k]) + res[i][j] for i < m, j < n:
+ * the ggml_mul_mat + ggml_add (+ ggml_silu) of decode_unet's from_latent / output_layer
+ * (src/shape_decoder.cpp:62-77,84-86,114) and of the ConvNeXt MLP (src/sparse.cpp:127-131).
+ * a [m][k] and w [n][k] (torch Linear weight) of dtype; bias float32 [n] or NULL; res [m][n]
+ * of res_dtype (TB_F32 or dtype) or NULL, may equal out; act TB_EPI_NONE or TB_EPI_SILU;
+ * out [m][n] of out_dtype (TB_F32 or dtype). 16-bit dtypes run on tcgen05 tensor cores (fp32
+ * accumulate) and need k a multiple of 64, or 16 or 32; TB_F32 runs on CUDA cores, any k.
+ * tb_layer_norm: out = act(LN(x) * w + b), LayerNorm over c channels (c % 8 == 0, <= 2048)
+ * with the given eps (1e-6 in the blocks, 1e-5 before decode_unet's output layer,
+ * src/shape_decoder.cpp:70); w, b float32 [c], both NULL for no affine. x of x_dtype, out of
+ * out_dtype (TB_F32 or x_dtype). */
+tb_status tb_linear(tb_ctx* ctx, int64_t m, int k, int n, const void* a, const void* w, const float* bias,
+                    const void* res, tb_dtype res_dtype, tb_epilogue act, tb_dtype dtype,
+                    tb_dtype out_dtype, void* out);
+tb_status tb_layer_norm(tb_ctx* ctx, const void* x, tb_dtype x_dtype, int64_t n, int c, const float* w,
+                        const float* b, float eps, tb_epilogue act, tb_dtype out_dtype, void* out);
 
 /* ---- SparseResBlockC2S3d ------------------------------------------------------------------
  * Parameters of one C2S up-block, device pointers named after the reference's tensors under

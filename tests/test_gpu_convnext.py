@@ -131,10 +131,23 @@ def test_block_bf16_matches_oracle(tb):
     assert max_rel(out.cpu().numpy(), _tail_ref(h, feats, nw, nb, w1, b1, w2, b2)) < 1e-2
 
 
+@pytest.mark.parametrize("c", [32, 512, 1024])
+def test_tail_wide_and_narrow_widths(tb, c):
+    # widths outside the fused kernel: LayerNorm, mlp.0 + SiLU and mlp.2 + residual as passes
+    rng = np.random.default_rng(c)
+    n = 700
+    h = (0.5 + 2.0 * rng.standard_normal((n, c))).astype(np.float32)
+    x = round_to(rng.standard_normal((n, c)).astype(np.float32), "bf16")
+    w1, w2, nw, nb, b1, b2 = _params(c, "bf16", c)
+    out = _run_tail(h, x, w1, w2, nw, nb, b1, b2, "bf16")
+    assert max_rel(out, _tail_ref(h, x, nw, nb, w1, b1, w2, b2, rnd="bf16")) < 3e-3
+    assert max_rel(out, _tail_ref(h, x, nw, nb, w1, b1, w2, b2)) < 1e-2
+
+
 def test_unsupported_width_reports_status(tb):
     from trellis_cpp_b200 import ops
     rng = np.random.default_rng(1)
-    n, c = 100, 96
+    n, c = 100, 80          # neither a fused width, 16, 32 nor a multiple of 64
     w1, w2, nw, nb, b1, b2 = _params(c, "bf16", 1)
     with pytest.raises(ops.TBError) as e:
         _run_tail(rng.standard_normal((n, c)).astype(np.float32), np.zeros((n, c), np.float32),

@@ -62,6 +62,8 @@ SIGNATURES = {
     "tb_convnext_tail": (_st, [_vp, _i64, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
     "tb_sparse_convnext": (_st, [_vp, _vp, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int,
                                  _vp]),
+    "tb_linear": (_st, [_vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _vp]),
+    "tb_layer_norm": (_st, [_vp, _vp, _int, _i64, _int, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
     "tb_gguf_open": (_st, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "tb_gguf_close": (None, [_vp]),
     "tb_gguf_n_tensors": (_i64, [_vp]),

@@ -99,6 +99,7 @@ tb_status tb_ctx_destroy(tb_ctx* ctx) {
     if (ctx->stage_ev_made)
         for (cudaEvent_t e : ctx->stage_ev) cudaEventDestroy(e);
     if (ctx->chunk_hi_host) cudaFreeHost(ctx->chunk_hi_host);
+    if (ctx->tail_ws) cudaFree(ctx->tail_ws);
     if (ctx->d_err) cudaFree(ctx->d_err);
     delete ctx;
     return TB_OK;
@@ -195,8 +196,9 @@ tb_status tb_sparse_convnext(tb_ctx* ctx, const int32_t* nbr, int64_t n, const v
     if (!ctx) return TB_ERR_INVALID_ARG;
     if (n < 0 || c <= 0) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_sparse_convnext: n < 0 or c <= 0");
     if (n == 0) return TB_OK;
-    if (dtype != TB_F32 && !tb_convnext_tc_supported(c))
-        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "tb_sparse_convnext: 16-bit operands need c in {64, 128, 256}");
+    if (dtype != TB_F32 && !tb_convnext_tc_supported(c) && !tb_convnext_two_pass_supported(c))
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED,
+                       "tb_sparse_convnext: 16-bit operands need c in {16, 32} or a multiple of 64 up to 2048");
     tb_status s = tb_ensure(ctx, &ctx->block_h, &ctx->block_h_bytes, (size_t)n * c * sizeof(float), "convnext conv output");
     if (s != TB_OK) return s;
     s = tb_submconv(ctx, nbr, n, feats, c, conv_w, conv_b, c, dtype, TB_F32, TB_EPI_NONE, ctx->block_h);

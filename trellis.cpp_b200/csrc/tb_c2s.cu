@@ -118,13 +118,13 @@ k_to_subdiv(const void* __restrict__ x, int64_t n, int cin, const float* __restr
     }
 }
 
-// Row LayerNorm (eps 1e-6) over c channels, optional affine, optional SiLU; one warp per output
+// Row LayerNorm (eps given: 1e-6 in the blocks, 1e-5 before decode_unet's output layer) over c channels, optional affine, optional SiLU; one warp per output
 // row. Output row r reads source row rows[r] (rows == nullptr: row r). Lane l owns the 8-channel
 // chunks l, l + 32, ... (NCH of them at most, c <= 256 NCH).
 template <int IK, int OK, int NCH>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 k_row_norm(const void* __restrict__ src, const int32_t* __restrict__ rows, int64_t n, int c,
-           const float* __restrict__ w, const float* __restrict__ b, int silu, void* __restrict__ out) {
+           const float* __restrict__ w, const float* __restrict__ b, int silu, float eps, void* __restrict__ out) {
     const int lane = threadIdx.x & 31;
     const int nchunk = c / 8;
     for (int64_t r = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); r < n;
@@ -157,7 +157,7 @@ k_row_norm(const void* __restrict__ src, const int32_t* __restrict__ rows, int64
         }
 #pragma unroll
         for (int s = 16; s > 0; s >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, s);
-        const float rstd = rsqrtf(s2 / (float)c + 1e-6f);
+        const float rstd = rsqrtf(s2 / (float)c + eps);
 #pragma unroll
         for (int j = 0; j < NCH; ++j) {
             const int k = lane + 32 * j;
@@ -205,13 +205,14 @@ int grid_for(tb_ctx* ctx, int64_t work, int per_block) {
 
 template <int IK, int OK>
 tb_status launch_row_norm_k(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t n, int c, const float* w,
-                            const float* b, int silu, void* out) {
+                            const float* b, int silu, float eps, void* out) {
     const int grid = grid_for(ctx, n, kWarpsPerBlock);
     const int nch = (c / 8 + 31) / 32;
-    if (nch <= 1) k_row_norm<IK, OK, 1><<<grid, kWarpsPerBlock * 32, 0, ctx->stream>>>(src, rows, n, c, w, b, silu, out);
-    else if (nch <= 2) k_row_norm<IK, OK, 2><<<grid, kWarpsPerBlock * 32, 0, ctx->stream>>>(src, rows, n, c, w, b, silu, out);
-    else if (nch <= 4) k_row_norm<IK, OK, 4><<<grid, kWarpsPerBlock * 32, 0, ctx->stream>>>(src, rows, n, c, w, b, silu, out);
-    else k_row_norm<IK, OK, 8><<<grid, kWarpsPerBlock * 32, 0, ctx->stream>>>(src, rows, n, c, w, b, silu, out);
+    const dim3 blk(kWarpsPerBlock * 32);
+    if (nch <= 1) k_row_norm<IK, OK, 1><<<grid, blk, 0, ctx->stream>>>(src, rows, n, c, w, b, silu, eps, out);
+    else if (nch <= 2) k_row_norm<IK, OK, 2><<<grid, blk, 0, ctx->stream>>>(src, rows, n, c, w, b, silu, eps, out);
+    else if (nch <= 4) k_row_norm<IK, OK, 4><<<grid, blk, 0, ctx->stream>>>(src, rows, n, c, w, b, silu, eps, out);
+    else k_row_norm<IK, OK, 8><<<grid, blk, 0, ctx->stream>>>(src, rows, n, c, w, b, silu, eps, out);
     TB_LAUNCH_CHECK(ctx, "k_row_norm");
     return TB_OK;
 }
@@ -222,14 +223,16 @@ tb_status launch_row_norm_k(tb_ctx* ctx, const void* src, const int32_t* rows, i
 // ggml_mul / ggml_add / ggml_silu chains of src/sparse.cpp:259-261,293. in_dtype is the source's
 // element type; out has `out_dtype`.
 tb_status tb_row_norm_launch(tb_ctx* ctx, const void* src, tb_dtype in_dtype, const int32_t* rows, int64_t n, int c,
-                             const float* w, const float* b, int silu, tb_dtype out_dtype, void* out) {
+                             const float* w, const float* b, int silu, tb_dtype out_dtype, void* out, float eps) {
     if (n == 0) return TB_OK;
     const int ik = kind_of(in_dtype), ok = kind_of(out_dtype);
-    if (ik == 0 && ok == 0) return launch_row_norm_k<0, 0>(ctx, src, rows, n, c, w, b, silu, out);
-    if (ik == 0 && ok == 1) return launch_row_norm_k<0, 1>(ctx, src, rows, n, c, w, b, silu, out);
-    if (ik == 0 && ok == 2) return launch_row_norm_k<0, 2>(ctx, src, rows, n, c, w, b, silu, out);
-    if (ik == 1 && ok == 1) return launch_row_norm_k<1, 1>(ctx, src, rows, n, c, w, b, silu, out);
-    if (ik == 2 && ok == 2) return launch_row_norm_k<2, 2>(ctx, src, rows, n, c, w, b, silu, out);
+    if (ik == 0 && ok == 0) return launch_row_norm_k<0, 0>(ctx, src, rows, n, c, w, b, silu, eps, out);
+    if (ik == 0 && ok == 1) return launch_row_norm_k<0, 1>(ctx, src, rows, n, c, w, b, silu, eps, out);
+    if (ik == 0 && ok == 2) return launch_row_norm_k<0, 2>(ctx, src, rows, n, c, w, b, silu, eps, out);
+    if (ik == 1 && ok == 1) return launch_row_norm_k<1, 1>(ctx, src, rows, n, c, w, b, silu, eps, out);
+    if (ik == 2 && ok == 2) return launch_row_norm_k<2, 2>(ctx, src, rows, n, c, w, b, silu, eps, out);
+    if (ik == 1 && ok == 0) return launch_row_norm_k<1, 0>(ctx, src, rows, n, c, w, b, silu, eps, out);
+    if (ik == 2 && ok == 0) return launch_row_norm_k<2, 0>(ctx, src, rows, n, c, w, b, silu, eps, out);
     return tb_fail(ctx, TB_ERR_UNSUPPORTED, "row norm: unsupported dtype pair");
 }
 

@@ -47,6 +47,8 @@ struct tb_ctx {
     cudaEvent_t stage_ev[2 + 2 * 32] = {};
     bool stage_ev_made = false;
     int32_t* chunk_hi_host = nullptr;
+    void* tail_ws = nullptr;       // ConvNeXt tail passes at wide C: LayerNorm output, activations
+    size_t tail_ws_bytes = 0;
 };
 
 // Record a failure on the context and return the status.
@@ -111,4 +113,14 @@ tb_status tb_convnext_tail_launch(tb_ctx* ctx, int64_t n, int c, const void* h, 
                                   const float* nw, const float* nb, const void* w1, const float* b1, const void* w2,
                                   const float* b2, tb_dtype dtype, tb_dtype out_dtype, void* out);
 bool tb_convnext_tc_supported(int c);
+bool tb_convnext_two_pass_supported(int c);
+// Row LayerNorm over c channels (c % 8 == 0, c <= 2048): out row r = act(LN(src row rows[r] or r)
+// * w + b) with eps; w/b may be NULL (no affine).
+tb_status tb_row_norm_launch(tb_ctx* ctx, const void* src, tb_dtype in_dtype, const int32_t* rows, int64_t n, int c,
+                             const float* w, const float* b, int silu, tb_dtype out_dtype, void* out,
+                             float eps = 1e-6f);
+// Per-voxel linear on tcgen05 (16-bit operands): out[m][n] = act(a[m] . w[n] + bias[n]) + res[m][n].
+tb_status tb_linear_launch(tb_ctx* ctx, int64_t m, int k, int n, const void* a, const void* w, const float* bias,
+                           const void* res, tb_dtype res_dtype, int act, tb_dtype dtype, tb_dtype out_dtype,
+                           void* out);
 uint64_t tb_hash_capacity(int64_t n);

@@ -757,6 +757,7 @@ tb_status launch_tail_tc(tb_ctx* ctx, int64_t n, const void* h, tb_dtype h_dtype
 }  // namespace
 
 bool tb_convnext_tc_supported(int c) { return c == 64 || c == 128 || c == 256; }
+bool tb_convnext_two_pass_supported(int c) { return c == 16 || c == 32 || (c % 64 == 0 && c <= 2048); }
 
 tb_status tb_convnext_tail_launch(tb_ctx* ctx, int64_t n, int c, const void* h, tb_dtype h_dtype, const void* x,
                                   const float* nw, const float* nb, const void* w1, const float* b1, const void* w2,
@@ -776,7 +777,22 @@ tb_status tb_convnext_tail_launch(tb_ctx* ctx, int64_t n, int c, const void* h, 
         case 64: return launch_tail_tc<64>(ctx, n, h, h_dtype, x, nw, nb, w1, b1, w2, b2, dtype, out_dtype, out);
         case 128: return launch_tail_tc<128>(ctx, n, h, h_dtype, x, nw, nb, w1, b1, w2, b2, dtype, out_dtype, out);
         case 256: return launch_tail_tc<256>(ctx, n, h, h_dtype, x, nw, nb, w1, b1, w2, b2, dtype, out_dtype, out);
-        default:
-            return tb_fail(ctx, TB_ERR_UNSUPPORTED, "convnext tail: 16-bit operands need C in {64, 128, 256}");
+        default: break;
     }
+    if (!tb_convnext_two_pass_supported(c))
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "convnext tail: 16-bit operands need C in {16, 32} or a multiple of 64 up to 2048");
+    // Widths whose LayerNorm tile does not fit the fused kernel's shared memory (C = 512, 1024 in
+    // decode_unet's first stages) run as three passes with the same roundings: LayerNorm to the
+    // operand type, mlp.0 + SiLU into a [n][4C] activation tile in HBM, mlp.2 + bias + residual.
+    const size_t es = tb_dtype_size(dtype);
+    const size_t y_b = ((size_t)n * c * es + 255) & ~size_t(255);
+    tb_status s = tb_ensure(ctx, &ctx->tail_ws, &ctx->tail_ws_bytes, y_b + (size_t)n * 4 * c * es, "convnext tail passes");
+    if (s != TB_OK) return s;
+    uint8_t* y = reinterpret_cast<uint8_t*>(ctx->tail_ws);
+    uint8_t* act = y + y_b;
+    s = tb_row_norm_launch(ctx, h, h_dtype, nullptr, n, c, nw, nb, 0, dtype, y, 1e-6f);
+    if (s != TB_OK) return s;
+    s = tb_linear_launch(ctx, n, c, 4 * c, y, w1, b1, nullptr, dtype, 1, dtype, dtype, act);
+    if (s != TB_OK) return s;
+    return tb_linear_launch(ctx, n, 4 * c, c, act, w2, b2, x, dtype, 0, dtype, out_dtype, out);
 }

@@ -213,6 +213,38 @@ def subdivide(coords: torch.Tensor, mask: torch.Tensor, max_children: int | None
     return child[: m.value], gidx[: m.value], mstart
 
 
+def linear(a: torch.Tensor, w: torch.Tensor, bias=None, act: str = "none", residual=None, out_dtype=None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = act(a @ w.T + bias) + residual (a [M,K], w [N,K] of a's dtype; bias float32 [N])."""
+    _need_cuda(a, w, bias, residual)
+    m, k = a.shape
+    n = w.shape[0]
+    if w.dtype != a.dtype or w.shape[1] != k:
+        raise ValueError("w must be [N, K] of a's dtype")
+    if bias is not None:
+        _f32_vec(bias, n, "bias")
+    od = a.dtype if out_dtype is None else out_dtype
+    if out is None:
+        out = torch.empty((m, n), dtype=od, device=a.device)
+    rd = residual.dtype if residual is not None else a.dtype
+    ctx = context(a.device)
+    check(_lib.load().tb_linear(ctx, m, k, n, _ptr(a), _ptr(w), _ptr(bias), _ptr(residual), _DT[rd], _EPI[act],
+                                _DT[a.dtype], _DT[out.dtype], _ptr(out)), "tb_linear", ctx)
+    return out
+
+
+def layer_norm(x: torch.Tensor, w=None, b=None, eps: float = 1e-6, act: str = "none", out_dtype=None) -> torch.Tensor:
+    """act(LayerNorm(x) * w + b) over the last dim (w, b float32 or None)."""
+    _need_cuda(x, w, b)
+    n, c = x.shape
+    od = x.dtype if out_dtype is None else out_dtype
+    out = torch.empty((n, c), dtype=od, device=x.device)
+    ctx = context(x.device)
+    check(_lib.load().tb_layer_norm(ctx, _ptr(x), _DT[x.dtype], n, c, _ptr(w), _ptr(b), eps, _EPI[act], _DT[od],
+                                    _ptr(out)), "tb_layer_norm", ctx)
+    return out
+
+
 def sparse_c2s(coords: torch.Tensor, feats: torch.Tensor, params: dict, cout: int, ext_mask=None,
                out_dtype=None, max_children: int | None = None):
     """``trellis::sparse_c2s`` (include/sparse.h:27-35, src/sparse.cpp:172-336) on the device.
