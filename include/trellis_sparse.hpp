@@ -13,6 +13,9 @@
 //                          tensors on the device, looked up by the reference's names; its
 //                          conv(), convnext() and c2s() give the weights of a block prefix
 //   read_slat              the hr_slat.bin decode input of src/decode_replay.cpp:19-28
+//   shape_decode, shape_upsample, tex_decode
+//                          include/shape_decoder.h: decode_unet (src/shape_decoder.cpp:79-138),
+//                          every stage on the device
 //   sparse_c2s             include/sparse.h:27-35 (src/sparse.cpp:172-336), the whole
 //                          SparseResBlockC2S3d; the block's device weights (C2SWeights) take
 //                          the place of Model + prefix
@@ -147,5 +150,28 @@ struct SlatInput {
     int res = 0;
 };
 SlatInput read_slat(const std::string& path);
+
+// The reference's ShapeOut (include/shape_decoder.h): per-voxel output fields [M][7] (ggml's
+// [7, M]), the final coordinates, the resolution and the per-stage subdivision masks.
+struct ShapeOut {
+    std::vector<float> feats7;
+    std::vector<std::array<int, 3>> coords;
+    int res = 512;
+    std::vector<std::vector<uint8_t>> subs;
+};
+
+// decode_unet (src/shape_decoder.cpp:79-117) on the device: from_latent, then per stage the
+// neighbor map, the stage's ConvNeXt blocks and its C2S up-block, then LayerNorm (eps 1e-5, no
+// affine) and output_layer. The stage layout (widths, block counts) is read from the
+// checkpoint's tensor names and shapes: blocks.<s>.<j>.conv.* are the ConvNeXt blocks of stage
+// s and blocks.<s>.<nblk>.* its C2S block, as in the reference's stage table
+// (src/shape_decoder.cpp:88). latent: [N0][32] float32.
+ShapeOut shape_decode(const GgufModel& m, const std::vector<float>& latent,
+                      const std::vector<std::array<int, 3>>& coords0, int resolution = 512);
+std::vector<std::array<int, 3>> shape_upsample(const GgufModel& m, const std::vector<float>& latent,
+                                               const std::vector<std::array<int, 3>>& coords0);
+std::vector<float> tex_decode(const GgufModel& m, const std::vector<float>& tex_latent,
+                              const std::vector<std::array<int, 3>>& coords0,
+                              const std::vector<std::vector<uint8_t>>& subs);
 
 }  // namespace trellis

@@ -342,6 +342,144 @@ C2SWeights GgufModel::c2s(const std::string& prefix) const {
     return w;
 }
 
+// ---- decode_unet on the device ----------------------------------------------------------------
+namespace {
+
+struct Stage {
+    std::string prefix;      // "blocks.<s>."
+    int c = 0, nblk = 0, cout = 0;
+};
+
+std::vector<Stage> stages_of(const GgufModel& m) {
+    std::vector<Stage> st;
+    for (int s = 0;; ++s) {
+        Stage g;
+        g.prefix = "blocks." + std::to_string(s) + ".";
+        while (m.has(g.prefix + std::to_string(g.nblk) + ".conv.weight")) ++g.nblk;
+        const std::string c2s = g.prefix + std::to_string(g.nblk);
+        if (!m.has(c2s + ".conv1.weight")) {
+            if (g.nblk) throw std::runtime_error("trellis: stage " + g.prefix + " has no C2S block");
+            break;
+        }
+        g.c = (int)m.shape(c2s + ".norm1.weight")[0];
+        g.cout = (int)m.shape(c2s + ".conv2.weight")[0];
+        st.push_back(g);
+    }
+    if (st.empty()) throw std::runtime_error("trellis: no decoder stages (blocks.0.*) in the model");
+    return st;
+}
+
+size_t esize(tb_dtype d) { return d == TB_F32 ? 4 : 2; }
+
+std::vector<float> decode_unet(const GgufModel& m, const std::vector<float>& latent, int out_ch,
+                               std::vector<std::array<int, 3>>& coords,
+                               const std::vector<std::vector<uint8_t>>* guide,
+                               std::vector<std::vector<uint8_t>>* subs_out, bool coords_only) {
+    const std::vector<Stage> st = stages_of(m);
+    const tb_dtype dt = m.weight_dtype;
+    const size_t es = esize(dt);
+    int64_t n = (int64_t)coords.size();
+    if ((int64_t)latent.size() != n * 32) throw std::runtime_error("trellis: decode: latent must be [N][32]");
+    if (guide && guide->size() < st.size()) throw std::runtime_error("trellis: decode: one guide mask per stage needed");
+    const int c0 = (int)m.shape("from_latent.weight")[0];
+    cuda_ok(cudaSetDevice(g_device), "cudaSetDevice");
+    tb_ctx* c = ctx();
+    // inputs: coordinates and the latent (rounded to the operand type like the features)
+    auto d_coords = std::make_unique<DBuf>((size_t)n * 12);
+    cuda_ok(cudaMemcpy(d_coords->p, coords.data(), (size_t)n * 12, cudaMemcpyHostToDevice), "upload coords");
+    DBuf d_lat((size_t)n * 32 * es);
+    if (dt == TB_F32) {
+        cuda_ok(cudaMemcpy(d_lat.p, latent.data(), latent.size() * 4, cudaMemcpyHostToDevice), "upload latent");
+    } else {
+        std::vector<uint16_t> hl(latent.size());
+        for (size_t k = 0; k < latent.size(); ++k)
+            hl[k] = dt == TB_BF16 ? f32_to_bf16_rne(latent[k]) : f32_to_f16_rne(latent[k]);
+        cuda_ok(cudaMemcpy(d_lat.p, hl.data(), hl.size() * 2, cudaMemcpyHostToDevice), "upload latent");
+    }
+    auto h = std::make_unique<DBuf>((size_t)n * c0 * es);
+    ok(tb_linear(c, n, 32, c0, d_lat.p, m.get("from_latent.weight"),
+                 static_cast<const float*>(m.get("from_latent.bias")), nullptr, dt, TB_EPI_NONE, dt, dt, h->p),
+       "from_latent");
+    int ch = c0;
+    for (size_t s = 0; s < st.size(); ++s) {
+        const Stage& g = st[s];
+        if (g.c != ch) throw std::runtime_error("trellis: decode: stage width does not match the previous stage");
+        DBuf nbr((size_t)n * 27 * 4);
+        ok(tb_build_neighbor_map(c, d_coords->as<int32_t>(), n, 3, nbr.as<int32_t>()), "stage map");
+        auto h2 = std::make_unique<DBuf>((size_t)n * ch * es);
+        for (int j = 0; j < g.nblk; ++j) {
+            const ConvNeXtWeights w = m.convnext(g.prefix + std::to_string(j));
+            ok(tb_sparse_convnext(c, nbr.as<int32_t>(), n, h->p, ch, w.conv.weight, w.conv.bias, w.norm_w, w.norm_b,
+                                  w.mlp0_w, w.mlp0_b, w.mlp2_w, w.mlp2_b, dt, dt, h2->p),
+               "ConvNeXt block");
+            std::swap(h, h2);
+        }
+        const C2SWeights w = m.c2s(g.prefix + std::to_string(g.nblk));
+        std::unique_ptr<DBuf> d_guide;
+        if (guide) {
+            if ((int64_t)(*guide)[s].size() != 8 * n) throw std::runtime_error("trellis: decode: guide mask size");
+            d_guide = std::make_unique<DBuf>((size_t)n * 8);
+            cuda_ok(cudaMemcpy(d_guide->p, (*guide)[s].data(), (size_t)n * 8, cudaMemcpyHostToDevice), "upload guide");
+        }
+        const int64_t cap = 8 * n;
+        auto child = std::make_unique<DBuf>((size_t)cap * 12);
+        auto out = std::make_unique<DBuf>((size_t)cap * g.cout * es);
+        DBuf mask((size_t)n * 8);
+        int64_t mc = 0;
+        ok(tb_sparse_c2s(c, d_coords->as<int32_t>(), n, 3, h->p, ch, g.cout, &w.p,
+                         d_guide ? d_guide->as<uint8_t>() : nullptr, dt, dt, cap, child->as<int32_t>(), out->p,
+                         mask.as<uint8_t>(), &mc),
+           "C2S block");
+        if (subs_out) {
+            std::vector<uint8_t> hm((size_t)n * 8);
+            cuda_ok(cudaMemcpy(hm.data(), mask.p, hm.size(), cudaMemcpyDeviceToHost), "download mask");
+            subs_out->push_back(std::move(hm));
+        }
+        d_coords = std::move(child);
+        h = std::move(out);
+        n = mc;
+        ch = g.cout;
+    }
+    coords.resize((size_t)n);
+    cuda_ok(cudaMemcpy(coords.data(), d_coords->p, (size_t)n * 12, cudaMemcpyDeviceToHost), "download coords");
+    if (coords_only) return {};
+    // LayerNorm (no affine, eps 1e-5) and output_layer (src/shape_decoder.cpp:62-77,114)
+    DBuf y((size_t)n * ch * es), o((size_t)n * out_ch * 4);
+    ok(tb_layer_norm(c, h->p, dt, n, ch, nullptr, nullptr, 1e-5f, TB_EPI_NONE, dt, y.p), "final LayerNorm");
+    ok(tb_linear(c, n, ch, out_ch, y.p, m.get("output_layer.weight"),
+                 static_cast<const float*>(m.get("output_layer.bias")), nullptr, dt, TB_EPI_NONE, dt, TB_F32, o.p),
+       "output_layer");
+    std::vector<float> res((size_t)n * out_ch);
+    cuda_ok(cudaMemcpy(res.data(), o.p, res.size() * 4, cudaMemcpyDeviceToHost), "download output");
+    ok(tb_ctx_check_device(c), "decode device check");
+    return res;
+}
+
+}  // namespace
+
+ShapeOut shape_decode(const GgufModel& m, const std::vector<float>& latent,
+                      const std::vector<std::array<int, 3>>& coords0, int resolution) {
+    ShapeOut so;
+    so.coords = coords0;
+    so.res = resolution;
+    so.feats7 = decode_unet(m, latent, (int)m.shape("output_layer.weight")[0], so.coords, nullptr, &so.subs, false);
+    return so;
+}
+
+std::vector<std::array<int, 3>> shape_upsample(const GgufModel& m, const std::vector<float>& latent,
+                                               const std::vector<std::array<int, 3>>& coords0) {
+    std::vector<std::array<int, 3>> coords = coords0;
+    decode_unet(m, latent, 0, coords, nullptr, nullptr, true);
+    return coords;
+}
+
+std::vector<float> tex_decode(const GgufModel& m, const std::vector<float>& tex_latent,
+                              const std::vector<std::array<int, 3>>& coords0,
+                              const std::vector<std::vector<uint8_t>>& subs) {
+    std::vector<std::array<int, 3>> coords = coords0;
+    return decode_unet(m, tex_latent, (int)m.shape("output_layer.weight")[0], coords, &subs, nullptr, false);
+}
+
 SlatInput read_slat(const std::string& path) {
     int64_t n = 0;
     int32_t res = 0;
