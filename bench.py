@@ -20,6 +20,11 @@ oracle/, all host threads) on a bounded sample of the same workload.
 parents (res-256 noisy shell) with its seeded child mask, Cin=256 -> Cout=128 bf16; metric
 children/s, roofline of conv1 (256 -> 8*128 channels, the block's dominant kernel).
 
+`--op decode` measures the sparse decoder UNet (decode_unet, src/shape_decoder.cpp:79-117) with
+the reference's stage table (widths 1024/512/256/128, 4/16/8/4 ConvNeXt blocks, C2S blocks, output
+64 -> 7) and random weights, on a res-32 noisy shell grown to res 512 by seeded shell-following
+masks (the texture decoder's guided path); metric output voxels/s.
+
 `--op convnext` measures one sparse ConvNeXt block instead (src/sparse.cpp:94-137 on the same
 shell): the conv into an fp32 h, then the fused LayerNorm + Linear C->4C + SiLU + Linear 4C->C +
 residual tail; metric voxels/s of the block, roofline of the tail kernel (HBM-bound).
@@ -621,6 +626,187 @@ def run_c2s(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- decoder UNet
+DEC_METRIC = ("output voxels/s through the sparse decoder UNet (from_latent, 4 stages of ConvNeXt blocks + C2S "
+              "up-blocks, LayerNorm + output_layer), res-32 shell -> res 512")
+DEC_STAGES = [(1024, 4, 512), (512, 16, 256), (256, 8, 128), (128, 4, 64)]    # C, ConvNeXt blocks, Cout
+
+
+def _dec_inputs():
+    from trellis_cpp_b200 import synth
+    coords = synth.shell(32, 12.5, 1.0, 8.0, 11, 2.0)
+    stage_coords, masks = [coords], []
+    res, rad, amp, sp = 32, 12.5, 1.0, 8.0
+    for _ in DEC_STAGES:
+        m = synth.child_mask(stage_coords[-1], res, rad, amp, sp, 11, 0.5)
+        masks.append(m)
+        c = stage_coords[-1][:, -3:].astype(np.int64)
+        idx = np.nonzero(m.reshape(-1))[0]
+        i, o = idx // 8, idx % 8
+        kids = np.stack([2 * c[i, 0] + (o & 1), 2 * c[i, 1] + ((o >> 1) & 1), 2 * c[i, 2] + ((o >> 2) & 1)], 1)
+        stage_coords.append(np.concatenate([np.zeros((kids.shape[0], 1), np.int64), kids], 1).astype(np.int32))
+        res, rad, amp, sp = 2 * res, 2 * rad, 2 * amp, 2 * sp
+    return stage_coords, masks
+
+
+def _dec_weights(rng_or_gen, make):
+    w = {"from_latent.weight": make((1024, 32), 1 / np.sqrt(32), True), "from_latent.bias": make((1024,), 0.1, False)}
+    for s, (c, nblk, cout) in enumerate(DEC_STAGES):
+        for j in range(nblk):
+            p = f"blocks.{s}.{j}."
+            w.update({p + "conv.weight": make((c, 27, c), 1 / np.sqrt(27 * c), True), p + "conv.bias": make((c,), 0.1, False),
+                      p + "norm.weight": make((c,), 0.1, False, 1.0), p + "norm.bias": make((c,), 0.1, False),
+                      p + "mlp.0.weight": make((4 * c, c), 1 / np.sqrt(c), True), p + "mlp.0.bias": make((4 * c,), 0.1, False),
+                      p + "mlp.2.weight": make((c, 4 * c), 1 / np.sqrt(4 * c), True), p + "mlp.2.bias": make((c,), 0.1, False)})
+        p = f"blocks.{s}.{nblk}."
+        w.update({p + "norm1.weight": make((c,), 0.1, False, 1.0), p + "norm1.bias": make((c,), 0.1, False),
+                  p + "conv1.weight": make((8 * cout, 27, c), 1 / np.sqrt(27 * c), True),
+                  p + "conv1.bias": make((8 * cout,), 0.1, False),
+                  p + "conv2.weight": make((cout, 27, cout), 1 / np.sqrt(27 * cout), True),
+                  p + "conv2.bias": make((cout,), 0.1, False)})
+    w["output_layer.weight"] = make((7, 64), 1 / np.sqrt(64), True)
+    w["output_layer.bias"] = make((7,), 0.1, False)
+    return w
+
+
+def _decode(ops, w, latent, coords, masks, stage_pairs=None):
+    """decode_unet through the library's C-ABI ops (device tensors); returns (out7, coords)."""
+    h = ops.linear(latent, w["from_latent.weight"], w["from_latent.bias"])
+    for s, (c, nblk, cout) in enumerate(DEC_STAGES):
+        nbr = ops.build_neighbor_table(coords)
+        if stage_pairs is not None:
+            stage_pairs.append(ops.count_valid_pairs(nbr, coords.shape[0]))
+        for j in range(nblk):
+            p = f"blocks.{s}.{j}."
+            h = ops.sparse_convnext(h, nbr, w[p + "conv.weight"], w[p + "conv.bias"], w[p + "norm.weight"],
+                                    w[p + "norm.bias"], w[p + "mlp.0.weight"], w[p + "mlp.0.bias"],
+                                    w[p + "mlp.2.weight"], w[p + "mlp.2.bias"])
+        p = f"blocks.{s}.{nblk}."
+        prm = {k[len(p):]: v for k, v in w.items() if k.startswith(p)}
+        h, coords, _ = ops.sparse_c2s(coords, h, prm, cout, ext_mask=masks[s], max_children=int(masks[s].sum()))
+    y = ops.layer_norm(h, eps=1e-5)
+    import torch
+    return ops.linear(y, w["output_layer.weight"], w["output_layer.bias"], out_dtype=torch.float32), coords
+
+
+def cpu_decode_patch(stage0, nthreads, patch=2):
+    """The decoder on the parents of a patch x, y in [x0, x0 + patch) of the res-32 shell with the
+    oracle port: fp32 multi-threaded convs (orc_submconv_f32_mt), numpy LayerNorm / MLP / linears,
+    the oracle's subdivide and gathers, shell-following masks as in the GPU run, random weights
+    of the same shapes (the time does not depend on their values). Returns (s per output voxel,
+    s, parents, output voxels)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from trellis_cpp_b200 import synth
+    rng = np.random.default_rng(5)
+    c = stage0[:, -3:]
+    x0, y0 = int(np.median(c[:, 0])), int(np.median(c[:, 1]))
+    par = stage0[(c[:, 0] >= x0) & (c[:, 0] < x0 + patch) & (c[:, 1] >= y0 - 4) & (c[:, 1] < y0 + 4)]
+    coords = np.ascontiguousarray(par[:, -3:])
+
+    def wt(co, ci):
+        return oracle.weight_tap_major(rng.standard_normal((co, 27, ci), dtype=np.float32) / np.sqrt(27 * ci))
+    t0 = time.perf_counter()
+    h = rng.standard_normal((coords.shape[0], 32), dtype=np.float32) @ \
+        (rng.standard_normal((32, 1024), dtype=np.float32) / np.sqrt(32))
+    res, rad, amp, sp = 32, 12.5, 1.0, 8.0
+    for c_in, nblk, cout in DEC_STAGES:
+        nbr = oracle.build_neighbor_table(coords)
+        for _ in range(nblk):
+            conv = oracle.submconv_f32_mt(nbr, h, wt(c_in, c_in), nthreads=nthreads)
+            y = oracle.layer_norm(conv).astype(np.float32)
+            a = oracle.silu(y @ (rng.standard_normal((c_in, 4 * c_in), dtype=np.float32) / np.sqrt(c_in)))
+            h = (a.astype(np.float32) @ (rng.standard_normal((4 * c_in, c_in), dtype=np.float32) / np.sqrt(4 * c_in))
+                 + h).astype(np.float32)
+        mask = synth.child_mask(coords, res, rad, amp, sp, 11, 0.5)
+        hn = oracle.silu(oracle.layer_norm(h)).astype(np.float32)
+        h1 = oracle.submconv_f32_mt(nbr, hn, wt(8 * cout, c_in), nthreads=nthreads)
+        child, gidx, _ = oracle.subdivide(coords, mask)
+        hc = oracle.silu(oracle.layer_norm(oracle.c2s_gather(h1, gidx, cout))).astype(np.float32)
+        nbr2 = oracle.build_neighbor_table(child)
+        h = oracle.submconv_f32_mt(nbr2, hc, wt(cout, cout), nthreads=nthreads) + \
+            np.repeat(oracle.c2s_gather(h, gidx, c_in // 8), cout // (c_in // 8), axis=1)
+        coords = np.ascontiguousarray(child)
+        res, rad, amp, sp = 2 * res, 2 * rad, 2 * amp, 2 * sp
+    out = oracle.layer_norm(h, eps=1e-5) @ rng.standard_normal((64, 7))
+    dt = time.perf_counter() - t0
+    return dt / max(1, out.shape[0]), dt, par.shape[0], out.shape[0]
+
+
+def run_decode(args):
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _load_package()
+    from trellis_cpp_b200 import ops
+    stage_coords, masks_np = _dec_inputs()
+    g = torch.Generator(device=dev).manual_seed(77)
+
+    def make(shape, scale, weight, offset=0.0):
+        t = offset + scale * torch.randn(shape, device=dev, generator=g)
+        return t.bfloat16() if weight else t.float()
+    w = _dec_weights(g, make)
+    coords = torch.from_numpy(stage_coords[0]).to(dev)
+    masks = [torch.from_numpy(m).to(dev) for m in masks_np]
+    latent = torch.randn((coords.shape[0], 32), device=dev, generator=g).bfloat16()
+    pairs = []
+    out, final = _decode(ops, w, latent, coords, masks, pairs)
+    for _ in range(max(2, args.warmup - 1)):
+        _decode(ops, w, latent, coords, masks)
+    torch.cuda.synchronize()
+    ops.check_device()
+    m_final = final.shape[0]
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    sampler.start()
+    time.sleep(0.8)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        _decode(ops, w, latent, coords, masks)
+    e1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    ops.check_device()
+    ms = e0.elapsed_time(e1) / args.steps
+    # algorithmic FLOPs: convs on present pairs, MLPs and linears per voxel
+    ns = [sc.shape[0] for sc in stage_coords]
+    flops = 2.0 * 32 * 1024 * ns[0] + 2.0 * 64 * 7 * ns[-1]
+    child_pairs = []
+    for s, (c, nblk, cout) in enumerate(DEC_STAGES):
+        flops += nblk * (2.0 * c * c * pairs[s] + 2 * 2.0 * 4 * c * c * ns[s])
+        flops += 2.0 * c * 8 * cout * pairs[s]
+        nb_child = ops.build_neighbor_table(torch.from_numpy(stage_coords[s + 1]).to(dev))
+        child_pairs.append(ops.count_valid_pairs(nb_child, ns[s + 1]))
+        flops += 2.0 * cout * cout * child_pairs[-1]
+    peak_tf, _, peak_kind = _peaks()
+    achieved = flops / (ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                "traffic": None, "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                "kernel": "the whole decode (convs, MLPs, linears)", "flops_per_step": flops}
+    line = {
+        "metric": DEC_METRIC, "value": m_final / (ms / 1e3), "unit": "voxels/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded res-32 noisy shell, seeded shell-following masks, random weights of the "
+                "reference's stage shapes)",
+        "config": {"workload": "decode_unet, stage table 1024x4/512x16/256x8/128x4 + C2S, out 7 channels",
+                   "voxels_per_stage": ns, "parent_pairs": pairs, "child_pairs": child_pairs,
+                   "l2": "weights 0.9 GB and activations larger than L2"},
+        "roofline": roofline, "cpu_baseline": None, "e2e": None, "clocks": sampler.summary(),
+    }
+    if not args.no_cpu:
+        nthreads = os.cpu_count() or 1
+        spv, dt, npar, nout = cpu_decode_patch(stage_coords[0], nthreads)
+        line["cpu_baseline"] = {"value": 1.0 / spv, "unit": "voxels/s", "cores": nthreads, "kind": "port",
+                                "sample": f"oracle port (fp32 multi-threaded convs, numpy MLPs, the oracle's "
+                                          f"subdivide and gathers) on a {npar}-parent patch of the shell grown to "
+                                          f"{nout} output voxels ({dt:.1f} s)"}
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -631,16 +817,16 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--workload", default=WORKLOAD, choices=["c4", "c4s"],
                     help="c4 (default, the benchmark) or c4s (half scale, for profiler captures)")
-    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s"],
-                    help="stack (default, the benchmark: map + conv x2), convnext (one ConvNeXt block) or c2s "
-                         "(one C2S up-block)")
+    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s", "decode"],
+                    help="stack (default, the benchmark: map + conv x2), convnext (one ConvNeXt block), c2s "
+                         "(one C2S up-block) or decode (the sparse decoder UNet)")
     args = ap.parse_args()
-    if args.op in ("convnext", "c2s"):
+    if args.op in ("convnext", "c2s", "decode"):
         if args.impl == "reference" or args.gpus != 1:
             print(json.dumps({"impl": args.impl, "unavailable": f"--op {args.op} is a single-GPU measurement of "
                               "our kernels; its CPU baseline is in the line's cpu_baseline"}))
             return 0
-        return run_convnext(args) if args.op == "convnext" else run_c2s(args)
+        return {"convnext": run_convnext, "c2s": run_c2s, "decode": run_decode}[args.op](args)
     if args.impl == "reference":
         return run_reference(args)
     return run_gpu(args)
