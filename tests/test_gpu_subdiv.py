@@ -75,3 +75,21 @@ def test_bias_act(tb, dt):
     ref = oracle.silu(x.float().cpu().numpy().astype(np.float64) + b.cpu().numpy())
     ops.bias_act(x, b, "silu")
     assert max_rel(x.float().cpu().numpy(), ref) < (1e-6 if dt == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("c,dt", [(64, torch.bfloat16), (16, torch.float32), (3, torch.float32)])
+def test_gather_and_scatter_rows(tb, c, dt):
+    # the halo packing of the multi-GPU step: gather rows into a contiguous buffer, scatter a
+    # received buffer back to its row positions (row sizes with and without 16-byte vectors)
+    from trellis_cpp_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(c)
+    src = torch.randn((5000, c), device="cuda", generator=g).to(dt)
+    rows = torch.randperm(5000, device="cuda", generator=g)[:1234].to(torch.int32)
+    packed = ops.gather_rows(src, rows)
+    assert torch.equal(packed, src[rows.long()])
+    dst = torch.zeros_like(src)
+    ops.scatter_rows(dst, rows, packed)
+    ops.check_device()
+    expect = torch.zeros_like(src)
+    expect[rows.long()] = src[rows.long()]
+    assert torch.equal(dst, expect)

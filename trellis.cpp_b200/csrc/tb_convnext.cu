@@ -49,24 +49,28 @@ constexpr int kThreads = (kIssuerWarp + 1) * 32;
 constexpr uint32_t kBlk = kRows * 128;                      // one [128 rows][128 B] swizzled block
 
 // mbarriers: two slots per kind (stage s of a ring at 2 * kind + s), then the drain barrier.
-enum { A1F, A1E, D1F, D1E, A2F, A2E, D2F, D2E, W1F, W1E, W2F, W2E, kKinds };
+enum { A1F, A1E, D1F, D1E, A2F, A2E, D2F, D2E, W1F, W1E, W2F, W2E, HF, HE, kKinds };
 constexpr int kNumBars = 2 * kKinds + 1;
 
 // Pipeline shape per width: hidden chunk HC, LayerNorm A tiles NA1, mlp.0 / mlp.2 weight stages
-// NW1 / NW2, output accumulators NB2, within one SM's 227 KB of shared memory and 512 TMEM columns
-// (C = 256 keeps one A tile and one mlp.2 stage to leave room for the staged parameters).
+// NW1 / NW2, output accumulators NB2, staged h tiles NH, within one SM's 227 KB of shared memory
+// and 512 TMEM columns (C = 256 keeps one A tile and one mlp.2 stage to leave room for the staged
+// parameters). With NH = 2 (C = 64: two 32 KB fp32 tiles fill the last of the 227 KB) the
+// LayerNorm warps read h from shared memory, bulk-copied two tiles ahead; wider tiles do not fit
+// and are loaded by the LayerNorm warps themselves.
 template <int C> struct TailCfg;
-template <> struct TailCfg<64> { static constexpr int HC = 128, NA1 = 2, NW1 = 2, NW2 = 2, NB2 = 2; };
-template <> struct TailCfg<128> { static constexpr int HC = 64, NA1 = 2, NW1 = 2, NW2 = 2, NB2 = 2; };
-template <> struct TailCfg<256> { static constexpr int HC = 64, NA1 = 1, NW1 = 2, NW2 = 1, NB2 = 1; };
+template <> struct TailCfg<64> { static constexpr int HC = 128, NA1 = 2, NW1 = 2, NW2 = 2, NB2 = 2, NH = 2; };
+template <> struct TailCfg<128> { static constexpr int HC = 64, NA1 = 2, NW1 = 2, NW2 = 2, NB2 = 2, NH = 0; };
+template <> struct TailCfg<256> { static constexpr int HC = 64, NA1 = 1, NW1 = 2, NW2 = 1, NB2 = 1, NH = 0; };
 
 template <int C> struct TailLayout {
     using K = TailCfg<C>;
     static constexpr int HC = K::HC, NCH = 4 * C / HC, KB1 = C / 64, KB2 = HC / 64;
     // one A tile, one activation tile, one mlp.0 stage ([HC rows][C]), one mlp.2 stage ([C rows][HC])
     static constexpr uint32_t A1 = KB1 * kBlk, A2 = KB2 * kBlk, W1 = KB1 * HC * 128, W2 = KB2 * C * 128;
+    static constexpr uint32_t H = kRows * C * 4;            // one staged h tile (fp32 at most)
     static constexpr uint32_t off_a2 = K::NA1 * A1, off_w1 = off_a2 + 2 * A2, off_w2 = off_w1 + K::NW1 * W1,
-                              off_bar = off_w2 + K::NW2 * W2;
+                              off_h = off_w2 + K::NW2 * W2, off_bar = off_h + K::NH * H;
     static constexpr bool resident = K::NW1 >= NCH && K::NW2 >= NCH;
     static constexpr uint32_t d2_col = 2 * HC;              // D1 slots at columns 0 and HC
     static constexpr uint32_t tmem_cols = (2 * HC + K::NB2 * C) <= 256 ? 256u : 512u;
@@ -154,7 +158,6 @@ __device__ __forceinline__ float silu_half(float d, float bh) {
     asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
     return fmaf(u, t, u);
 }
-
 // Eight consecutive values (16 bytes) of row r, K chunk kc (0..7 within a 64-wide K block) of a
 // [128 rows][128 B] K-major block with the 128-byte swizzle: chunk kc sits at kc ^ (r & 7).
 __device__ __forceinline__ void put16(uint8_t* blk, int r, int kc, uint4 v) {
@@ -184,6 +187,126 @@ __device__ __forceinline__ void prefetch_tile_l2(const uint8_t* base, int64_t n,
 // .sync.aligned instructions (TMEM loads, elect.sync, shuffles) stay converged.
 __device__ __forceinline__ bool wait_all(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, err));
+}
+
+// LayerNorm warp with staged h (C = 64): the CTA's h tiles arrive by TMA two tiles ahead in the
+// 128-byte-swizzled layout (in each 128-byte box of a row, 16-byte chunk c of row r sits at
+// c ^ (r & 7)), so a thread reads its own row without bank conflicts. Thread = row: the mean and
+// variance (one shifted pass), then the normalised row, in two passes over shared memory, with no
+// shuffles and one rsqrt per row (the shuffle reductions and their per-row-group rsqrt queued
+// behind the activation warps' MUFU and shared-memory traffic).
+template <int C, int HK, int XK>
+__device__ __forceinline__ void ln_warp_staged(const TailParams& p, const CUtensorMap* hmap, uint8_t* a1, uint8_t* hst,
+                                               uint32_t b0, const float* s_nw, const float* s_nb, int ntl, int w,
+                                               int lane, volatile int* s_abort) {
+    using L = TailLayout<C>;
+    constexpr int ES = HK == 0 ? 4 : 2, NBOX = C * ES / 128, VPC = 16 / ES;   // values per 16-byte chunk
+    constexpr uint32_t kBoxBytes = kRows * 128;
+    const int r = w * 32 + lane;
+    int issued = 0, consumed = 0;
+    auto issue = [&](int u) {
+        const int tile_u = blockIdx.x + u * gridDim.x;
+        const uint32_t fb = bar_at(b0, HF, u & 1);
+        mbar_arrive_expect_tx(fb, NBOX * kBoxBytes);
+#pragma unroll
+        for (int b = 0; b < NBOX; ++b)
+            tma_load_2d(smem_u32(hst + (u & 1) * L::H + b * kBoxBytes), hmap, b * (128 / ES), tile_u * kRows, fb);
+    };
+    if (w == 0 && lane == 0)
+        for (; issued < 2 && issued < ntl; ++issued) issue(issued);
+    for (int t = 0; t < ntl; ++t) {
+        const int s = t % L::K::NA1;
+        if (!wait_all(bar_at(b0, HF, t & 1), (uint32_t)((t >> 1) & 1), s_abort, p.err)) break;
+        consumed = t + 1;
+        if (t >= L::K::NA1 && !wait_all(bar_at(b0, A1E, s), (uint32_t)(((t / L::K::NA1) - 1) & 1), s_abort, p.err))
+            break;
+        if (w == 0) TB_STAMP(0, t);
+        const uint8_t* hrow = hst + (t & 1) * L::H + r * 128;
+        // VPC values of chunk c (0..7) of box b of this thread's row
+        auto chunk = [&](int b, int c, float* v) {
+            const uint4 u = *reinterpret_cast<const uint4*>(hrow + b * kBoxBytes + ((c ^ (r & 7)) << 4));
+            if constexpr (HK == 0) {
+                v[0] = __uint_as_float(u.x), v[1] = __uint_as_float(u.y), v[2] = __uint_as_float(u.z),
+                v[3] = __uint_as_float(u.w);
+            } else {
+                const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 f = unpack2<HK>(wd[q]);
+                    v[2 * q] = f.x, v[2 * q + 1] = f.y;
+                }
+            }
+        };
+        // one pass for both statistics, shifted by the row's first value (x - x0 keeps the sums
+        // small, so E[(x-x0)^2] - E[x-x0]^2 does not cancel for rows far from zero)
+        float x0;
+        {
+            float v[VPC];
+            chunk(0, 0, v);
+            x0 = v[0];
+        }
+        float part[4] = {0.f, 0.f, 0.f, 0.f}, q2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int b = 0; b < NBOX; ++b)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                float v[VPC];
+                chunk(b, c, v);
+#pragma unroll
+                for (int e = 0; e < VPC; ++e) {
+                    const float d = v[e] - x0;
+                    part[e & 3] += d;
+                    q2[e & 3] = fmaf(d, d, q2[e & 3]);
+                }
+            }
+        const float dm = ((part[0] + part[1]) + (part[2] + part[3])) * (1.0f / C);
+        const float mean = x0 + dm;
+        const float var = fmaxf(((q2[0] + q2[1]) + (q2[2] + q2[3])) * (1.0f / C) - dm * dm, 0.f);
+        const float rs = rsqrtf(var + 1e-6f);
+        uint8_t* a1s = a1 + s * L::A1;
+#pragma unroll 2
+        for (int oc = 0; oc < C / 8; ++oc) {                  // 8 channels = one 16-byte chunk of A1
+            float v[8];
+            if constexpr (VPC == 4) {
+                chunk((oc * 8) / 32, ((oc * 8) % 32) / 4, v);
+                chunk((oc * 8) / 32, ((oc * 8) % 32) / 4 + 1, v + 4);
+            } else {
+                chunk((oc * 8) / 64, ((oc * 8) % 64) / 8, v);
+            }
+            const float4 w0 = *reinterpret_cast<const float4*>(s_nw + oc * 8);
+            const float4 w1 = *reinterpret_cast<const float4*>(s_nw + oc * 8 + 4);
+            const float4 n0 = *reinterpret_cast<const float4*>(s_nb + oc * 8);
+            const float4 n1 = *reinterpret_cast<const float4*>(s_nb + oc * 8 + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const float bv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                pk[e] = pack2<XK>((v[2 * e] - mean) * rs * wv[2 * e] + bv[2 * e],
+                                  (v[2 * e + 1] - mean) * rs * wv[2 * e + 1] + bv[2 * e + 1]);
+            put16(a1s + (oc >> 3) * kBlk, r, oc & 7, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(bar_at(b0, A1F, s));
+            mbar_arrive(bar_at(b0, HE, t & 1));       // this warp is done with the staged tile
+        }
+        if (w == 0 && lane == 0 && t + 2 < ntl) {
+            // the copy of tile t + 2 reuses this stage once all four LayerNorm warps have read it
+            if (!mbar_wait(bar_at(b0, HE, t & 1), (uint32_t)((t >> 1) & 1), s_abort, p.err)) {
+                __syncwarp(1u);
+            } else {
+                issue(t + 2);
+                issued = t + 3;
+            }
+        }
+        __syncwarp();
+        if (w == 0) TB_STAMP(1, t);
+    }
+    // copies still in flight after an abort land before the CTA exits
+    if (w == 0 && lane == 0)
+        for (int u = consumed; u < issued; ++u) wait_bounded(bar_at(b0, HF, u & 1), (uint32_t)((u >> 1) & 1));
 }
 
 // LayerNorm warp: rows [32 w, 32 w + 32) of every tile of this CTA into the A tiles. Eight
@@ -238,6 +361,7 @@ __device__ __forceinline__ void ln_warp(const TailParams& p, uint8_t* a1, uint32
                 for (int e = 0; e < V; ++e) sm += val(i, e);
                 mean[i] = sm;
             }
+            if (w == 0 && bs == 0) TB_STAMP(13, t);
 #pragma unroll
             for (int o = 4; o > 0; o >>= 1)
 #pragma unroll
@@ -278,12 +402,22 @@ __device__ __forceinline__ void ln_warp(const TailParams& p, uint8_t* a1, uint32
                     put16(a1s + (cb >> 6) * kBlk, rr, (cb & 63) >> 3, make_uint4(pk[0], pk[1], pk[2], pk[3]));
                 }
             }
+            if (w == 0) TB_STAMP(bs == 0 ? 14 : 15, t);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_at(b0, A1F, s));
         if (w == 0) TB_STAMP(1, t);
     }
+}
+
+// The LayerNorm role: staged h tiles where shared memory holds them (C = 64), else row loads.
+template <int C, int HK, int XK>
+__device__ __forceinline__ void ln_role(const TailParams& p, const CUtensorMap* hmap, uint8_t* a1, uint8_t* hst,
+                                        uint32_t b0, const float* s_nw, const float* s_nb, int ntl, int w, int lane,
+                                        volatile int* s_abort) {
+    if constexpr (TailCfg<C>::NH > 0) ln_warp_staged<C, HK, XK>(p, hmap, a1, hst, b0, s_nw, s_nb, ntl, w, lane, s_abort);
+    else ln_warp<C, HK, XK>(p, a1, b0, s_nw, s_nb, ntl, w, lane, s_abort);
 }
 
 // What every warp role of the tail kernel reads.
@@ -428,7 +562,7 @@ __device__ __forceinline__ void out_warp(const RoleCtx& x) {
 template <int C>
 __global__ void __launch_bounds__(kThreads, 1)
 k_convnext_tail(const __grid_constant__ CUtensorMap w1map, const __grid_constant__ CUtensorMap w2map,
-                const TailParams p) {
+                const __grid_constant__ CUtensorMap hmap, const TailParams p) {
     using L = TailLayout<C>;
     using K = typename L::K;
     constexpr int HC = L::HC, NCH = L::NCH, KB1 = L::KB1, KB2 = L::KB2;
@@ -463,12 +597,15 @@ k_convnext_tail(const __grid_constant__ CUtensorMap w1map, const __grid_constant
             mbar_init(bar_at(b0, W1E, s), 1);
             mbar_init(bar_at(b0, W2F, s), 1);
             mbar_init(bar_at(b0, W2E, s), 1);
+            mbar_init(bar_at(b0, HF, s), 1);
+            mbar_init(bar_at(b0, HE, s), kLnWarps);
         }
         mbar_init(b0 + 8u * (kNumBars - 1), 1);
         s_misc[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&w1map)) : "memory");
         asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&w2map)) : "memory");
+        if (K::NH > 0) asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&hmap)) : "memory");
     }
     for (int i = threadIdx.x; i < 4 * C; i += kThreads) s_b1h[i] = 0.5f * __ldg(p.b1 + i);
     for (int i = threadIdx.x; i < C; i += kThreads) {
@@ -490,11 +627,11 @@ k_convnext_tail(const __grid_constant__ CUtensorMap w1map, const __grid_constant
     if (warp < kActWarp0) {
         // ------------------------------------------------------------------ LayerNorm warps
         if (p.x_kind == 2) {
-            if (p.h_kind == 0) ln_warp<C, 0, 2>(p, a1, b0, s_nw, s_nb, ntl, warp, lane, s_abort);
-            else ln_warp<C, 2, 2>(p, a1, b0, s_nw, s_nb, ntl, warp, lane, s_abort);
+            if (p.h_kind == 0) ln_role<C, 0, 2>(p, &hmap, a1, smem + L::off_h, b0, s_nw, s_nb, ntl, warp, lane, s_abort);
+            else ln_role<C, 2, 2>(p, &hmap, a1, smem + L::off_h, b0, s_nw, s_nb, ntl, warp, lane, s_abort);
         } else {
-            if (p.h_kind == 0) ln_warp<C, 0, 1>(p, a1, b0, s_nw, s_nb, ntl, warp, lane, s_abort);
-            else ln_warp<C, 1, 1>(p, a1, b0, s_nw, s_nb, ntl, warp, lane, s_abort);
+            if (p.h_kind == 0) ln_role<C, 0, 1>(p, &hmap, a1, smem + L::off_h, b0, s_nw, s_nb, ntl, warp, lane, s_abort);
+            else ln_role<C, 1, 1>(p, &hmap, a1, smem + L::off_h, b0, s_nw, s_nb, ntl, warp, lane, s_abort);
         }
     } else if (warp < kOutWarp0) {
         // ------------------------------------------------------------------ activation warps
@@ -716,7 +853,7 @@ tb_status launch_tail_tc(tb_ctx* ctx, int64_t n, const void* h, tb_dtype h_dtype
     p.trace = nullptr;
 #endif
 
-    CUtensorMap w1map, w2map;
+    CUtensorMap w1map, w2map, hmap;
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType dt = dtype == TB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     {
@@ -739,6 +876,21 @@ tb_status launch_tail_tc(tb_ctx* ctx, int64_t n, const void* h, tb_dtype h_dtype
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for mlp.2 weights");
     }
+    hmap = w1map;                      // not read unless the h tiles are staged
+    if (TailCfg<C>::NH > 0) {
+        // h [n][C] in boxes of 128 bytes x 128 rows, 128-byte swizzle (rows past n read as zero)
+        const int es = h_dtype == TB_F32 ? 4 : 2;
+        const CUtensorMapDataType hdt = h_dtype == TB_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                        : (h_dtype == TB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+        const cuuint64_t gdim[2] = {(cuuint64_t)C, (cuuint64_t)n};
+        const cuuint64_t gstride[1] = {(cuuint64_t)C * es};
+        const cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)kRows};
+        CUresult cr = reinterpret_cast<EncodeTiledFn>(ctx->encode_tiled)(
+            &hmap, hdt, 2, const_cast<void*>(h), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for h");
+    }
     const size_t smem = L::smem;
     if (smem > (size_t)ctx->max_smem_optin) return tb_fail(ctx, TB_ERR_UNSUPPORTED, "convnext tail: shared memory too small");
     static size_t smem_set[3] = {0, 0, 0};      // per C; the attribute only ever grows
@@ -749,7 +901,7 @@ tb_status launch_tail_tc(tb_ctx* ctx, int64_t n, const void* h, tb_dtype h_dtype
         smem_set[si] = smem;
     }
     const int grid = std::max(1, std::min(p.ntiles, ctx->num_sms));
-    k_convnext_tail<C><<<grid, kThreads, smem, ctx->stream>>>(w1map, w2map, p);
+    k_convnext_tail<C><<<grid, kThreads, smem, ctx->stream>>>(w1map, w2map, hmap, p);
     TB_LAUNCH_CHECK(ctx, "k_convnext_tail");
     return TB_OK;
 }
