@@ -25,6 +25,10 @@ the reference's stage table (widths 1024/512/256/128, 4/16/8/4 ConvNeXt blocks, 
 64 -> 7) and random weights, on a res-32 noisy shell grown to res 512 by seeded shell-following
 masks (the texture decoder's guided path); metric output voxels/s.
 
+`--op mesh` measures dual_grid_to_mesh (src/dual_grid.cpp:16-56) on the config-4 shell taken as
+the decoded voxels (res 1024) with seeded decoder-head fields; metric voxels/s; CPU baseline = the
+reference's own dual_grid_to_mesh compiled from its sources (oracle/_ref) where it was built.
+
 `--op convnext` measures one sparse ConvNeXt block instead (src/sparse.cpp:94-137 on the same
 shell): the conv into an fp32 h, then the fused LayerNorm + Linear C->4C + SiLU + Linear 4C->C +
 residual tail; metric voxels/s of the block, roofline of the tail kernel (HBM-bound).
@@ -626,6 +630,123 @@ def run_c2s(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- dual-grid mesh
+MESH_METRIC = ("voxels/s through dual_grid_to_mesh (src/dual_grid.cpp:16-56): dual vertices, coordinate "
+               "lookups of each intersected edge's quad, split and triangles in the reference's order")
+
+
+def cpu_mesh_step(coords, f7, res):
+    """The reference's own dual_grid_to_mesh (oracle/_ref) when it was built, else the oracle
+    port; one call over the whole workload. Returns (seconds per voxel, seconds, kind, F)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    t0 = time.perf_counter()
+    if oracle.ref_available():
+        _, faces = oracle.ref_dual_grid_mesh(coords, f7, res)
+        kind = "reference"
+    else:
+        _, faces, _ = oracle.dual_grid_mesh(coords, f7, res)
+        kind = "port"
+    dt = time.perf_counter() - t0
+    return dt / len(coords), dt, kind, int(faces.shape[0])
+
+
+def run_mesh(args):
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _load_package()
+    from trellis_cpp_b200 import ops, synth
+
+    coords_np = np.ascontiguousarray(synth.coords_for(args.workload)[:, -3:])
+    n = coords_np.shape[0]
+    res = 1024
+    f7_np = (np.random.default_rng(77).standard_normal((n, 7)) * 2).astype(np.float32)
+    coords = torch.from_numpy(coords_np).to(dev)
+    f7 = torch.from_numpy(f7_np).to(dev)
+    faces = None
+    for _ in range(max(3, args.warmup)):
+        _, faces = ops.dual_grid_mesh(coords, f7, res)
+    torch.cuda.synchronize()
+    ops.check_device()
+    nf = faces.shape[0]
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    sampler.start()
+    time.sleep(0.8)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ops.dual_grid_mesh(coords, f7, res)
+    e1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    ops.check_device()
+    ms_step = e0.elapsed_time(e1) / args.steps
+
+    # end to end: pinned host inputs up, the call, vertices and triangles down
+    e2e = None
+    if not args.no_e2e:
+        hc = torch.from_numpy(coords_np).pin_memory()
+        hf = torch.from_numpy(f7_np).pin_memory()
+        hv = torch.empty((n, 3), dtype=torch.float32).pin_memory()
+        hfa = torch.empty((6 * n, 3), dtype=torch.int32).pin_memory()
+        dc = torch.empty_like(coords)
+        df = torch.empty_like(f7)
+
+        def e2e_step():
+            dc.copy_(hc, non_blocking=True)
+            df.copy_(hf, non_blocking=True)
+            v, fa = ops.dual_grid_mesh(dc, df, res)
+            hv.copy_(v, non_blocking=True)
+            hfa[: fa.shape[0]].copy_(fa, non_blocking=True)
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        x0 = torch.cuda.Event(enable_timing=True)
+        x1 = torch.cuda.Event(enable_timing=True)
+        k = max(1, min(args.steps, 20))
+        x0.record()
+        for _ in range(k):
+            e2e_step()
+        x1.record()
+        torch.cuda.synchronize()
+        ms_e2e = x0.elapsed_time(x1) / k
+        e2e = {"value": n / (ms_e2e / 1e3), "unit": "voxels/s", "h2d_bytes_per_step": n * 40,
+               "d2h_bytes_per_step": n * 12 + nf * 12, "steps": k, "ms_per_step": ms_e2e,
+               "call": "tb_dual_grid_mesh with pinned host inputs and outputs"}
+    _, peak_bw, peak_kind = _peaks()
+    alg_bytes = n * (12 + 28 + 12) + nf * 12
+    achieved = alg_bytes / (ms_step / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak_bw, "unit": "GB/s", "frac": achieved / peak_bw,
+                "traffic": None, "peak_source": f"{peak_kind} hbm_gbs",
+                "kernel": "tb_dual_grid_mesh (whole call: seven-tap map build + k_mesh_count + scan + k_mesh_emit)",
+                "bytes_per_launch": alg_bytes}
+    cpu = None
+    if not args.no_cpu:
+        spv, dt, kind, cpu_f = cpu_mesh_step(coords_np, f7_np, res)
+        if cpu_f != nf:
+            raise RuntimeError(f"CPU and GPU triangle counts differ: {cpu_f} vs {nf}")
+        cpu = {"value": 1.0 / spv, "unit": "voxels/s", "cores": 1, "kind": kind,
+               "sample": ("the reference's own dual_grid_to_mesh (compiled from its sources)" if kind == "reference"
+                          else "oracle port of dual_grid_to_mesh") + f", single-threaded, whole workload ({dt:.2f} s)"}
+    line = {
+        "metric": MESH_METRIC, "value": n / (ms_step / 1e3), "unit": "voxels/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded res-1024 noisy shell, decoder-head fields N(0, 2^2))",
+        "config": {"workload": f"{args.workload}: res-1024 noisy shell as the decoded voxels, 7 fields per voxel",
+                   "voxels": n, "triangles": nf,
+                   "l2": f"inputs {n * 40 / 1e6:.0f} MB, outputs {(n * 12 + nf * 12) / 1e6:.0f} MB per step "
+                         "(larger than L2)"},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": (ops.NBR_MAP_LAUNCHES + 3) * args.steps, "clocks": sampler.summary(),
+    }
+    print(json.dumps(line))
+    return 0
+
+
 # ----------------------------------------------------------------------------- decoder UNet
 DEC_METRIC = ("output voxels/s through the sparse decoder UNet (from_latent, 4 stages of ConvNeXt blocks + C2S "
               "up-blocks, LayerNorm + output_layer), res-32 shell -> res 512")
@@ -817,16 +938,16 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--workload", default=WORKLOAD, choices=["c4", "c4s"],
                     help="c4 (default, the benchmark) or c4s (half scale, for profiler captures)")
-    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s", "decode"],
+    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s", "decode", "mesh"],
                     help="stack (default, the benchmark: map + conv x2), convnext (one ConvNeXt block), c2s "
-                         "(one C2S up-block) or decode (the sparse decoder UNet)")
+                         "(one C2S up-block), decode (the sparse decoder UNet) or mesh (dual_grid_to_mesh)")
     args = ap.parse_args()
-    if args.op in ("convnext", "c2s", "decode"):
+    if args.op in ("convnext", "c2s", "decode", "mesh"):
         if args.impl == "reference" or args.gpus != 1:
             print(json.dumps({"impl": args.impl, "unavailable": f"--op {args.op} is a single-GPU measurement of "
                               "our kernels; its CPU baseline is in the line's cpu_baseline"}))
             return 0
-        return {"convnext": run_convnext, "c2s": run_c2s, "decode": run_decode}[args.op](args)
+        return {"convnext": run_convnext, "c2s": run_c2s, "decode": run_decode, "mesh": run_mesh}[args.op](args)
     if args.impl == "reference":
         return run_reference(args)
     return run_gpu(args)

@@ -165,6 +165,22 @@ typedef enum tb_conv_path {
 } tb_conv_path;
 tb_status tb_ctx_set_conv_path(tb_ctx* ctx, tb_conv_path path);
 
+/* ---- dual-grid mesh extraction (trellis::dual_grid_to_mesh, src/dual_grid.cpp:16-56) ------
+ * The decoder head's 7 fields per voxel become a triangle mesh. coords: int32
+ * [n][coord_stride] (x,y,z), or (b,x,y,z) with the batch folded into the key as in the
+ * neighbor map; feats7: float32 [n][7] (ggml's [7, n]): vertex-offset logits (0-2), the
+ * intersected logits of the x, y, z edges (3-5), the split-weight logit (6). All device.
+ * verts: float32 [n][3] = (coord + 2 sigmoid(f) - 0.5) * (1 / res) - 0.5 per axis.
+ * faces: int32 [max_faces][3] (8-byte aligned): for voxel i ascending and axis x, y, z, when
+ * the logit is not <= 0 and the voxel and its three edge neighbours all exist (a later
+ * duplicate coordinate wins), the quad's two triangles, split along the diagonal whose
+ * corners have the larger product of softplus weights (the 1-3 diagonal on ties).
+ * *f_out (host) = F, the triangle count; the call synchronises. TB_ERR_TOO_LARGE (F
+ * written, faces incomplete) when F > max_faces; 6n always suffices. res > 0. */
+tb_status tb_dual_grid_mesh(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord_stride,
+                            const float* feats7, int res, float* verts, int32_t* faces,
+                            int64_t max_faces, int64_t* f_out);
+
 /* ---- subdivide and channel-to-spatial gather (sparse_c2s, src/sparse.cpp:172-336) -------
  * tb_subdivide replaces the host octant loop of src/sparse.cpp:205-222: for parent i
  * ascending and octant o ascending with mask[o + 8i] != 0, emit the child

@@ -13,6 +13,7 @@
 //                          tensors on the device, looked up by the reference's names; its
 //                          conv(), convnext() and c2s() give the weights of a block prefix
 //   read_slat              the hr_slat.bin decode input of src/decode_replay.cpp:19-28
+//   dual_grid_to_mesh      src/dual_grid.cpp:16-56, the decoder head's fields to a mesh
 //   shape_decode, shape_upsample, tex_decode
 //                          include/shape_decoder.h: decode_unet (src/shape_decoder.cpp:79-138),
 //                          every stage on the device
@@ -173,5 +174,18 @@ std::vector<std::array<int, 3>> shape_upsample(const GgufModel& m, const std::ve
 std::vector<float> tex_decode(const GgufModel& m, const std::vector<float>& tex_latent,
                               const std::vector<std::array<int, 3>>& coords0,
                               const std::vector<std::vector<uint8_t>>& subs);
+
+// The reference's Mesh (include/dual_grid.h): verts [V*3] float32, faces [F*3] int32.
+struct Mesh {
+    std::vector<float> verts;
+    std::vector<int32_t> faces;
+    int V() const { return (int)verts.size() / 3; }
+    int F() const { return (int)faces.size() / 3; }
+};
+
+// dual_grid_to_mesh (src/dual_grid.cpp:16-56) on the device: one dual vertex per voxel in the
+// world cube [-0.5, 0.5]^3 and two triangles per intersected edge whose four voxels exist, in
+// the reference's order (tb_dual_grid_mesh).
+Mesh dual_grid_to_mesh(const ShapeOut& so);
 
 }  // namespace trellis

@@ -15,6 +15,9 @@ Functions and the reference lines they follow (paths inside pwilkin/trellis.cpp)
 * :func:`c2s_gather` -- ``src/sparse.cpp:263-266,288``
 * :func:`c2s_block` -- the whole ``sparse_c2s`` data flow, ``src/sparse.cpp:172-336``
   (LayerNorm/SiLU in numpy, convs through the C restatement)
+* :func:`dual_grid_mesh` -- ``src/dual_grid.cpp:16-56``
+* :func:`ref_dual_grid_mesh` -- the reference's own ``dual_grid_to_mesh``, compiled from its
+  sources into ``oracle/_ref/`` (only where those sources were present at build time)
 """
 from __future__ import annotations
 
@@ -26,7 +29,9 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _SO = os.path.join(_HERE, "liboracle.so")
+REF_MESH_SO = os.path.join(_HERE, "_ref", "libref_dual_grid.so")
 _lib = None
+_ref_mesh = None
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _u8p = ctypes.POINTER(ctypes.c_uint8)
@@ -73,6 +78,8 @@ def lib():
         L.orc_c2s_gather.argtypes = [_f32p, _i32p, ctypes.c_int64, ctypes.c_int, _f32p]
         L.orc_count_valid.restype = ctypes.c_int64
         L.orc_count_valid.argtypes = [_i32p, ctypes.c_int64]
+        L.orc_dual_grid_mesh.restype = ctypes.c_int64
+        L.orc_dual_grid_mesh.argtypes = [_i32p, ctypes.c_int64, _f32p, ctypes.c_int, _f32p, _i32p, _f32p]
         _lib = L
     return _lib
 
@@ -256,3 +263,42 @@ def c2s_block(coords, feats, w, cout, ext_mask=None):
     xs = c2s_gather(feats, gidx, k)                                          # :307
     o = o + np.repeat(xs.astype(np.float64), cout // k, axis=1)              # :322-323
     return o, child, mask
+
+
+def dual_grid_mesh(coords: np.ndarray, feats7: np.ndarray, res: int):
+    """``dual_grid_to_mesh`` (``src/dual_grid.cpp:16-56``): returns (verts [N,3] f32, faces
+    [F,3] int32, gap [F/2] f32), gap = the relative margin of each quad's split decision."""
+    c = np.ascontiguousarray(coords, dtype=np.int32)
+    f7 = np.ascontiguousarray(feats7, dtype=np.float32)
+    n = c.shape[0]
+    assert c.shape == (n, 3) and f7.shape == (n, 7)
+    verts = np.empty((n, 3), dtype=np.float32)
+    faces = np.empty((6 * n, 3), dtype=np.int32)
+    gap = np.empty(3 * n, dtype=np.float32)
+    f = lib().orc_dual_grid_mesh(_p(c, _i32p), n, _p(f7, _f32p), res, _p(verts, _f32p), _p(faces, _i32p),
+                                 _p(gap, _f32p))
+    if f < 0:
+        raise MemoryError("orc_dual_grid_mesh: allocation failed")
+    return verts, faces[:f].copy(), gap[:f // 2].copy()
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_MESH_SO)
+
+
+def ref_dual_grid_mesh(coords: np.ndarray, feats7: np.ndarray, res: int):
+    """The reference's own ``trellis::dual_grid_to_mesh`` (``oracle/_ref``): (verts, faces)."""
+    global _ref_mesh
+    if _ref_mesh is None:
+        L = ctypes.CDLL(REF_MESH_SO)
+        L.ref_dual_grid_mesh.restype = ctypes.c_int64
+        L.ref_dual_grid_mesh.argtypes = [_i32p, ctypes.c_int64, _f32p, ctypes.c_int, _f32p, _i32p, ctypes.c_int64]
+        _ref_mesh = L
+    c = np.ascontiguousarray(coords, dtype=np.int32)
+    f7 = np.ascontiguousarray(feats7, dtype=np.float32)
+    n = c.shape[0]
+    verts = np.empty((n, 3), dtype=np.float32)
+    faces = np.empty((6 * n, 3), dtype=np.int32)
+    f = _ref_mesh.ref_dual_grid_mesh(_p(c, _i32p), n, _p(f7, _f32p), res, _p(verts, _f32p), _p(faces, _i32p),
+                                     6 * n)
+    return verts, faces[:f].copy()

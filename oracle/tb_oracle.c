@@ -17,6 +17,7 @@
  *   orc_submconv_f32_mt        same, fp32, threads over voxel blocks (the CPU baseline)
  *   orc_subdivide              src/sparse.cpp:205-222   octant loop, child coords, gidx
  *   orc_c2s_gather             src/sparse.cpp:263-266,288  child takes channel block o
+ *   orc_dual_grid_mesh         src/dual_grid.cpp:16-56  dual vertices, quad lookup, split
  *
  * Parity pin: tests/golden/make_golden.py runs the reference's own torch restatements
  * (tools/ref_sparse_conv.py:47-67, tools/ref_c2s.py:38-79) on seeded inputs and commits
@@ -278,4 +279,69 @@ int64_t orc_count_valid(const int32_t* nbr, int64_t n) {
     int64_t p = 0;
     for (int64_t k = 0; k < 27 * n; ++k) p += (nbr[k] != (int32_t)n);
     return p;
+}
+
+/* ---- dual_grid_to_mesh: src/dual_grid.cpp:16-56 ------------------------------------------
+ * f7 [N][7] fp32 per voxel (ggml's [7, N]): channels 0-2 vertex-offset logits, 3-5 the
+ * intersected logits of the x, y, z edges, 6 the split-weight logit.
+ *   verts[i][a] = ((float)coord[i][a] + (2 sigmoid(f7[i][a]) - 0.5)) * (1 / res) - 0.5
+ * For voxel i ascending and axis a ascending, when f7[i][3+a] is not <= 0 and the four voxels
+ * coord[i] + ORC_EDGE_OFF[a][k] are all present (rows q0..q3; a later duplicate wins), two
+ * triangles: {q0,q1,q2, q0,q2,q3} when softplus(f7[q0][6]) softplus(f7[q2][6]) >
+ * softplus(f7[q1][6]) softplus(f7[q3][6]), else {q0,q1,q3, q3,q1,q2}.
+ * coords [N][3]; verts [N][3]; faces: room for 6N triangles (18N int32). gap (may be NULL):
+ * per emitted quad, |w02 - w13| / max(w02, w13), the margin of its split decision. Returns
+ * the triangle count F, or -1 on a failed allocation. */
+static const int ORC_EDGE_OFF[3][4][3] = {   /* the quad around each edge axis (o_voxel's table) */
+    {{0, 0, 0}, {0, 0, 1}, {0, 1, 1}, {0, 1, 0}},
+    {{0, 0, 0}, {1, 0, 0}, {1, 0, 1}, {0, 0, 1}},
+    {{0, 0, 0}, {0, 1, 0}, {1, 1, 0}, {1, 0, 0}},
+};
+
+static float orc_sigmoidf(float x) { return 1.0f / (1.0f + expf(-x)); }
+static float orc_softplusf(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+int64_t orc_dual_grid_mesh(const int32_t* coords, int64_t n, const float* f7, int res, float* verts,
+                           int32_t* faces, float* gap) {
+    const float vs = 1.0f / (float)res, org = -0.5f;
+    for (int64_t i = 0; i < n; ++i)
+        for (int a = 0; a < 3; ++a) {
+            const float dv = 2.0f * orc_sigmoidf(f7[7 * i + a]) - 0.5f;
+            verts[3 * i + a] = ((float)coords[3 * i + a] + dv) * vs + org;
+        }
+    if (n == 0) return 0;
+    orc_map m;
+    if (orc_map_init(&m, n)) { orc_map_free(&m); return -1; }
+    for (int64_t i = 0; i < n; ++i) orc_map_put(&m, orc_key_row(coords + 3 * i, 3, 0, 0, 0), (int32_t)i);
+    int64_t f = 0, quad = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t* c = coords + 3 * i;
+        for (int a = 0; a < 3; ++a) {
+            if (f7[7 * i + 3 + a] <= 0.0f) continue;
+            int32_t q[4];
+            int ok = 1;
+            for (int k = 0; k < 4 && ok; ++k) {
+                q[k] = orc_map_get(&m, orc_key_row(c, 3, ORC_EDGE_OFF[a][k][0], ORC_EDGE_OFF[a][k][1],
+                                                   ORC_EDGE_OFF[a][k][2]), -1);
+                ok = q[k] >= 0;
+            }
+            if (!ok) continue;
+            const float w02 = orc_softplusf(f7[7 * (int64_t)q[0] + 6]) * orc_softplusf(f7[7 * (int64_t)q[2] + 6]);
+            const float w13 = orc_softplusf(f7[7 * (int64_t)q[1] + 6]) * orc_softplusf(f7[7 * (int64_t)q[3] + 6]);
+            int32_t* t = faces + 3 * f;
+            if (w02 > w13) {
+                t[0] = q[0]; t[1] = q[1]; t[2] = q[2]; t[3] = q[0]; t[4] = q[2]; t[5] = q[3];
+            } else {
+                t[0] = q[0]; t[1] = q[1]; t[2] = q[3]; t[3] = q[3]; t[4] = q[1]; t[5] = q[2];
+            }
+            if (gap) {
+                const float hi = w02 > w13 ? w02 : w13;
+                gap[quad] = hi > 0.0f ? fabsf(w02 - w13) / hi : 0.0f;
+            }
+            f += 2;
+            ++quad;
+        }
+    }
+    orc_map_free(&m);
+    return f;
 }

@@ -19,9 +19,9 @@ statements. What it writes:
   negative, a dense 3^3 block, an isolated voxel, and one voxel.
 
 Weights are drawn as bf16-representable float32 values, so the same fixture also serves
-the bf16 operand mode exactly. Run it in a container that has the reference at
-``$TRELLIS_REF`` (default ``/root/reference``). The GPU box never runs it: tests read
-only the .npz files.
+the bf16 operand mode exactly. Run it where the reference project is present, at
+``$TRELLIS_REF`` (default: a ``reference`` directory beside this repository). The GPU box
+never runs it: tests read only the .npz files.
 """
 from __future__ import annotations
 
@@ -33,8 +33,8 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
-REF = os.environ.get("TRELLIS_REF", "/root/reference")
 HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("TRELLIS_REF", os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))), "reference"))
 
 
 def _bf16_exact(t: torch.Tensor) -> torch.Tensor:

@@ -53,6 +53,7 @@ SIGNATURES = {
     "tb_submconv_range": (_st, [_vp, _vp, _i64, _i64, _i64, _vp, _int, _vp, _vp, _int, _int, _int, _int, _vp]),
     "tb_subdivide": (_st, [_vp, _vp, _i64, _int, _vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64)]),
     "tb_c2s_gather": (_st, [_vp, _vp, _vp, _i64, _int, _int, _vp]),
+    "tb_dual_grid_mesh": (_st, [_vp, _vp, _i64, _int, _vp, _int, _vp, _vp, _i64, ctypes.POINTER(_i64)]),
     "tb_bias_act": (_st, [_vp, _vp, _i64, _int, _vp, _int, _int]),
     "tb_submconv_stack_host": (_st, [_vp, _vp, _i64, _int, _vp, ctypes.POINTER(ConvLayer), _int, _int,
                                      _int, _vp]),

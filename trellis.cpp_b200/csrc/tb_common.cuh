@@ -92,6 +92,15 @@ tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int s
                             int32_t* nbr, void* table, uint64_t cap, const int* gate);
 tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws);
 size_t tb_nbr_workspace_bytes(int64_t n);
+// The seven neighbor offsets in {0,1}^3 other than (1,1,1), the corners of the dual-grid quads,
+// as taps of the map (tap = kd*9 + kh*3 + kw): slot j = (dx,dy,dz)
+//   0 (0,0,0)  1 (0,0,1)  2 (0,1,0)  3 (0,1,1)  4 (1,0,0)  5 (1,0,1)  6 (1,1,0)
+__host__ __device__ constexpr int tb_quad_tap(int j) {
+    return j == 0 ? 13 : j == 1 ? 14 : j == 2 ? 16 : j == 3 ? 17 : j == 4 ? 22 : j == 5 ? 23 : 25;
+}
+// Those seven taps of the map: out[j*n + i] = row of coords[i] + slot j's offset, or n when
+// absent; the same table and lookups as the 27-tap map. ws: tb_nbr_workspace_bytes(n).
+tb_status tb_nbr_build_quad_taps(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* out, void* ws);
 tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
                             const void* feats, int ci, const void* weight, const float* bias, int co,
                             tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);

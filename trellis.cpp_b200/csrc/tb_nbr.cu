@@ -93,6 +93,17 @@ __device__ __forceinline__ int lookup(const Slot* __restrict__ t, uint64_t mask,
     return absent;
 }
 
+// The taps a lookup writes: all 27 (NT = 27, out[tap * N + i]) or the seven quad-corner taps of
+// the dual-grid mesh (NT = 7, out[j * N + i] for tap tb_quad_tap(j)). Both lists are known at
+// compile time, so the per-tap index arithmetic folds into constants.
+template <int NT>
+__device__ __forceinline__ constexpr int tap_at(int j) {
+    static_assert(NT == 27 || NT == 7, "tap set");
+    if constexpr (NT == 27) return j;
+    else return tb_quad_tap(j);
+}
+
+template <int NT>
 __global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int stride,
                              const Slot* __restrict__ t, uint64_t mask,
                              const int* __restrict__ special_p, int32_t* __restrict__ nbr,
@@ -103,10 +114,11 @@ __global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int 
         int32_t c[4];
         for (int d = 0; d < stride; ++d) c[d] = coords[i * stride + d];
 #pragma unroll
-        for (int tap = 0; tap < 27; ++tap) {
+        for (int j = 0; j < NT; ++j) {
+            const int tap = tap_at<NT>(j);
             const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
             const uint64_t k = key_of(c, stride, kd - 1, kh - 1, kw - 1);
-            nbr[(int64_t)tap * n + i] = lookup(t, mask, special, k, (int)n, err);
+            nbr[(int64_t)j * n + i] = lookup(t, mask, special, k, (int)n, err);
         }
     }
 }
@@ -173,22 +185,36 @@ __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int 
     // consecutive voxels mostly share a block: one lane per distinct block of the warp claims it
     const uint64_t k = valid ? block_key(b, x >> 2, y >> 2, z >> 2) : (kEmpty - (uint64_t)lane);
     const unsigned same = __match_any_sync(0xffffffffu, k);
-    if (!valid || (same & ((1u << lane) - 1u)) != 0) return;
-    // the table holds twice the buckets; a probe run this long means far more blocks than
-    // buckets (the table filling up), so the voxel hash builds the map
-    uint64_t h = block_slot(b, x >> 2, y >> 2, z >> 2, mask);
-    for (int probe = 0; probe < 64; ++probe) {
-        const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
-        if (prev == kEmpty) {
-            const unsigned int id = atomicAdd(&ctl->nblocks, 1u);
-            if (id >= pool_blocks) ctl->fallback = 1;
-            t[h].row = (int)id;
-            return;
+    bool claimed = false;
+    uint64_t h = 0;
+    if (valid && (same & ((1u << lane) - 1u)) == 0) {
+        // the table holds twice the buckets; a probe run this long means far more blocks than
+        // buckets (the table filling up), so the voxel hash builds the map
+        h = block_slot(b, x >> 2, y >> 2, z >> 2, mask);
+        int probe = 0;
+        for (; probe < 64; ++probe) {
+            const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
+            if (prev == kEmpty) {
+                claimed = true;
+                break;
+            }
+            if (prev == k) break;
+            h = (h + 1) & mask;
         }
-        if (prev == k) return;
-        h = (h + 1) & mask;
+        if (probe == 64) ctl->fallback = 1;
     }
-    ctl->fallback = 1;
+    // bucket ids for the blocks this warp claimed: one counter update per warp
+    const unsigned cm = __ballot_sync(0xffffffffu, claimed);
+    if (cm == 0) return;
+    const int first = __ffs(cm) - 1;
+    unsigned int base = 0;
+    if (lane == first) base = atomicAdd(&ctl->nblocks, (unsigned int)__popc(cm));
+    base = __shfl_sync(0xffffffffu, base, first);
+    if (claimed) {
+        const unsigned int id = base + (unsigned int)__popc(cm & ((1u << lane) - 1u));
+        if (id >= pool_blocks) ctl->fallback = 1;
+        t[h].row = (int)id;
+    }
 }
 
 __global__ void k_pool_clear(int32_t* __restrict__ pool, const BlockCtl* __restrict__ ctl) {
@@ -212,14 +238,20 @@ __global__ void k_vox_insert(const int32_t* __restrict__ coords, int64_t n, int 
     atomicMax(&pool[(int64_t)bucket * 64 + (((x & 3) << 4) | ((y & 3) << 2) | (z & 3))], (int32_t)i);
 }
 
+constexpr int kLookupThreads = 256;    // block size of k_blk_lookup (its shared-memory table)
+
 // 27 lookups per voxel. Per axis the taps reach at most one block besides the voxel's own (the
-// one below at position 0, above at position 3), so the up to 8 blocks are looked up once and
-// each tap picks one with three predicates fixed per voxel.
-__global__ void k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t,
-                             uint64_t mask, const BlockCtl* __restrict__ ctl, const int32_t* __restrict__ pool,
-                             int32_t* __restrict__ nbr) {
+// one below at position 0, above at position 3), so the up to 8 blocks are looked up once. Their
+// bucket bases go to shared memory (a column per thread, so reads never conflict), and each tap
+// reads the one its three "leaves the block" bits select instead of a select tree over eight
+// registers.
+template <int NT>
+__global__ void __launch_bounds__(kLookupThreads)
+k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t, uint64_t mask,
+             const BlockCtl* __restrict__ ctl, const int32_t* __restrict__ pool, int32_t* __restrict__ nbr) {
+    __shared__ int s_base[8][kLookupThreads];
     if (ctl->fallback) return;
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t i = blockIdx.x * (int64_t)kLookupThreads + threadIdx.x;
     if (i >= n) return;
     int32_t b, x, y, z;
     read_coords(coords + i * stride, stride, b, x, y, z);
@@ -228,8 +260,7 @@ __global__ void k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int 
     const int ox = lx == 0 ? -1 : (lx == 3 ? 1 : 0);
     const int oy = ly == 0 ? -1 : (ly == 3 ? 1 : 0);
     const int oz = lz == 0 ? -1 : (lz == 3 ? 1 : 0);
-    // bucket base (bucket * 64) of block own + (ax ? ox : 0, ay ? oy : 0, az ? oz : 0), or -1
-    int base[8];
+    // s_base[m] = bucket base (bucket * 64) of block own + (ax ? ox : 0, ay ? oy : 0, az ? oz : 0), or -1
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
         const int ax = (m >> 2) & 1, ay = (m >> 1) & 1, az = m & 1;
@@ -237,24 +268,24 @@ __global__ void k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int 
         const int32_t cx = bx + (ax ? ox : 0), cy = by + (ay ? oy : 0), cz = bz + (az ? oz : 0);
         int bucket = -1;
         if (need && cx >= 0 && cy >= 0 && cz >= 0) bucket = block_find(t, mask, b, cx, cy, cz);
-        base[m] = bucket >= 0 ? bucket * 64 : -1;
+        s_base[m][threadIdx.x] = bucket >= 0 ? bucket * 64 : -1;
     }
-    // per axis and offset d: does x + d leave the block
-    const bool xm = lx == 0, xp = lx == 3, ym = ly == 0, yp = ly == 3, zm = lz == 0, zp = lz == 3;
+    // per axis and offset d in {-1, 0, +1}: the block-select bit (x + d leaves the block) and the
+    // position in the block, pre-shifted into the bucket index
+    const int mx[3] = {lx == 0 ? 4 : 0, 0, lx == 3 ? 4 : 0};
+    const int my[3] = {ly == 0 ? 2 : 0, 0, ly == 3 ? 2 : 0};
+    const int mz[3] = {lz == 0 ? 1 : 0, 0, lz == 3 ? 1 : 0};
+    const int px[3] = {((lx - 1) & 3) << 4, lx << 4, ((lx + 1) & 3) << 4};
+    const int py[3] = {((ly - 1) & 3) << 2, ly << 2, ((ly + 1) & 3) << 2};
+    const int pz[3] = {(lz - 1) & 3, lz, (lz + 1) & 3};
 #pragma unroll
-    for (int tap = 0; tap < 27; ++tap) {
-        const int dx = tap / 9 - 1, dy = (tap / 3) % 3 - 1, dz = tap % 3 - 1;
-        const bool ax = dx < 0 ? xm : (dx > 0 ? xp : false);
-        const bool ay = dy < 0 ? ym : (dy > 0 ? yp : false);
-        const bool az = dz < 0 ? zm : (dz > 0 ? zp : false);
-        const int b01 = az ? base[1] : base[0], b23 = az ? base[3] : base[2];
-        const int b45 = az ? base[5] : base[4], b67 = az ? base[7] : base[6];
-        const int blo = ay ? b23 : b01, bhi = ay ? b67 : b45;
-        const int bb = ax ? bhi : blo;
-        const int loc = (((lx + dx) & 3) << 4) | (((ly + dy) & 3) << 2) | ((lz + dz) & 3);
+    for (int j = 0; j < NT; ++j) {
+        const int tap = tap_at<NT>(j);
+        const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+        const int bb = s_base[mx[kd] | my[kh] | mz[kw]][threadIdx.x];
         int32_t r = -1;
-        if (bb >= 0) r = __ldg(pool + bb + loc);
-        nbr[(int64_t)tap * n + i] = r >= 0 ? r : (int32_t)n;
+        if (bb >= 0) r = __ldg(pool + bb + (px[kd] | py[kh] | pz[kw]));
+        nbr[(int64_t)j * n + i] = r >= 0 ? r : (int32_t)n;
     }
 }
 
@@ -324,8 +355,11 @@ uint64_t tb_hash_capacity(int64_t n) {
 
 // `table` holds cap Slots followed by one int (the all-ones key cell); 16*cap + 16 bytes.
 // `gate` (may be null) skips the build when it points at 0.
-tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride,
-                            int32_t* nbr, void* table, uint64_t cap, const int* gate) {
+namespace {
+
+template <int NT>
+tb_status nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* table,
+                         uint64_t cap, const int* gate) {
     Slot* t = reinterpret_cast<Slot*>(table);
     int* special = reinterpret_cast<int*>(t + cap);
     const uint64_t mask = cap - 1;
@@ -337,9 +371,17 @@ tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int s
     const int64_t blocks = std::min<int64_t>((n + tpb - 1) / tpb, (int64_t)ctx->num_sms * 16);
     k_hash_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, ctx->d_err, gate);
     TB_LAUNCH_CHECK(ctx, "k_hash_insert");
-    k_nbr_lookup<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, nbr, ctx->d_err, gate);
+    k_nbr_lookup<NT><<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, nbr, ctx->d_err,
+                                                                 gate);
     TB_LAUNCH_CHECK(ctx, "k_nbr_lookup");
     return TB_OK;
+}
+
+}  // namespace
+
+tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride,
+                            int32_t* nbr, void* table, uint64_t cap, const int* gate) {
+    return nbr_build_impl<27>(ctx, coords, n, stride, nbr, table, cap, gate);
 }
 
 // Buckets for at most N/4 + 64 blocks, and fewer than 2^25 so a bucket's first entry index
@@ -353,9 +395,12 @@ size_t tb_nbr_workspace_bytes(int64_t n) {
     return cap * sizeof(Slot) + 16 + sizeof(BlockCtl) + tb_nbr_pool_blocks(n) * 64 * sizeof(int32_t);
 }
 
+namespace {
+
 // Block layout first; its kernels and the voxel-hash kernels read BlockCtl::fallback, so
 // exactly one of the two writes the map.
-tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws) {
+template <int NT>
+tb_status nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws) {
     const uint64_t cap = tb_hash_capacity(n);                   // voxel-hash table (fallback)
     const uint64_t pool_blocks = tb_nbr_pool_blocks(n);
     const uint64_t cap_b = tb_hash_capacity((int64_t)pool_blocks);   // block table, a prefix of it
@@ -376,10 +421,21 @@ tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int
     TB_LAUNCH_CHECK(ctx, "k_pool_clear");
     k_vox_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool);
     TB_LAUNCH_CHECK(ctx, "k_vox_insert");
-    k_blk_lookup<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool, nbr);
+    static_assert(kLookupThreads == 256, "k_blk_lookup runs with the builder's block size");
+    k_blk_lookup<NT><<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool, nbr);
     TB_LAUNCH_CHECK(ctx, "k_blk_lookup");
     // voxel hash, run only when the block layout did not apply
-    return tb_nbr_build_impl(ctx, coords, n, stride, nbr, ws, cap, &ctl->fallback);
+    return nbr_build_impl<NT>(ctx, coords, n, stride, nbr, ws, cap, &ctl->fallback);
+}
+
+}  // namespace
+
+tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws) {
+    return nbr_build_blocks<27>(ctx, coords, n, stride, nbr, ws);
+}
+
+tb_status tb_nbr_build_quad_taps(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* out, void* ws) {
+    return nbr_build_blocks<7>(ctx, coords, n, stride, out, ws);
 }
 
 extern "C" tb_status tb_build_neighbor_map(tb_ctx* ctx, const int32_t* coords, int64_t n,
@@ -517,6 +573,7 @@ extern "C" tb_status tb_build_neighbor_map_noalloc(void* stream, const int32_t* 
     k_hash_clear<<<clear_blocks, tpb, 0, st>>>(t, cap, special, nullptr);
     const int64_t blocks = (n + tpb - 1) / tpb;
     k_hash_insert<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, err, nullptr);
-    k_nbr_lookup<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, nbr_out, err, nullptr);
+    k_nbr_lookup<27><<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, nbr_out, err,
+                                                      nullptr);
     return cudaGetLastError() == cudaSuccess ? TB_OK : TB_ERR_CUDA;
 }

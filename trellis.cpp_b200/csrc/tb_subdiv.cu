@@ -7,6 +7,7 @@
 // sequential loop. Three kernels: per-block counts, a scan of the block totals, then each
 // block rescans its parents and writes children.
 #include "tb_common.cuh"
+#include "tb_scan.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -34,32 +35,8 @@ __device__ __forceinline__ uint32_t parent_bits(const uint8_t* __restrict__ mask
     return b;
 }
 
-// Exclusive scan of one value per thread across the block; returns the block total too.
 __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, int64_t* total) {
-    __shared__ int64_t warp_sums[kSubThreads / 32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int64_t x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) warp_sums[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        int64_t s = lane < kSubThreads / 32 ? warp_sums[lane] : 0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int64_t y = __shfl_up_sync(0xffffffffu, s, o);
-            if (lane >= o) s += y;
-        }
-        if (lane < kSubThreads / 32) warp_sums[lane] = s;   // inclusive
-    }
-    __syncthreads();
-    const int64_t warp_off = warp > 0 ? warp_sums[warp - 1] : 0;
-    *total = warp_sums[kSubThreads / 32 - 1];
-    __syncthreads();
-    return warp_off + x - v;
+    return tb_scan::block_exclusive_scan<kSubThreads>(v, total);
 }
 
 __global__ void k_sub_count(const uint8_t* __restrict__ mask, int64_t n, int64_t* __restrict__ block_sums) {
@@ -71,31 +48,6 @@ __global__ void k_sub_count(const uint8_t* __restrict__ mask, int64_t n, int64_t
     int64_t total;
     block_exclusive_scan(c, &total);
     if (threadIdx.x == 0) block_sums[blockIdx.x] = total;
-}
-
-// Single block: exclusive scan of nb block totals in place; writes the grand total.
-__global__ void k_sub_scan_blocks(int64_t* __restrict__ sums, int64_t nb, int64_t* __restrict__ grand) {
-    int64_t carry = 0;
-    for (int64_t base = 0; base < nb; base += (int64_t)kSubThreads * kPerThread) {
-        int64_t v[kPerThread];
-        int64_t s = 0;
-#pragma unroll
-        for (int j = 0; j < kPerThread; ++j) {
-            const int64_t k = base + (int64_t)threadIdx.x * kPerThread + j;
-            v[j] = k < nb ? sums[k] : 0;
-            s += v[j];
-        }
-        int64_t total;
-        int64_t off = block_exclusive_scan(s, &total) + carry;
-#pragma unroll
-        for (int j = 0; j < kPerThread; ++j) {
-            const int64_t k = base + (int64_t)threadIdx.x * kPerThread + j;
-            if (k < nb) sums[k] = off;
-            off += v[j];
-        }
-        carry += total;
-    }
-    if (threadIdx.x == 0) *grand = carry;
 }
 
 __global__ void k_sub_emit(const int32_t* __restrict__ coords, int64_t n, int stride,
@@ -198,8 +150,8 @@ extern "C" tb_status tb_subdivide(tb_ctx* ctx, const int32_t* coords, int64_t n,
     int64_t* grand = sums + nb;
     k_sub_count<<<(unsigned)nb, kSubThreads, 0, ctx->stream>>>(mask, n, sums);
     TB_LAUNCH_CHECK(ctx, "k_sub_count");
-    k_sub_scan_blocks<<<1, kSubThreads, 0, ctx->stream>>>(sums, nb, grand);
-    TB_LAUNCH_CHECK(ctx, "k_sub_scan_blocks");
+    tb_scan::k_scan_block_totals<kSubThreads, kPerThread><<<1, kSubThreads, 0, ctx->stream>>>(sums, nb, grand);
+    TB_LAUNCH_CHECK(ctx, "k_scan_block_totals");
     k_sub_emit<<<(unsigned)nb, kSubThreads, 0, ctx->stream>>>(coords, n, coord_stride, mask, sums, child_coords,
                                                               gidx, mstart, max_children);
     TB_LAUNCH_CHECK(ctx, "k_sub_emit");

@@ -179,6 +179,25 @@ SubdivideResult subdivide(const std::vector<std::array<int, 3>>& coords, const s
     return r;
 }
 
+Mesh dual_grid_to_mesh(const ShapeOut& so) {
+    const int64_t n = (int64_t)so.coords.size();
+    if ((int64_t)so.feats7.size() != 7 * n) throw std::runtime_error("trellis: dual_grid_to_mesh: feats7 must have 7*M entries");
+    Mesh mesh;
+    if (n == 0) return mesh;
+    cuda_ok(cudaSetDevice(g_device), "cudaSetDevice");
+    DBuf dc((size_t)n * 12), df((size_t)n * 28), dv((size_t)n * 12), dfa((size_t)n * 72);
+    cuda_ok(cudaMemcpy(dc.p, so.coords.data(), (size_t)n * 12, cudaMemcpyHostToDevice), "upload coords");
+    cuda_ok(cudaMemcpy(df.p, so.feats7.data(), (size_t)n * 28, cudaMemcpyHostToDevice), "upload feats7");
+    int64_t f = 0;
+    ok(tb_dual_grid_mesh(ctx(), dc.as<int32_t>(), n, 3, df.as<float>(), so.res, dv.as<float>(), dfa.as<int32_t>(),
+                         6 * n, &f), "tb_dual_grid_mesh");
+    mesh.verts.resize((size_t)n * 3);
+    mesh.faces.resize((size_t)f * 3);
+    cuda_ok(cudaMemcpy(mesh.verts.data(), dv.p, (size_t)n * 12, cudaMemcpyDeviceToHost), "download verts");
+    if (f > 0) cuda_ok(cudaMemcpy(mesh.faces.data(), dfa.p, (size_t)f * 12, cudaMemcpyDeviceToHost), "download faces");
+    return mesh;
+}
+
 C2SResult sparse_c2s(const C2SWeights& w, const std::vector<float>& feats_in, int Cin,
                      const std::vector<std::array<int, 3>>& coords, int Cout,
                      const std::vector<uint8_t>* ext_subdiv) {

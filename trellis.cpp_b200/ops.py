@@ -213,6 +213,26 @@ def subdivide(coords: torch.Tensor, mask: torch.Tensor, max_children: int | None
     return child[: m.value], gidx[: m.value], mstart
 
 
+def dual_grid_mesh(coords: torch.Tensor, feats7: torch.Tensor, res: int, max_faces: int | None = None):
+    """trellis::dual_grid_to_mesh (src/dual_grid.cpp:16-56) on the device: (verts [N,3] float32,
+    faces [F,3] int32) from int32 coords [N,3|4] and the decoder head's float32 [N,7] fields."""
+    _need_cuda(coords, feats7)
+    if coords.dtype != torch.int32 or coords.dim() != 2 or coords.shape[1] not in (3, 4):
+        raise ValueError("coords must be int32 [N,3] or [N,4]")
+    n, s = coords.shape
+    if feats7.dtype != torch.float32 or tuple(feats7.shape) != (n, 7):
+        raise ValueError("feats7 must be a contiguous float32 [N, 7] tensor")
+    if max_faces is None:
+        max_faces = 6 * n
+    verts = torch.empty((n, 3), dtype=torch.float32, device=coords.device)
+    faces = torch.empty((max(max_faces, 1), 3), dtype=torch.int32, device=coords.device)
+    f = ctypes.c_int64()
+    ctx = context(coords.device)
+    check(_lib.load().tb_dual_grid_mesh(ctx, _ptr(coords), n, s, _ptr(feats7), int(res), _ptr(verts), _ptr(faces),
+                                        max_faces, ctypes.byref(f)), "tb_dual_grid_mesh", ctx)
+    return verts, faces[: f.value]
+
+
 def linear(a: torch.Tensor, w: torch.Tensor, bias=None, act: str = "none", residual=None, out_dtype=None,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """out = act(a @ w.T + bias) + residual (a [M,K], w [N,K] of a's dtype; bias float32 [N])."""
