@@ -148,15 +148,19 @@ __device__ __forceinline__ uint64_t block_slot(int32_t b, int32_t bx, int32_t by
 }
 
 // Bucket of the block (b, bx, by, bz), or -1 when the block holds no voxel.
-__device__ __forceinline__ int block_find(const Slot* __restrict__ t, uint64_t mask, int32_t b, int32_t bx,
-                                          int32_t by, int32_t bz) {
-    const uint64_t k = block_key(b, bx, by, bz);
-    uint64_t h = block_slot(b, bx, by, bz, mask);
+__device__ __forceinline__ ulonglong2 slot_at(const Slot* __restrict__ t, uint64_t h) {
+    return __ldg(reinterpret_cast<const ulonglong2*>(t) + h);
+}
+
+// Bucket of key k given its home slot h and that slot's contents s (loaded by the caller, so
+// that several first probes can be in flight together), or -1 when the block holds no voxel.
+__device__ __forceinline__ int block_resolve(const Slot* __restrict__ t, uint64_t mask, uint64_t k, uint64_t h,
+                                             ulonglong2 s) {
     for (uint64_t probe = 0; probe <= mask; ++probe) {
-        const ulonglong2 s = __ldg(reinterpret_cast<const ulonglong2*>(t) + h);
         if (s.x == k) return (int)(uint32_t)s.y;
         if (s.x == kEmpty) return -1;
         h = (h + 1) & mask;
+        s = slot_at(t, h);
     }
     return -1;
 }
@@ -166,54 +170,81 @@ __device__ __forceinline__ void read_coords(const int32_t* c, int stride, int32_
     else { b = 0; x = c[0]; y = c[1]; z = c[2]; }
 }
 
+constexpr int kInsPer = 4;      // voxels per thread in the insert kernels
+
 // Claims each voxel's block and hands the block a bucket; flags coordinates outside the range
-// where block lookup equals the reference's key lookup, and bucket overflow.
+// where block lookup equals the reference's key lookup, and bucket overflow. A warp takes
+// 32 * kInsPer consecutive voxels (group j = voxels j*32 .. j*32+31 of its range) and issues the
+// first claim attempt of every group before it waits on any: the kernel is bound by the latency
+// of these dependent round trips, not by bandwidth.
 __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int stride, Slot* __restrict__ t,
                              uint64_t mask, BlockCtl* __restrict__ ctl, unsigned int pool_blocks) {
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
-    int32_t b = 0, x = 0, y = 0, z = 0;
-    bool valid = i < n;
-    if (valid) {
-        read_coords(coords + i * stride, stride, b, x, y, z);
-        if ((uint32_t)x > (uint32_t)kMaxCoord || (uint32_t)y > (uint32_t)kMaxCoord ||
-            (uint32_t)z > (uint32_t)kMaxCoord || (uint32_t)b > 15u) {
-            ctl->fallback = 1;
-            valid = false;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * kInsPer;
+    uint64_t k[kInsPer], h[kInsPer];
+    bool lead[kInsPer];
+#pragma unroll
+    for (int j = 0; j < kInsPer; ++j) {
+        const int64_t i = warp0 + j * 32 + lane;
+        int32_t b = 0, x = 0, y = 0, z = 0;
+        bool valid = i < n;
+        if (valid) {
+            read_coords(coords + i * stride, stride, b, x, y, z);
+            if ((uint32_t)x > (uint32_t)kMaxCoord || (uint32_t)y > (uint32_t)kMaxCoord ||
+                (uint32_t)z > (uint32_t)kMaxCoord || (uint32_t)b > 15u) {
+                ctl->fallback = 1;
+                valid = false;
+            }
         }
+        // consecutive voxels mostly share a block: one lane per distinct block of the group claims it
+        k[j] = valid ? block_key(b, x >> 2, y >> 2, z >> 2) : (kEmpty - (uint64_t)lane);
+        const unsigned same = __match_any_sync(0xffffffffu, k[j]);
+        lead[j] = valid && (same & ((1u << lane) - 1u)) == 0;
+        h[j] = valid ? block_slot(b, x >> 2, y >> 2, z >> 2, mask) : 0;
     }
-    // consecutive voxels mostly share a block: one lane per distinct block of the warp claims it
-    const uint64_t k = valid ? block_key(b, x >> 2, y >> 2, z >> 2) : (kEmpty - (uint64_t)lane);
-    const unsigned same = __match_any_sync(0xffffffffu, k);
-    bool claimed = false;
-    uint64_t h = 0;
-    if (valid && (same & ((1u << lane) - 1u)) == 0) {
+    unsigned long long prev[kInsPer];
+#pragma unroll
+    for (int j = 0; j < kInsPer; ++j)
+        prev[j] = lead[j] ? atomicCAS(&t[h[j]].key, kEmpty, (unsigned long long)k[j]) : 0ull;
+    bool claimed[kInsPer];
+#pragma unroll
+    for (int j = 0; j < kInsPer; ++j) {
+        claimed[j] = false;
+        if (!lead[j]) continue;
         // the table holds twice the buckets; a probe run this long means far more blocks than
         // buckets (the table filling up), so the voxel hash builds the map
-        h = block_slot(b, x >> 2, y >> 2, z >> 2, mask);
         int probe = 0;
         for (; probe < 64; ++probe) {
-            const unsigned long long prev = atomicCAS(&t[h].key, kEmpty, (unsigned long long)k);
-            if (prev == kEmpty) {
-                claimed = true;
+            if (prev[j] == kEmpty) {
+                claimed[j] = true;
                 break;
             }
-            if (prev == k) break;
-            h = (h + 1) & mask;
+            if (prev[j] == k[j]) break;
+            h[j] = (h[j] + 1) & mask;
+            if (probe + 1 < 64) prev[j] = atomicCAS(&t[h[j]].key, kEmpty, (unsigned long long)k[j]);
         }
         if (probe == 64) ctl->fallback = 1;
     }
     // bucket ids for the blocks this warp claimed: one counter update per warp
-    const unsigned cm = __ballot_sync(0xffffffffu, claimed);
-    if (cm == 0) return;
-    const int first = __ffs(cm) - 1;
+    unsigned cm[kInsPer];
+    unsigned total = 0;
+#pragma unroll
+    for (int j = 0; j < kInsPer; ++j) {
+        cm[j] = __ballot_sync(0xffffffffu, claimed[j]);
+        total += (unsigned)__popc(cm[j]);
+    }
+    if (total == 0) return;
     unsigned int base = 0;
-    if (lane == first) base = atomicAdd(&ctl->nblocks, (unsigned int)__popc(cm));
-    base = __shfl_sync(0xffffffffu, base, first);
-    if (claimed) {
-        const unsigned int id = base + (unsigned int)__popc(cm & ((1u << lane) - 1u));
-        if (id >= pool_blocks) ctl->fallback = 1;
-        t[h].row = (int)id;
+    if (lane == 0) base = atomicAdd(&ctl->nblocks, total);
+    base = __shfl_sync(0xffffffffu, base, 0);
+#pragma unroll
+    for (int j = 0; j < kInsPer; ++j) {
+        if (claimed[j]) {
+            const unsigned int id = base + (unsigned int)__popc(cm[j] & ((1u << lane) - 1u));
+            if (id >= pool_blocks) ctl->fallback = 1;
+            t[h[j]].row = (int)id;
+        }
+        base += (unsigned)__popc(cm[j]);
     }
 }
 
@@ -226,16 +257,35 @@ __global__ void k_pool_clear(int32_t* __restrict__ pool, const BlockCtl* __restr
 }
 
 // The largest row index of each coordinate wins, as the reference's later insert overwrites.
+// Four voxels per thread (blockDim apart, so each load of a warp is coalesced); their first
+// table probes are in flight together.
 __global__ void k_vox_insert(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t,
                              uint64_t mask, const BlockCtl* __restrict__ ctl, int32_t* __restrict__ pool) {
     if (ctl->fallback) return;
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    int32_t b, x, y, z;
-    read_coords(coords + i * stride, stride, b, x, y, z);
-    const int bucket = block_find(t, mask, b, x >> 2, y >> 2, z >> 2);
-    if (bucket < 0) return;                                          // cannot happen after k_blk_insert
-    atomicMax(&pool[(int64_t)bucket * 64 + (((x & 3) << 4) | ((y & 3) << 2) | (z & 3))], (int32_t)i);
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x * kInsPer + threadIdx.x;
+    uint64_t k[kInsPer], h[kInsPer];
+    int loc[kInsPer];
+    ulonglong2 s[kInsPer];
+#pragma unroll
+    for (int j = 0; j < kInsPer; ++j) {
+        const int64_t i = i0 + (int64_t)j * blockDim.x;
+        if (i < n) {
+            int32_t b, x, y, z;
+            read_coords(coords + i * stride, stride, b, x, y, z);
+            k[j] = block_key(b, x >> 2, y >> 2, z >> 2);
+            h[j] = block_slot(b, x >> 2, y >> 2, z >> 2, mask);
+            loc[j] = ((x & 3) << 4) | ((y & 3) << 2) | (z & 3);
+            s[j] = slot_at(t, h[j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kInsPer; ++j) {
+        const int64_t i = i0 + (int64_t)j * blockDim.x;
+        if (i >= n) break;
+        const int bucket = block_resolve(t, mask, k[j], h[j], s[j]);
+        if (bucket < 0) continue;                                    // cannot happen after k_blk_insert
+        atomicMax(&pool[(int64_t)bucket * 64 + loc[j]], (int32_t)i);
+    }
 }
 
 constexpr int kLookupThreads = 256;    // block size of k_blk_lookup (its shared-memory table)
@@ -267,7 +317,10 @@ k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Sl
         const bool need = (!ax || ox) && (!ay || oy) && (!az || oz);
         const int32_t cx = bx + (ax ? ox : 0), cy = by + (ay ? oy : 0), cz = bz + (az ? oz : 0);
         int bucket = -1;
-        if (need && cx >= 0 && cy >= 0 && cz >= 0) bucket = block_find(t, mask, b, cx, cy, cz);
+        if (need && cx >= 0 && cy >= 0 && cz >= 0) {
+            const uint64_t h = block_slot(b, cx, cy, cz, mask);
+            bucket = block_resolve(t, mask, block_key(b, cx, cy, cz), h, slot_at(t, h));
+        }
         s_base[m][threadIdx.x] = bucket >= 0 ? bucket * 64 : -1;
     }
     // per axis and offset d in {-1, 0, +1}: the block-select bit (x + d leaves the block) and the
@@ -415,11 +468,12 @@ tb_status nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int st
     k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap_b, reinterpret_cast<int*>(t + cap), nullptr);
     TB_LAUNCH_CHECK(ctx, "k_hash_clear");
     const int64_t blocks = (n + tpb - 1) / tpb;
-    k_blk_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, (unsigned)pool_blocks);
+    const int64_t ins_blocks = (n + (int64_t)tpb * kInsPer - 1) / ((int64_t)tpb * kInsPer);
+    k_blk_insert<<<(unsigned)ins_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, (unsigned)pool_blocks);
     TB_LAUNCH_CHECK(ctx, "k_blk_insert");
     k_pool_clear<<<ctx->num_sms * 8, tpb, 0, ctx->stream>>>(pool, ctl);
     TB_LAUNCH_CHECK(ctx, "k_pool_clear");
-    k_vox_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool);
+    k_vox_insert<<<(unsigned)ins_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool);
     TB_LAUNCH_CHECK(ctx, "k_vox_insert");
     static_assert(kLookupThreads == 256, "k_blk_lookup runs with the builder's block size");
     k_blk_lookup<NT><<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool, nbr);
