@@ -1,9 +1,10 @@
 """The z-slab step (dist.SlabRunner) on two GPUs of one box, over NCCL: every rank's owned rows
 after map + conv(SiLU) + conv must equal the same rows of the one-GPU step on the whole shell,
 bit for bit (the pair kernel sums each row's taps in a fixed order, wherever the row sits), for
-the eager step and for the recorded CUDA-graph replay. Skipped on a box with fewer than two
-GPUs. The ranks are child processes with a short process-group timeout; each releases its
-graph before destroying the group."""
+the eager step and for the recorded CUDA-graph replay. It runs only where two GPUs are visible
+and TB_MULTI_GPU_TESTS=1 is set, so that a single-GPU test run never starts NCCL ranks. The
+ranks are child processes with a short process-group timeout; each releases its graph before
+destroying the group."""
 import datetime
 import json
 import os
@@ -73,7 +74,8 @@ def _rank(rank, world, init_file, result_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.skipif(torch.cuda.device_count() < 2 or os.environ.get("TB_MULTI_GPU_TESTS") != "1",
+                    reason="needs two GPUs and TB_MULTI_GPU_TESTS=1")
 def test_two_rank_slab_step_matches_one_gpu(tb):
     with tempfile.TemporaryDirectory() as d:
         mp.start_processes(_rank, args=(2, os.path.join(d, "pg"), d), nprocs=2, start_method="spawn")
