@@ -81,3 +81,50 @@ def test_header_is_plain_c_and_links(tb, tmp_path):
     assert r.returncode == 0, r.stdout + r.stderr
     status, version = r.stdout.strip().split("|")
     assert status == "ok" and "sm_100a" in version
+
+
+CXX_PROGRAM = r"""
+#include "trellis_sparse.hpp"
+#include <cstdio>
+
+// Every host-mirror entry point, referenced so that the link resolves it; run() is never
+// called on a box without a GPU (main only runs it with an argument).
+static int run() {
+    std::vector<std::array<int, 3>> c{{0, 0, 0}};
+    std::vector<float> f(64, 0.f);
+    auto nbr = trellis::build_neighbor_table(c);
+    trellis::ConvWeights cw{};
+    auto y = trellis::sparse_submconv(cw, f, nbr, 1);
+    trellis::ConvNeXtWeights nw{};
+    auto z = trellis::sparse_convnext(nw, f, nbr, 1);
+    auto sd = trellis::subdivide(c, std::vector<uint8_t>(8, 1));
+    trellis::C2SWeights c2{};
+    auto up = trellis::sparse_c2s(c2, f, 64, c, 32);
+    auto m = trellis::GgufModel::load("model.gguf");
+    auto sl = trellis::read_slat("hr_slat.bin");
+    auto so = trellis::shape_decode(m, sl.feats, sl.coords);
+    auto gc = trellis::shape_upsample(m, sl.feats, sl.coords);
+    auto tx = trellis::tex_decode(m, sl.feats, sl.coords, so.subs);
+    trellis::Mesh mesh = trellis::dual_grid_to_mesh(so);
+    return (int)(y.size() + z.size() + sd.coords.size() + up.feats.size() + gc.size() + tx.size()) + mesh.F();
+}
+
+int main(int argc, char**) {
+    if (argc > 1) return run();
+    std::printf("%s\n", tb_version());
+    return 0;
+}
+"""
+
+
+def test_cxx_mirror_header_compiles_and_links(tb, tmp_path):
+    cxx = shutil.which("g++") or pytest.skip("g++ not found")
+    from trellis_cpp_b200 import _lib
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    (tmp_path / "mirror.cpp").write_text(CXX_PROGRAM)
+    b = subprocess.run([cxx, "-std=c++17", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                        str(tmp_path / "mirror.cpp"), "-o", str(tmp_path / "mirror"), "-L", libdir, "-ltb_sparse",
+                        "-Wl,-rpath," + libdir], capture_output=True, text=True)
+    assert b.returncode == 0, b.stderr
+    r = subprocess.run([str(tmp_path / "mirror")], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and "sm_100a" in r.stdout, r.stdout + r.stderr
