@@ -41,8 +41,11 @@ def _ptr(t) -> ctypes.c_void_p:
 
 
 def context(device=None):
-    """The per-device tb_ctx, bound to torch's current stream on that device."""
-    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index or 0)
+    """The per-device tb_ctx, bound to torch's current stream on that device (the current device
+    when `device` is None or names no index). One context per device is shared by every caller
+    in the process; like the C contexts it wraps, it is not safe to use from two threads at once."""
+    idx = None if device is None else torch.device(device).index
+    dev = torch.device("cuda", torch.cuda.current_device() if idx is None else idx)
     lib = _lib.load()
     h = _ctxs.get(dev.index)
     stream = torch.cuda.current_stream(dev).cuda_stream
