@@ -72,6 +72,25 @@ def _peaks():
     return 1590.0, 6650.0, "fallback"
 
 
+def _cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), or "" where it cannot be read."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return ""
+
+
+def _emit(line: dict) -> None:
+    """Print the bench's JSON line; a CPU baseline also names the host CPU it ran on."""
+    if isinstance(line.get("cpu_baseline"), dict):
+        line["cpu_baseline"].setdefault("cpu", _cpu_model())
+    print(json.dumps(line), flush=True)
+
+
 def _profile_traffic(name="submconv_pair_c4.md"):
     """DRAM bytes per launch at full size from a committed ncu summary, or None."""
     p = os.path.join(ROOT, "profiles", name)
@@ -203,7 +222,7 @@ def run_reference(args):
                                    f"{sample} output rows (threads={nthreads}); per-voxel times summed"},
         "e2e": {"value": value, "unit": "voxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line))
+    _emit(line)
     return 0
 
 
@@ -382,7 +401,7 @@ def run_gpu(args):
             "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps, "clocks": clocks, "kernels": kernel_stats,
         }
-        print(json.dumps(line))
+        _emit(line)
     if world > 1:
         runner.close()
         dist.destroy_process_group()
@@ -506,7 +525,7 @@ def run_convnext(args):
         "kernels": {"conv_ms": conv_ms, "tail_ms": tail_ms,
                     "conv_tflops": 2.0 * c * c * pairs / (conv_ms / 1e3) / 1e12},
     }
-    print(json.dumps(line))
+    _emit(line)
     return 0
 
 
@@ -626,7 +645,7 @@ def run_c2s(args):
         "roofline": roofline, "cpu_baseline": cpu, "e2e": None,
         "gpu_launches": (2 * ops.NBR_MAP_LAUNCHES + 9) * args.steps, "clocks": sampler.summary(),
     }
-    print(json.dumps(line))
+    _emit(line)
     return 0
 
 
@@ -743,7 +762,7 @@ def run_mesh(args):
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": (ops.NBR_MAP_LAUNCHES + 3) * args.steps, "clocks": sampler.summary(),
     }
-    print(json.dumps(line))
+    _emit(line)
     return 0
 
 
@@ -924,7 +943,7 @@ def run_decode(args):
                                 "sample": f"oracle port (fp32 multi-threaded convs, numpy MLPs, the oracle's "
                                           f"subdivide and gathers) on a {npar}-parent patch of the shell grown to "
                                           f"{nout} output voxels ({dt:.1f} s)"}
-    print(json.dumps(line))
+    _emit(line)
     return 0
 
 
