@@ -423,7 +423,12 @@ class GgufFile:
             _io_check(lib.tb_gguf_tensor_info(self._g, i, ctypes.byref(name), ctypes.byref(typ), ctypes.byref(nd), ne,
                                               ctypes.byref(nb)), "tb_gguf_tensor_info")
             shape = tuple(int(ne[d]) for d in range(nd.value))[::-1]
-            self.tensors[name.value.decode()] = (i, int(typ.value), shape, int(nb.value))
+            try:
+                key = name.value.decode("utf-8")
+            except UnicodeDecodeError:
+                self.close()
+                raise TBError(1, "GgufFile", f"tensor {i}: name is not valid UTF-8") from None
+            self.tensors[key] = (i, int(typ.value), shape, int(nb.value))
 
     def close(self):
         if self._g:
