@@ -108,3 +108,23 @@ def test_slat_dump(tb, tmp_path):
     with pytest.raises(ops.TBError) as e:
         ops.read_slat(p)
     assert "size does not match" in str(e.value)
+
+
+@pytest.mark.parametrize("header,tail", [((-1, 64), 0), ((2 ** 31 - 1, 64), 100), ((0x10000000, 64), 64), ((7,), 0)])
+def test_slat_rejects_bad_headers(tb, tmp_path, header, tail):
+    # a negative count, counts whose data the file cannot hold (including one whose byte size
+    # overflows 32 bits), and a header cut short: all rejected before any allocation of N rows
+    from trellis_cpp_b200 import ops
+    p = tmp_path / "bad.bin"
+    p.write_bytes(np.array(header, dtype=np.int32).tobytes() + bytes(tail))
+    with pytest.raises(ops.TBError):
+        ops.read_slat(p)
+
+
+def test_slat_empty_dump(tb, tmp_path):
+    # N = 0 is a valid (empty) dump; the resolution is passed through as the reference reads it
+    from trellis_cpp_b200 import ops
+    p = tmp_path / "empty.bin"
+    p.write_bytes(np.array([0, 64], dtype=np.int32).tobytes())
+    c, x, r = ops.read_slat(p)
+    assert c.shape == (0, 3) and x.shape == (0, 32) and r == 64
