@@ -83,3 +83,24 @@ def test_slab_bounds_balanced(tb):
         sizes = [tbdist.plan_slabs(coords, world, r).n_owned for r in range(world)]
         assert sum(sizes) == coords.shape[0]
         assert max(sizes) < 1.15 * coords.shape[0] / world
+
+
+def test_slab_plan_edge_cases(tb):
+    from trellis_cpp_b200 import dist as tbdist
+    rng = np.random.default_rng(4)
+    c = rng.integers(0, 12, (2000, 3)).astype(np.int32)
+    # one rank owns everything and has no halo
+    p = tbdist.plan_slabs(c, 1, 0)
+    assert p.n_owned == len(c) and p.n_local == len(c)
+    assert p.send_lo.size == p.send_hi.size == p.recv_lo.size == p.recv_hi.size == 0
+    # as many ranks as planes: one plane per slab, and every halo plane is a neighbour's owned plane
+    world = 12
+    plans = [tbdist.plan_slabs(c, world, r) for r in range(world)]
+    assert all(pl.z_hi - pl.z_lo == 1 for pl in plans)
+    assert np.array_equal(np.sort(np.concatenate([pl.owned for pl in plans])), np.arange(len(c)))
+    for r in range(1, world):
+        assert np.array_equal(plans[r].halo_lo, plans[r - 1].owned)
+        assert plans[r].recv_lo.size == plans[r - 1].send_hi.size
+    # more ranks than planes cannot be cut into slabs
+    with pytest.raises(ValueError):
+        tbdist.plan_slabs(c, 13, 0)
