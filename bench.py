@@ -43,6 +43,7 @@ import subprocess
 import sys
 import threading
 import time
+import zlib
 
 import numpy as np
 
@@ -401,6 +402,10 @@ def run_gpu(args):
             "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps, "clocks": clocks, "kernels": kernel_stats,
         }
+        if world == 1 and not args.no_configs:
+            # every other BASELINE configuration, timed after the headline (not part of its value)
+            line["configs"] = run_configs(dev, max(3, min(args.steps, 20)), max(3, args.warmup),
+                                          cpu=not args.no_cpu)
         _emit(line)
     if world > 1:
         runner.close()
@@ -548,11 +553,10 @@ def cpu_c2s_step(coords, mask, feats, w, cout, planes=4):
     return dt / max(1, child.shape[0]), dt, int(sel.sum()), int(child.shape[0])
 
 
-def run_c2s(args):
+def measure_c2s(dev, steps, warmup, cpu=True):
+    """One tb_sparse_c2s call on config 3's shape, timed by CUDA events; returns a dict with the
+    line's fields (value in children/s, roofline of conv1, CPU baseline)."""
     import torch
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
-    _load_package()
     from trellis_cpp_b200 import ops, synth
 
     cin, cout = 256, 128
@@ -583,43 +587,20 @@ def run_c2s(args):
     def step():
         return ops.sparse_c2s(coords, feats, prm, cout, ext_mask=mask, max_children=m_children)
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         out, child, _ = step()
     torch.cuda.synchronize()
     ops.check_device()
     m = child.shape[0]
-    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
-    sampler.start()
-    time.sleep(0.8)
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    sampler.stop()
+    ms_step = _time_op(step, steps, 0)
     ops.check_device()
-    ms_step = e0.elapsed_time(e1) / args.steps
 
     # conv1 alone (the block's dominant kernel) for the roofline
     nbr = ops.build_neighbor_table(coords)
     h = torch.empty((n, cin), dtype=bf, device=dev)
     h.copy_(feats)
     h1 = torch.empty((n, 8 * cout), dtype=torch.float32, device=dev)
-    for _ in range(3):
-        ops.sparse_submconv(h, nbr, prm["conv1.weight"], prm["conv1.bias"], out=h1)
-    torch.cuda.synchronize()
-    c0 = torch.cuda.Event(enable_timing=True)
-    c1 = torch.cuda.Event(enable_timing=True)
-    reps = 10
-    c0.record()
-    for _ in range(reps):
-        ops.sparse_submconv(h, nbr, prm["conv1.weight"], prm["conv1.bias"], out=h1)
-    c1.record()
-    torch.cuda.synchronize()
-    conv1_ms = c0.elapsed_time(c1) / reps
+    conv1_ms = _time_op(lambda: ops.sparse_submconv(h, nbr, prm["conv1.weight"], prm["conv1.bias"], out=h1), 10, 3)
     pairs = ops.count_valid_pairs(nbr, n)
     peak_tf, peak_bw, peak_kind = _peaks()
     flops1 = 2.0 * cin * 8 * cout * pairs
@@ -627,23 +608,43 @@ def run_c2s(args):
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
                 "traffic": None, "peak_source": f"{peak_kind} bf16_tflops (burst)", "kernel": "k_submconv_brick (conv1)",
                 "flops_per_launch": flops1, "conv1_ms": conv1_ms}
-    cpu = None
-    if not args.no_cpu:
+    cpu_b = None
+    if cpu:
         spc, dt, np_, nc_ = cpu_c2s_step(parents, mask_np, feats_np, w, cout)
-        cpu = {"value": 1.0 / spc, "unit": "children/s", "cores": os.cpu_count() or 1, "kind": "port",
-               "sample": f"oracle port (numpy fp64) c2s_block on {np_} parents of 4 x-planes -> {nc_} children "
-                         f"({dt:.2f} s)"}
+        cpu_b = {"value": 1.0 / spc, "unit": "children/s", "cores": os.cpu_count() or 1, "kind": "port",
+                 "cpu": _cpu_model(),
+                 "sample": f"oracle port (numpy fp64) c2s_block on {np_} parents of 4 x-planes -> {nc_} children "
+                           f"({dt:.2f} s)"}
+    del h, h1, nbr
+    torch.cuda.empty_cache()
+    return {"workload": "c3: res-256 shell parents -> res-512 children, external (texture-decoder style) mask, "
+                        "Cin=256 Cout=128 bf16 operands, fp32 conv outputs and skip",
+            "metric": "children/s through one SparseResBlockC2S3d up-block",
+            "value": m / (ms_step / 1e3), "unit": "children/s", "ms_per_step": ms_step, "steps": steps,
+            "parents": n, "children": m, "parent_valid_pairs": pairs, "roofline": roofline, "cpu_baseline": cpu_b,
+            "l2": "conv1 output 1.0 GB per step (larger than L2)",
+            "launches_per_step": 2 * ops.NBR_MAP_LAUNCHES + 9}
+
+
+def run_c2s(args):
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _load_package()
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    sampler.start()
+    time.sleep(0.8)
+    r = measure_c2s(dev, args.steps, args.warmup, cpu=not args.no_cpu)
+    sampler.stop()
     line = {
-        "metric": C2S_METRIC, "value": m / (ms_step / 1e3), "unit": "children/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "metric": C2S_METRIC, "value": r["value"], "unit": "children/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded res-256 noisy shell, seeded thickness mask, random weights of the block's shapes)",
-        "config": {"workload": "c3: res-256 shell parents -> res-512 children, external (texture-decoder style) mask, "
-                               "Cin=256 Cout=128 bf16 operands, fp32 conv outputs and skip",
-                   "parents": n, "children": m, "parent_valid_pairs": pairs,
-                   "l2": "conv1 output 1.0 GB per step (larger than L2)"},
-        "roofline": roofline, "cpu_baseline": cpu, "e2e": None,
-        "gpu_launches": (2 * ops.NBR_MAP_LAUNCHES + 9) * args.steps, "clocks": sampler.summary(),
+        "config": {"workload": r["workload"], "parents": r["parents"], "children": r["children"],
+                   "parent_valid_pairs": r["parent_valid_pairs"], "l2": r["l2"]},
+        "roofline": r["roofline"], "cpu_baseline": r["cpu_baseline"], "e2e": None,
+        "gpu_launches": r["launches_per_step"] * args.steps, "clocks": sampler.summary(),
     }
     _emit(line)
     return 0
@@ -947,6 +948,243 @@ def run_decode(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- every BASELINE config
+# One timed entry per configuration of BASELINE.json (C1, C2, C3, C5 at C=32 and C=512; C4 is the
+# headline line itself) plus two row-order probes of the C4 conv. Each entry: the conv (or block)
+# timed with CUDA events on HBM-resident inputs, its roofline against the measured peak, a parity
+# check of sampled rows against the oracle, and the oracle port timed on a bounded sample.
+CFG_TABLE = {
+    # name: (coords, ci, co, dtype, epilogue, cpu sample rows, bias std)
+    "c1": ("c1", 64, 64, "f32", "none", None, 0.0),
+    "c2": ("c2", 256, 256, "f16", "none", 4096, 0.01),
+    "c5_32": ("c5_32", 32, 32, "f16", "none", 65536, 0.0),
+    "c5_512": ("c5_512", 512, 512, "f16", "none", 1024, 0.0),
+}
+
+
+def _l2_flush_buffer(dev):
+    import torch
+    return torch.empty(64 << 20, dtype=torch.float32, device=dev)     # 256 MB > the 126 MB L2
+
+
+def _time_op(fn, steps, warmup, flush=None):
+    """Mean ms per call of fn() by CUDA events on the current stream. With `flush` (a buffer
+    larger than L2) the buffer is rewritten before every timed call, outside the events."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if flush is None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+    evs = []
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return float(np.mean([a.elapsed_time(b) for a, b in evs]))
+
+
+def _sample_rows(n, k, seed):
+    rng = np.random.default_rng(seed)
+    return np.sort(rng.choice(n, size=min(n, k), replace=False)).astype(np.int64)
+
+
+def _torch_conv_rows(nbr, feats, w, bias, n, rows, silu):
+    """Output rows `rows` of the conv as a plain torch fp32 gather + matmul on the device (an
+    independent check of the kernel's arithmetic; absent taps contribute zero)."""
+    import torch
+    r = torch.from_numpy(np.ascontiguousarray(rows, dtype=np.int64)).to(feats.device)
+    nb = nbr.view(27, n)[:, r].long()                                     # [27, m]
+    present = (nb != n).unsqueeze(-1)
+    x = feats.float()[nb.clamp(max=n - 1)] * present                     # [27, m, ci]
+    y = torch.einsum("tmc,otc->mo", x, w.float())
+    if bias is not None:
+        y = y + bias.float()
+    return torch.nn.functional.silu(y) if silu else y
+
+
+def _mini_problem(nbr, feats, n, rows):
+    """The conv of output rows `rows` as a small stand-alone problem for the CPU: the rows come
+    first in the local order, followed by every other row they read. Returns (tap-major int32 map
+    [27 * n_loc] with sentinel n_loc, float32 features [n_loc, ci]); local rows 0..len(rows)-1
+    are the requested ones. Only these rows leave the device."""
+    import torch
+    r_t = torch.from_numpy(np.ascontiguousarray(rows, dtype=np.int64)).to(feats.device)
+    nb = nbr.view(27, n)[:, r_t].cpu().numpy().astype(np.int64)        # [27, m]
+    m = rows.size
+    present = nb != n
+    others = np.setdiff1d(np.unique(nb[present]), rows)
+    order = np.concatenate([np.asarray(rows, dtype=np.int64), others])
+    perm = np.argsort(order, kind="stable")
+    sorted_ids = order[perm]
+    n_loc = order.size
+    loc = np.full((27, n_loc), n_loc, dtype=np.int32)
+    loc[:, :m] = np.where(present, perm[np.searchsorted(sorted_ids, np.where(present, nb, sorted_ids[0]))], n_loc)
+    f = feats[torch.from_numpy(order).to(feats.device)].float().cpu().numpy()
+    return np.ascontiguousarray(loc.reshape(-1)), f
+
+
+def measure_conv_config(name, dev, steps, warmup, cpu=True, coords_np=None, order_note=None):
+    """One BASELINE conv configuration: map prebuilt, one conv timed; returns the entry dict."""
+    import torch
+    from trellis_cpp_b200 import ops, synth
+    cname, ci, co, dts, epi, cpu_rows, bstd = CFG_TABLE[name]
+    if coords_np is None:
+        coords_np = synth.coords_for(cname)
+    n = coords_np.shape[0]
+    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dts]
+    g = torch.Generator(device=dev).manual_seed(zlib.crc32(name.encode()) & 0xFFFF)
+    feats = torch.randn((n, ci), device=dev, generator=g).to(tdt)
+    w = (torch.randn((co, 27, ci), device=dev, generator=g) / np.sqrt(27 * ci)).to(tdt)
+    bias = (bstd * torch.randn(co, device=dev, generator=g)) if bstd else None
+    coords = torch.from_numpy(coords_np).to(dev)
+    nbr = torch.empty(27 * n, dtype=torch.int32, device=dev)
+    ops.build_neighbor_table(coords, out=nbr)
+    out = torch.empty((n, co), dtype=tdt, device=dev)
+    small = n * ci * feats.element_size() + 108 * n < (256 << 20)
+    flush = _l2_flush_buffer(dev) if small else None
+    conv = lambda: ops.sparse_submconv(feats, nbr, w, bias, epi=epi, out=out)   # noqa: E731
+    conv_ms = _time_op(conv, steps, warmup, flush)
+    map_ms = _time_op(lambda: ops.build_neighbor_table(coords, out=nbr), max(3, steps // 2), 2, flush)
+    ops.check_device()
+    pairs = ops.count_valid_pairs(nbr, n)
+    peak_tf, peak_bw, peak_kind = _peaks()
+    esz = feats.element_size()
+    flops = 2.0 * ci * co * pairs
+    bytes_ = n * (ci + co) * esz + 108 * n + 27 * ci * co * esz + (4 * co if bias is not None else 0)
+    t_tensor = flops / (peak_tf * 1e12) if dts != "f32" else 0.0
+    t_hbm = bytes_ / (peak_bw * 1e9)
+    if dts == "f32" or t_hbm >= t_tensor:
+        achieved = bytes_ / (conv_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak_bw, "unit": "GB/s", "frac": achieved / peak_bw,
+                "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": bytes_}
+    else:
+        achieved = flops / (conv_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                "frac": achieved / peak_tf, "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                "flops_per_launch": flops}
+    path = "k_conv_f32 (FFMA)" if dts == "f32" else (
+        "k_submconv_pair" if ci == 64 and co in (32, 64) else
+        ("k_submconv_brick" if ci % 64 == 0 else "k_submconv_tc (gather4)"))
+    roof["kernel"] = path
+    # parity of sampled rows against a plain torch fp32 gather + matmul of the same operands
+    rows = _sample_rows(n, 256, 5)
+    ref = _torch_conv_rows(nbr, feats, w, bias, n, rows, epi == "silu")
+    got = out[torch.from_numpy(rows).to(dev)].float()
+    mrel = float((got - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+    w_h = w.float().cpu().numpy()
+    tol = 1e-4 if dts == "f32" else 1e-2
+    entry = {
+        "workload": synth.CONFIGS[cname]["desc"] if order_note is None else order_note, "voxels": n,
+        "ci": ci, "co": co, "dtype": dts, "metric": "voxels/s through one 3^3 submanifold conv (map prebuilt)",
+        "value": n / (conv_ms / 1e3), "unit": "voxels/s", "ms_per_step": conv_ms, "steps": steps,
+        "map_ms": map_ms, "valid_pairs": pairs, "mean_valid_taps": pairs / max(n, 1),
+        "effective_tflops": flops / (conv_ms / 1e3) / 1e12, "roofline": roof,
+        "l2": "L2 flushed before each timed call (inputs under 256 MB)" if small else "inputs larger than L2",
+        "parity": {"vs": "torch fp32 gather + matmul of the same operands", "rows_checked": int(rows.size),
+                   "max_rel": mrel,
+                   "tol": tol, "ok": mrel < tol},
+    }
+    if cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle      # the CPU baseline leg: the oracle port is what is timed here
+        nthreads = os.cpu_count() or 1
+        sample = n if cpu_rows is None else min(n, cpu_rows)
+        row0 = (n - sample) // 2
+        nbr_s, f_s = _mini_problem(nbr, feats, n, np.arange(row0, row0 + sample, dtype=np.int64))
+        wt = oracle.weight_tap_major(w_h)
+        t0 = time.perf_counter()
+        oracle.submconv_f32_mt_range(nbr_s, f_s, wt, 0, sample, nthreads=nthreads)
+        dt = time.perf_counter() - t0
+        entry["cpu_baseline"] = {"value": sample / dt, "unit": "voxels/s", "cores": nthreads, "kind": "port",
+                                 "cpu": _cpu_model(),
+                                 "sample": f"oracle port fp32 conv on {sample} consecutive rows (their neighbor rows "
+                                           f"gathered first), {nthreads} threads ({dt:.2f} s)"}
+    del feats, w, nbr, out, flush
+    torch.cuda.empty_cache()
+    return entry
+
+
+def _c4_orders(dev):
+    """The C4 conv's input in two other row orders than the generator's x-major one:
+    (a) the order a decoder produces it -- the res-512 (half-scale) shell subdivided with a seeded
+    thickness mask into res-1024 children by tb_subdivide, parent-major and octant-ascending
+    (src/sparse.cpp:205-222); (b) the C4 voxels in Morton (z-order curve) order."""
+    import torch
+    from trellis_cpp_b200 import ops, synth
+    parents = synth.coords_for("c4s")
+    mask = synth.child_mask(parents, 512, 220.0, 8.0, 64.0, 4, 0.5)
+    child, _, _ = ops.subdivide(torch.from_numpy(parents).to(dev), torch.from_numpy(mask.reshape(-1)).to(dev),
+                                int(mask.sum()))
+    child = child.cpu().numpy()
+    c4 = synth.coords_for("c4")
+
+    def morton(c):
+        def spread(v):
+            v = v.astype(np.uint64) & np.uint64(0x1FFFFF)
+            r = np.zeros_like(v)
+            for b in range(21):
+                r |= ((v >> np.uint64(b)) & np.uint64(1)) << np.uint64(3 * b)
+            return r
+        return spread(c[:, -3]) << np.uint64(2) | spread(c[:, -2]) << np.uint64(1) | spread(c[:, -1])
+    c4m = np.ascontiguousarray(c4[np.argsort(morton(c4), kind="stable")])
+    xsorted = np.ascontiguousarray(child[np.lexsort((child[:, -1], child[:, -2], child[:, -3]))])
+    return np.ascontiguousarray(child), xsorted, c4m
+
+
+def run_configs_line(args):
+    """`--op configs`: the per-config entries alone, as one JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _load_package()
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    sampler.start()
+    time.sleep(0.8)
+    res = run_configs(dev, max(3, min(args.steps, 20)), max(3, args.warmup), cpu=not args.no_cpu)
+    sampler.stop()
+    _emit({"metric": "per-configuration conv throughput (BASELINE configs C1-C5)", "n_gpus": 1,
+           "configs": res, "clocks": sampler.summary()})
+    return 0
+
+
+def run_configs(dev, steps, warmup, cpu=True):
+    """Every BASELINE configuration other than the headline C4 step (see CFG_TABLE), C3's C2S
+    block, and the C4 conv on decoder-ordered and Morton-ordered rows."""
+    import torch
+    res = {}
+    for name in ("c1", "c2", "c5_32", "c5_512"):
+        st = steps if name != "c5_512" else max(3, steps // 4)
+        res[name] = measure_conv_config(name, dev, st, warmup, cpu)
+    res["c3"] = measure_c2s(dev, max(3, steps // 2), warmup, cpu)
+    dec, dec_sorted, c4m = _c4_orders(dev)
+    CFG_TABLE["c4_order"] = ("c4", 64, 64, "bf16", "silu", None, 0.0)
+    res["c4_decoder_order"] = measure_conv_config(
+        "c4_order", dev, steps, warmup, False, dec,
+        "res-512 shell subdivided to res 1024 (decoder order: parent-major, octant-ascending), C=64 bf16")
+    res["c4_decoder_sorted"] = measure_conv_config(
+        "c4_order", dev, steps, warmup, False, dec_sorted,
+        "the same children sorted x-major (the reference's key order), C=64 bf16")
+    res["c4_morton"] = measure_conv_config(
+        "c4_order", dev, steps, warmup, False, c4m, "C4 shell in Morton order, C=64 bf16")
+    res["c4_xmajor"] = measure_conv_config(
+        "c4_order", dev, steps, warmup, False, None, "C4 shell in x-major order (as the headline), C=64 bf16")
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -957,16 +1195,18 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--workload", default=WORKLOAD, choices=["c4", "c4s"],
                     help="c4 (default, the benchmark) or c4s (half scale, for profiler captures)")
-    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s", "decode", "mesh"],
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-config entries of the headline line")
+    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s", "decode", "mesh", "configs"],
                     help="stack (default, the benchmark: map + conv x2), convnext (one ConvNeXt block), c2s "
                          "(one C2S up-block), decode (the sparse decoder UNet) or mesh (dual_grid_to_mesh)")
     args = ap.parse_args()
-    if args.op in ("convnext", "c2s", "decode", "mesh"):
+    if args.op in ("convnext", "c2s", "decode", "mesh", "configs"):
         if args.impl == "reference" or args.gpus != 1:
             print(json.dumps({"impl": args.impl, "unavailable": f"--op {args.op} is a single-GPU measurement of "
                               "our kernels; its CPU baseline is in the line's cpu_baseline"}))
             return 0
-        return {"convnext": run_convnext, "c2s": run_c2s, "decode": run_decode, "mesh": run_mesh}[args.op](args)
+        return {"convnext": run_convnext, "c2s": run_c2s, "decode": run_decode, "mesh": run_mesh,
+                "configs": run_configs_line}[args.op](args)
     if args.impl == "reference":
         return run_reference(args)
     return run_gpu(args)

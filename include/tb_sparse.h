@@ -85,9 +85,15 @@ tb_status tb_build_neighbor_map(tb_ctx* ctx, const int32_t* coords, int64_t n,
  *   - n may be at most TB_NOALLOC_MAX_VOXELS; a larger n returns TB_ERR_TOO_LARGE and enqueues
  *     nothing.
  *   - Runs on the calling thread's current device and enqueues on `stream` (a cudaStream_t,
- *     NULL = legacy default stream); returns without synchronising.
+ *     NULL = legacy default stream); returns without synchronising. coords and nbr_out must
+ *     be device (or managed) memory of that device, else TB_ERR_INVALID_ARG.
  *   - The first call on a device looks up the array's device address (with that device
- *     current); make that first call before any stream capture.
+ *     current); make that first call before any stream capture. With lazy module loading
+ *     (CUDA_MODULE_LOADING=LAZY, the CUDA 12 default) that first lookup also loads the
+ *     library's device code on that device, which backs the 16 MiB array and may synchronise
+ *     the device: make the first call at start-up, or set CUDA_MODULE_LOADING=EAGER.
+ *   - TB_ERR_CUDA reports a failed launch of this call's own kernels only; an error that
+ *     earlier, unrelated work left pending is neither reported nor cleared.
  *   - All calls on one device share the single table, and each call clears it before use:
  *     calls that overlap on the GPU (for example on two streams) race and corrupt each
  *     other's maps. Serialise them on one stream. */

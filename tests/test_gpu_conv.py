@@ -235,3 +235,22 @@ def test_c4_two_stacked_convs(tb):
     # conv 1 (with SiLU, bf16 output) on the same rows
     ref1 = oracle.submconv_rows(nb, f.float().cpu().numpy(), w1.float().cpu().numpy(), rows, silu=True)
     assert max_rel(h[torch.from_numpy(rows).cuda()].float().cpu().numpy(), ref1) < 1e-2
+
+
+def test_c1_full_config_fp32_every_row(tb):
+    """Configuration C1 at its own size: the res-64 band (12,660 voxels), Cin = Cout = 64, fp32
+    operands (the reference's --f32 precision mode, src/sparse.cpp:16-19), features N(0,1),
+    weights N(0, 1/(27*64)), bias 0. Every output row against the oracle at 1e-4."""
+    from trellis_cpp_b200 import ops, synth
+    coords = synth.coords_for("c1")
+    n = coords.shape[0]
+    assert n == 12660
+    rng = np.random.default_rng(101)
+    feats = rng.standard_normal((n, 64)).astype(np.float32)
+    w = (rng.standard_normal((64, 27, 64)) / np.sqrt(27 * 64)).astype(np.float32)
+    out, nbr = _run(coords, feats, w, np.zeros(64, np.float32), "f32")
+    nb = nbr.cpu().numpy()
+    assert np.array_equal(nb, oracle.build_neighbor_table(coords))
+    ref = oracle.submconv(nb, feats, w, np.zeros(64, np.float32))
+    assert out.shape == ref.shape
+    assert max_rel(out, ref) < 1e-4

@@ -91,6 +91,45 @@ def test_gguf_rejects_bad_files(tb, tmp_path):
         ops.GgufFile(tmp_path / "missing.gguf")
 
 
+def _gguf_one_tensor(ne, ggml_type=0, offset=0, data=b""):
+    """A minimal GGUF v3 file: no metadata, one tensor info with the given dims, type and
+    offset, 32-byte alignment, then `data`."""
+    import struct
+    name = b"t"
+    head = b"GGUF" + struct.pack("<IQQ", 3, 1, 0)
+    info = struct.pack("<Q", len(name)) + name + struct.pack("<I", len(ne))
+    info += b"".join(struct.pack("<Q", e) for e in ne) + struct.pack("<IQ", ggml_type, offset)
+    body = head + info
+    body += bytes((-len(body)) % 32)
+    return body + data
+
+
+@pytest.mark.parametrize("ne,offset", [
+    ((1 << 40, 1 << 40, 1 << 40, 1 << 40), 0),   # the element count wraps 2^64 several times
+    ((1 << 32, 1 << 32), 0),                     # exactly 2^64 elements: wraps to 0
+    ((1 << 31, 1 << 31, 4), 0),                  # 2^64 elements again, over three dims
+    ((1 << 30, 1 << 30), 0),                     # no wrap, but 2^62 bytes: past the end
+    ((4,), (1 << 64) - 8),                       # the data offset wraps the end-of-file check
+])
+def test_gguf_rejects_overflowing_tensor_infos(tb, tmp_path, ne, offset):
+    from trellis_cpp_b200 import ops
+    p = tmp_path / "big.gguf"
+    p.write_bytes(_gguf_one_tensor(ne, 0, offset, bytes(64)))
+    with pytest.raises(ops.TBError):
+        ops.GgufFile(p)
+
+
+def test_gguf_hand_written_file_parses(tb, tmp_path):
+    """The crafted layout itself is valid: four F32 values at offset 0 read back."""
+    from trellis_cpp_b200 import ops
+    vals = np.arange(4, dtype=np.float32)
+    p = tmp_path / "small.gguf"
+    p.write_bytes(_gguf_one_tensor((4,), 0, 0, vals.tobytes()))
+    f = ops.GgufFile(p)
+    np.testing.assert_array_equal(f.numpy("t"), vals)
+    f.close()
+
+
 def test_slat_dump(tb, tmp_path):
     from trellis_cpp_b200 import ops
     rng = np.random.default_rng(2)

@@ -20,6 +20,7 @@ from conftest import random_voxels
 
 pytestmark = pytest.mark.gpu
 
+TB_ERR_INVALID_ARG = 1
 TB_ERR_TOO_LARGE = 6
 
 
@@ -38,8 +39,13 @@ def _inputs():
     from trellis_cpp_b200 import synth
     rng = np.random.default_rng(21)
     dups = rng.integers(0, 14, size=(9000, 3)).astype(np.int32)          # many duplicate rows
+    # exactly the maximum size, so the table spans all of its slots and the cell after them;
+    # a (-1,-1,-1) voxel has the all-ones key, which lives in that separate cell
+    full = random_voxels(524288 - 1, 90, 22)
+    full = np.concatenate([full[:1000], np.full((1, 3), -1, np.int32), full[1000:]])
     return [("c2 shell", synth.coords_for("c2")),                        # 249K voxels, [N,4]
             ("random with duplicates", dups),
+            ("maximum size with an all-ones key", full),
             ("small box", random_voxels(3000, 30, 4))]
 
 
@@ -68,3 +74,15 @@ def test_noalloc_rejects_sizes_above_the_limit(tb):
                                            ctypes.c_void_p(coords.data_ptr()), n, 3,
                                            ctypes.c_void_p(out.data_ptr()))
     assert st == TB_ERR_TOO_LARGE
+
+
+def test_noalloc_rejects_host_memory(tb):
+    """Coordinates in (pinned) host memory are refused before anything is launched."""
+    from trellis_cpp_b200 import _lib
+    lib = _lib.load()
+    coords = torch.zeros((64, 3), dtype=torch.int32).pin_memory()
+    out = torch.zeros(27 * 64, dtype=torch.int32, device="cuda")
+    st = lib.tb_build_neighbor_map_noalloc(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                                           ctypes.c_void_p(coords.data_ptr()), 64, 3,
+                                           ctypes.c_void_p(out.data_ptr()))
+    assert st == TB_ERR_INVALID_ARG

@@ -171,16 +171,21 @@ tb_status tb_gguf_open(const char* path, tb_gguf** out) {
         t.name = r.str();
         t.n_dims = r.get<uint32_t>();
         if (!r.ok || t.n_dims < 1 || t.n_dims > 4) { r.ok = false; break; }
+        // the element count and the byte size must not wrap: a wrapped product would report a
+        // shape whose bytes differ from nbytes, and callers size buffers from ne[]
         uint64_t elems = 1;
         for (uint32_t d = 0; d < t.n_dims; ++d) {
             const uint64_t e = r.get<uint64_t>();
-            if (e > (1ull << 40)) r.ok = false;
+            if (e > (1ull << 40) || (e != 0 && elems > UINT64_MAX / e)) r.ok = false;
             t.ne[d] = (int64_t)e;
-            elems *= e;
+            if (r.ok) elems *= e;
         }
         t.type = r.get<uint32_t>();
         t.offset = r.get<uint64_t>();
-        t.nbytes = elems * type_size(t.type);   // 0 for types this reader does not convert
+        const uint64_t esz = type_size(t.type);
+        if (esz != 0 && elems > UINT64_MAX / esz) r.ok = false;
+        if (!r.ok) break;
+        t.nbytes = elems * esz;   // 0 for types this reader does not convert
         g->index[t.name] = (int64_t)i;
     }
     if (!r.ok) {
@@ -191,7 +196,9 @@ tb_status tb_gguf_open(const char* path, tb_gguf** out) {
     g->data_off = (pos + g->alignment - 1) / g->alignment * g->alignment;
     fclose(f);
     for (const GgufTensor& t : g->tensors)
-        if (t.nbytes && g->data_off + t.offset + t.nbytes > fsize) {
+        // compared without sums that can wrap: data_off <= fsize here, then offset and nbytes in turn
+        if (t.nbytes && (g->data_off > fsize || t.offset > fsize - g->data_off ||
+                         t.nbytes > fsize - g->data_off - t.offset)) {
             const std::string name = t.name;
             delete g;
             return io_fail(TB_ERR_INVALID_ARG, std::string("tb_gguf_open: ") + path + ": tensor " + name +

@@ -75,7 +75,7 @@ __global__ void k_hash_insert(const int32_t* __restrict__ coords, int64_t n, int
             if (prev == kEmpty || prev == k) { atomicMax(&t[h].row, (int)i); done = true; break; }
             h = (h + 1) & mask;
         }
-        if (!done) atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
+        if (!done && err) atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
     }
 }
 
@@ -89,7 +89,7 @@ __device__ __forceinline__ int lookup(const Slot* __restrict__ t, uint64_t mask,
         if (s.x == kEmpty) return absent;
         h = (h + 1) & mask;
     }
-    atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
+    if (err) atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
     return absent;
 }
 
@@ -582,7 +582,8 @@ namespace {
 
 constexpr int64_t kNoAllocMaxVoxels = TB_NOALLOC_MAX_VOXELS;
 constexpr uint64_t kNoAllocSlots = 2 * (uint64_t)kNoAllocMaxVoxels;      // load factor <= 1/2
-constexpr size_t kNoAllocBytes = kNoAllocSlots * sizeof(Slot) + 256;    // slots + all-ones-key cell + error word
+constexpr size_t kNoAllocBytes = kNoAllocSlots * sizeof(Slot) + 256;    // slots + the all-ones-key cell
+static_assert(kNoAllocBytes == TB_NOALLOC_SCRATCH, "the header states the array's size");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
@@ -591,6 +592,20 @@ void* g_noalloc_addr[kMaxDevices];          // device address of g_noalloc_scrat
 int g_noalloc_sms[kMaxDevices];
 std::once_flag g_noalloc_once[kMaxDevices];
 cudaError_t g_noalloc_setup_err[kMaxDevices];
+
+// True when p is device (or managed) memory that device `dev` can use as a kernel argument.
+bool noalloc_on_device(const void* p, int dev) {
+    cudaPointerAttributes a;
+    const cudaError_t pending = cudaPeekAtLastError();
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        // clear the error this query left, but only when no earlier error was pending: that one
+        // belongs to the caller's own work
+        if (pending == cudaSuccess) cudaGetLastError();
+        return false;
+    }
+    if (a.type == cudaMemoryTypeManaged) return true;
+    return a.type == cudaMemoryTypeDevice && a.device == dev;
+}
 
 }  // namespace
 
@@ -602,6 +617,8 @@ extern "C" tb_status tb_build_neighbor_map_noalloc(void* stream, const int32_t* 
     if (!coords || !nbr_out) return TB_ERR_INVALID_ARG;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TB_ERR_CUDA;
+    // both arrays must live on the current device: the kernels run there
+    if (!noalloc_on_device(coords, dev) || !noalloc_on_device(nbr_out, dev)) return TB_ERR_INVALID_ARG;
     // one-time set-up per device, with that device current: the host-side name of the array is
     // only a stand-in, so its device address has to be looked up before a kernel may use it
     std::call_once(g_noalloc_once[dev], [dev]() {
@@ -620,14 +637,27 @@ extern "C" tb_status tb_build_neighbor_map_noalloc(void* stream, const int32_t* 
     const uint64_t cap = tb_hash_capacity(n);                   // <= kNoAllocSlots for n <= the maximum
     Slot* t = reinterpret_cast<Slot*>(g_noalloc_addr[dev]);
     int* special = reinterpret_cast<int*>(t + cap);
-    int* err = reinterpret_cast<int*>(reinterpret_cast<unsigned char*>(g_noalloc_addr[dev]) + kNoAllocBytes - 4);
+    // No error word: the table has at least 2n slots for at most n keys, and the probe loops may
+    // scan the whole table, so an insert always finds a free or matching slot and a lookup always
+    // reaches one; the probe bound of the hash kernels can never be hit here.
+    int* const no_err = nullptr;
+    const int* const no_gate = nullptr;
     const int tpb = 256;
-    // every call rebuilds the table from scratch: the previous call's contents are cleared here
-    const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)g_noalloc_sms[dev] * 16);
-    k_hash_clear<<<clear_blocks, tpb, 0, st>>>(t, cap, special, nullptr);
     const int64_t blocks = (n + tpb - 1) / tpb;
-    k_hash_insert<<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, err, nullptr);
-    k_nbr_lookup<27><<<(unsigned)blocks, tpb, 0, st>>>(coords, n, coord_stride, t, cap - 1, special, nbr_out, err,
-                                                      nullptr);
-    return cudaGetLastError() == cudaSuccess ? TB_OK : TB_ERR_CUDA;
+    // every call rebuilds the table from scratch: the previous call's contents are cleared here.
+    // Each launch's own status is checked (cudaLaunchKernelEx returns it), so an error left
+    // pending by unrelated earlier work is neither reported as this call's nor cleared.
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(tpb);
+    cfg.stream = st;
+    cfg.gridDim = dim3((unsigned)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)g_noalloc_sms[dev] * 16));
+    if (cudaLaunchKernelEx(&cfg, k_hash_clear, t, cap, special, no_gate) != cudaSuccess) return TB_ERR_CUDA;
+    cfg.gridDim = dim3((unsigned)blocks);
+    if (cudaLaunchKernelEx(&cfg, k_hash_insert, coords, n, coord_stride, t, cap - 1, special, no_err, no_gate) !=
+        cudaSuccess)
+        return TB_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, k_nbr_lookup<27>, coords, n, coord_stride, (const Slot*)t, cap - 1,
+                           (const int*)special, nbr_out, no_err, no_gate) != cudaSuccess)
+        return TB_ERR_CUDA;
+    return TB_OK;
 }
