@@ -251,7 +251,9 @@ def run_gpu(args):
 
     if world > 1:
         from trellis_cpp_b200 import dist as tbdist
-        runner = tbdist.SlabRunner(coords_np, CI, dev, g)
+        uid = [ops.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        runner = tbdist.SlabRunner(coords_np, CI, dev, g, uid[0])
         step = lambda: runner.step(w1, w2)  # noqa: E731  (replaced by the recorded graph below)
         n_local = runner.n_owned
         nbr_for_flops = None
@@ -285,7 +287,7 @@ def run_gpu(args):
         step()
     torch.cuda.synchronize()
     if world > 1:
-        # each rank replays one CUDA graph per step (map, packs, NCCL halo exchanges, convs)
+        # each rank replays one CUDA graph per step (map, both convs with their NCCL halo exchanges)
         runner.capture(w1, w2)
         step = runner.replay
     if nbr_for_flops is not None:
@@ -347,6 +349,49 @@ def run_gpu(args):
         kernel_stats = {"conv_ms_avg": conv_ms, "conv1_ms": float(np.mean(c1)), "conv2_ms": float(np.mean(c2)),
                         "map_ms_est": ms_step - float(np.mean(c1)) - float(np.mean(c2))}
 
+    parity = None
+    if world > 1:
+        # per-rank times of the map and of each conv (eager steps after the timed replays; a conv
+        # call includes its halo exchange, overlapped with the interior planes), slowest rank
+        evs = []
+        for _ in range(max(3, min(args.steps, 10))):
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            e[0].record()
+            runner.dist.build_map()
+            e[1].record()
+            runner.dist.submconv(runner.feats, w1, None, epi="silu", out=runner.h)
+            e[2].record()
+            runner.dist.submconv(runner.h, w2, None, out=runner.out)
+            e[3].record()
+            evs.append(e)
+        torch.cuda.synchronize()
+        map_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in evs]))
+        conv_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in evs] + [e[2].elapsed_time(e[3]) for e in evs]))
+        tm = torch.tensor([conv_ms, map_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        conv_ms_max, map_ms_max = float(tm[0].item()), float(tm[1].item())
+        flops_gpu = 2.0 * CI * CO * pairs_total / world        # one conv's algorithmic FLOPs per GPU
+        achieved = flops_gpu / (conv_ms_max / 1e3) / 1e12
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                    "frac": achieved / peak_tf, "traffic": None, "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                    "kernel": "k_submconv_pair (per GPU: one conv's owned-row FLOPs / the slowest rank's conv "
+                              "time, halo exchange included)", "flops_per_launch": flops_gpu}
+        kernel_stats = {"conv_ms_slowest_rank": conv_ms_max, "map_ms_slowest_rank": map_ms_max,
+                        "conv_ms_this_rank": conv_ms, "map_ms_this_rank": map_ms}
+        # every owned row against the single-GPU step of the whole shell, run on each rank's GPU
+        r = runner.check_against_single_gpu(w1, w2)
+        rel = torch.tensor([r["max_abs"] / max(r["max_ref"], 1e-30)], device=dev, dtype=torch.float64)
+        dist.all_reduce(rel, op=dist.ReduceOp.MAX)
+        cnt = torch.tensor([r["rows_checked"], r["rows_bit_exact"]], device=dev, dtype=torch.int64)
+        dist.all_reduce(cnt)
+        mrel = float(rel.item())
+        parity = {"vs": "the single-GPU step (map, conv, conv) of the whole shell, on each rank's GPU",
+                  "rows_checked": int(cnt[0].item()), "rows_bit_exact": int(cnt[1].item()),
+                  "bit_exact": bool(int(cnt[1].item()) == int(cnt[0].item())), "max_rel": mrel, "tol": 1e-2,
+                  "ok": bool(mrel < 1e-2 and int(cnt[0].item()) == n_total),
+                  "note": "slab-local rows sum each row's 27 taps in another order (axes relabelled to put z "
+                          "first), so bf16 outputs may differ by an ulp"}
+
     # ---- end to end through the host-buffer C-ABI call (pinned host in, host out)
     e2e = None
     if world == 1 and not args.no_e2e:
@@ -370,8 +415,46 @@ def run_gpu(args):
                "d2h_bytes_per_step": int(out_h.numel() * 2), "steps": k_e2e, "ms_per_step": dt * 1e3,
                "call": "tb_submconv_stack_host"}
 
+    if world > 1 and not args.no_e2e:
+        # end to end per rank: this rank's local coordinates and owned features from pinned host
+        # memory, the slab's map and both convs (halo exchanges inside), owned output rows back
+        rows_np = runner.rows.cpu().numpy()
+        coords_loc_h = torch.from_numpy(np.ascontiguousarray(coords_np[rows_np])).pin_memory()
+        feats_own_h = runner.feats[runner.owned].cpu().pin_memory()
+        out_own_h = torch.empty((runner.n_owned, CO), dtype=torch.bfloat16).pin_memory()
+        coords_loc_d = torch.empty(coords_loc_h.shape, dtype=torch.int32, device=dev)
+
+        def e2e_step():
+            coords_loc_d.copy_(coords_loc_h, non_blocking=True)
+            runner.feats[runner.owned].copy_(feats_own_h, non_blocking=True)
+            runner.dist.load_coords(coords_loc_d)
+            runner.step(w1, w2)
+            out_own_h.copy_(runner.out[runner.owned], non_blocking=True)
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        k_e2e = max(3, min(args.steps, 10))
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(k_e2e):
+            e2e_step()
+        b.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([a.elapsed_time(b) / k_e2e], device=dev, dtype=torch.float64)
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        nb = torch.tensor([coords_loc_h.numel() * 4 + feats_own_h.numel() * 2, out_own_h.numel() * 2],
+                          device=dev, dtype=torch.int64)
+        dist.all_reduce(nb)
+        e2e_ms = float(te.item())
+        e2e = {"value": n_total / (e2e_ms / 1e3), "unit": "voxels/s", "h2d_bytes_per_step": int(nb[0].item()),
+               "d2h_bytes_per_step": int(nb[1].item()), "steps": k_e2e, "ms_per_step": e2e_ms,
+               "call": "per rank: pinned H2D of local coords + owned features, tb_dist_load_coords, "
+                       "tb_dist_build_map, tb_dist_submconv x2, D2H of owned rows (CUDA events, slowest rank)"}
+
     cpu_baseline = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and not args.no_cpu:
         feats_c, wt1, wt2, nbr_c = _cpu_inputs(coords_np)
         nthreads = os.cpu_count() or 1
         sample = min(n_total, 1 << 18)
@@ -380,6 +463,8 @@ def run_gpu(args):
                         "sample": f"oracle port: full single-threaded neighbor map ({n_total} voxels, "
                                   f"{t_map:.2f} s) + both fp32 convs on {sample} rows with {nthreads} threads "
                                   f"({t_conv:.2f} s); per-voxel times summed"}
+    if world > 1:
+        dist.barrier()              # the other ranks wait while rank 0 times the CPU baseline
 
     launches_per_step = ops.NBR_MAP_LAUNCHES + 2   # neighbor map, conv, conv
     if world > 1:
@@ -402,6 +487,8 @@ def run_gpu(args):
             "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps, "clocks": clocks, "kernels": kernel_stats,
         }
+        if parity is not None:
+            line["parity"] = parity
         if world == 1 and not args.no_configs:
             # every other BASELINE configuration, timed after the headline (not part of its value)
             line["configs"] = run_configs(dev, max(3, min(args.steps, 20)), max(3, args.warmup),

@@ -125,7 +125,8 @@ tb_status tb_submconv(tb_ctx* ctx, const int32_t* nbr, int64_t n,
 /* tb_submconv_range: the output rows [row0, row0 + nrows) of tb_submconv, the reference's
  * submconv_range(r0, nr) (src/sparse.cpp:64-79) used to chunk a conv over voxels. nbr, feats
  * and out are the whole n-row arrays (out [n][co]); only the range's rows of out are written,
- * and its inputs may be any rows of feats. row0 must be a multiple of 256. */
+ * and its inputs may be any rows of feats. row0 may be any row: the tensor-core kernels run the
+ * whole tiles that hold the range and store only its rows. */
 tb_status tb_submconv_range(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
                             const void* feats, int ci, const void* weight, const float* bias,
                             int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
@@ -303,6 +304,75 @@ tb_status tb_gather_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int6
                          int64_t row_bytes, void* out);
 tb_status tb_scatter_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t m,
                           int64_t row_bytes, void* out);
+
+/* ---- multi-GPU sharded convs: z-slabs with a one-plane NCCL halo --------------------------
+ * No reference counterpart: the reference is single-GPU (src/sparse.cpp:94-118 only chunks
+ * output rows on one device). These calls let its per-stage caller (src/shape_decoder.cpp:91-113:
+ * build_neighbor_table, then the stage's sparse_submconv calls) run one process per GPU: each rank
+ * partitions the stage's voxels, builds the map of its slab and runs each conv on its owned rows,
+ * with the halo exchanged inside the conv call. Callable from C/C++ without torch.
+ *
+ * tb_nccl_unique_id / tb_nccl_comm_create / tb_nccl_comm_destroy: a communicator for callers
+ *   that have none (rank 0 makes the 128-byte id, every rank receives it out of band, e.g. over
+ *   torch.distributed or MPI). NCCL is loaded at run time (libnccl.so.2, the copy already in the
+ *   process when there is one); TB_ERR_UNSUPPORTED where it cannot be loaded. A communicator
+ *   passed to tb_dist_create must come from that same library.
+ * tb_dist_create: a sharding handle on ctx's device for `rank` of `world` (nccl_comm: an
+ *   ncclComm_t of `world` ranks). The dist enqueues on ctx's stream and on a communication
+ *   stream of its own; it owns neither ctx nor the communicator. With nccl_comm NULL nothing is
+ *   exchanged: the caller puts the halo rows into feats before each tb_dist_submconv (one process
+ *   driving several slabs, or world == 1).
+ * tb_dist_partition_zslab: every rank passes the same voxel set (device coords [n][stride]). The
+ *   z axis is cut into `world` slabs of whole planes at voxel-count quantiles (tb_zslab_cuts);
+ *   this rank owns z_lo <= z < z_hi and holds the neighbours' planes z_lo-1 and z_hi as a halo.
+ *   Its local rows are [plane z_lo-1 | owned planes in z order | plane z_hi], each plane in the
+ *   input's order, so the owned rows are local rows [owned_begin, owned_begin + n_owned).
+ *   Synchronises (two small read-backs). Fails when the voxels span fewer z planes than ranks.
+ * tb_dist_local_rows: the global row of every local row (device int32 [n_local]), to gather a
+ *   stage's features into local order (tb_gather_rows) and scatter owned outputs back.
+ * tb_dist_load_coords: replace the local coordinates with coords_local (device [n_local][stride],
+ *   the local rows' coordinates in local order, e.g. uploaded from a host copy); the next
+ *   tb_dist_build_map uses them.
+ * tb_dist_build_map: the neighbor map of the local rows (dist-owned), tb_build_neighbor_map's map
+ *   of those rows up to a relabelling of taps (it is built on (z, x, y); tb_dist_submconv
+ *   permutes the weight's taps to match).
+ * tb_dist_submconv: one conv of tb_submconv's semantics on the local rows: feats [n_local][ci]
+ *   holds the input's owned rows; the call fills its halo rows from the neighbours (NCCL send/recv
+ *   of the edge planes, on the communication stream) while the interior planes are computed, then
+ *   computes the two edge planes. out [n_local][co]: owned rows written, halo rows untouched;
+ *   feats's halo rows are overwritten. Same dtype and shape rules as tb_submconv. Rows match the
+ *   single-GPU conv up to fp32 accumulation order.
+ * tb_dist_count_valid_pairs: present (voxel, tap) pairs over the owned rows; synchronises.
+ * tb_dist_local_map: the dist-owned local map (device int32 [27][n_local]) after build_map. */
+typedef struct tb_dist tb_dist;
+typedef struct tb_zslab {
+    int32_t z_lo, z_hi;             /* owned planes: z_lo <= z < z_hi */
+    int64_t n_local;                /* local rows: halo plane z_lo-1, owned planes, halo plane z_hi */
+    int64_t n_owned;
+    int64_t owned_begin;            /* owned rows are local rows [owned_begin, owned_begin + n_owned) */
+    int64_t n_halo_lo, n_halo_hi;   /* rows of planes z_lo-1 and z_hi (received) */
+    int64_t n_edge_lo, n_edge_hi;   /* rows of planes z_lo and z_hi-1 (sent) */
+} tb_zslab;
+
+tb_status tb_nccl_unique_id(uint8_t* id /* [128] */);
+tb_status tb_nccl_comm_create(const uint8_t* id /* [128] */, int rank, int world, int device, void** comm);
+tb_status tb_nccl_comm_destroy(void* comm);
+tb_status tb_dist_create(tb_ctx* ctx, void* nccl_comm, int rank, int world, tb_dist** out);
+tb_status tb_dist_destroy(tb_dist* d);
+const char* tb_dist_last_error(const tb_dist* d);
+tb_status tb_dist_partition_zslab(tb_dist* d, const int32_t* coords, int64_t n, int coord_stride, tb_zslab* slab);
+tb_status tb_dist_local_rows(tb_dist* d, int32_t* rows);
+tb_status tb_dist_load_coords(tb_dist* d, const int32_t* coords_local);
+tb_status tb_dist_build_map(tb_dist* d);
+tb_status tb_dist_local_map(const tb_dist* d, const int32_t** nbr);
+tb_status tb_dist_submconv(tb_dist* d, void* feats, int ci, const void* weight, const float* bias, int co,
+                           tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
+tb_status tb_dist_count_valid_pairs(tb_dist* d, int64_t* pairs);
+/* The slab cut on the host (what tb_dist_partition_zslab computes from its histogram): counts
+ * [nz] = voxels of plane z_min + i; cuts [world + 1]: cuts[0] the first occupied plane,
+ * cuts[world] one past the last, slab r = [cuts[r], cuts[r+1]) with at least one plane each.
+ * TB_ERR_INVALID_ARG when the occupied range has fewer planes than ranks. */
+tb_status tb_zslab_cuts(const int64_t* counts, int32_t nz, int32_t z_min, int world, int32_t* cuts);
 
 /* ---- model and input files, read without ggml --------------------------------------------
  * GGUF checkpoints as the reference's tools/convert.py writes them and src/trellis_model.cpp:96-137

@@ -35,7 +35,11 @@ def _worker(rank, world, init_file, result_dir):
         scatter = lambda t, idx, src: t.index_copy_(0, idx.long(), src)       # noqa: E731
         own = torch.from_numpy(plan.own_local)
         assert np.array_equal(plan.local_rows()[plan.own_local], plan.owned)
-        assert np.all(np.diff(plan.local_rows()) > 0)           # local rows in global order
+        zl = coords[plan.local_rows(), -1]
+        assert np.all(np.diff(zl) >= 0)                          # local rows ordered by z ...
+        same_z = np.diff(zl) == 0
+        assert np.all(np.diff(plan.local_rows())[same_z] > 0)   # ... and by input order within a plane
+        assert np.array_equal(plan.own_local, np.arange(plan.own_local[0], plan.own_local[0] + plan.n_owned))
         x = torch.full((plan.n_local, 16), float("nan"), dtype=torch.float32)
         x[own] = torch.from_numpy(feats[plan.owned])
         tbdist.exchange_halo(plan, x, gather, scatter)
@@ -104,3 +108,26 @@ def test_slab_plan_edge_cases(tb):
     # more ranks than planes cannot be cut into slabs
     with pytest.raises(ValueError):
         tbdist.plan_slabs(c, 13, 0)
+
+
+def test_host_cut_matches_library_cut(tb):
+    """tb_zslab_cuts (the cut tb_dist_partition_zslab makes from its device histogram) equals
+    the host planner's slab_bounds on shells, boxes, sparse planes and more ranks."""
+    from trellis_cpp_b200 import dist as tbdist, ops, synth
+    rng = np.random.default_rng(8)
+    cases = [synth.coords_for("c1"), synth.coords_for("c2")]
+    sparse = rng.integers(0, 40, (500, 3)).astype(np.int32)
+    sparse[:, 2] = rng.choice([3, 4, 9, 17, 18, 30, 31, 32, 39], 500)       # empty planes between
+    cases.append(sparse)
+    cases.append(np.array([[0, 0, 5], [0, 0, 6], [1, 1, 7]], np.int32))
+    for c in cases:
+        z = c[:, -1].astype(np.int64)
+        zmin = int(z.min()) - 3                                                # leading empty planes
+        counts = np.bincount(z - zmin, minlength=int(z.max()) - zmin + 5)     # and trailing ones
+        nplanes = int(z.max() - z.min() + 1)
+        for world in (1, 2, 3, 4, 8, 16):
+            if world > nplanes:
+                with pytest.raises(ops.TBError):
+                    ops.zslab_cuts(counts, zmin, world)
+                continue
+            assert np.array_equal(ops.zslab_cuts(counts, zmin, world), tbdist.slab_bounds(z, world)), world

@@ -62,16 +62,46 @@ def test_range_writes_only_its_rows(tb):
     assert not out[:512].any() and not out[1512:].any()
 
 
-def test_range_rejects_unaligned_start(tb):
+@pytest.mark.parametrize("ci,co,dtype,path", [(64, 64, torch.bfloat16, "pair"), (128, 64, torch.bfloat16, "brick"),
+                                              (32, 32, torch.float16, "gather"), (24, 40, torch.float32, "auto")])
+def test_range_any_start_row(tb, ci, co, dtype, path):
+    """Ranges may start and end anywhere: the kernels run the whole tiles that hold the range and
+    store only its rows (the slab-local convs of the multi-GPU path start mid-tile)."""
+    from trellis_cpp_b200 import ops
+    n = 3000
+    coords, f, w, b = _conv_inputs(n, ci, co, dtype, 4, 20)
+    nbr = ops.build_neighbor_table(coords)
+    ops.set_conv_path(path)
+    try:
+        whole = ops.sparse_submconv(f, nbr, w, b, out_dtype=torch.float32)
+        out = torch.zeros_like(whole)
+        for r0, nr in ((100, 200), (300, 1), (301, 1000), (1301, 1699)):
+            ops.sparse_submconv_range(f, nbr, w, b, r0, nr, out)
+        out2 = torch.zeros_like(whole)
+        ops.sparse_submconv_range(f, nbr, w, b, 777, 555, out2)
+        ops.check_device()
+    finally:
+        ops.set_conv_path("auto")
+    assert not out[:100].any()
+    assert not out2[:777].any() and not out2[777 + 555:].any()
+    if path in ("pair", "auto"):
+        assert torch.equal(out[100:], whole[100:])
+        assert torch.equal(out2[777:1332], whole[777:1332])
+    else:
+        assert max_rel(out[100:].cpu().numpy(), whole[100:].cpu().numpy()) < 1e-5
+        assert max_rel(out2[777:1332].cpu().numpy(), whole[777:1332].cpu().numpy()) < 1e-5
+
+
+def test_range_rejects_bad_bounds(tb):
     from trellis_cpp_b200 import ops
     coords, f, w, b = _conv_inputs(600, 64, 64, torch.bfloat16, 4, 20)
     nbr = ops.build_neighbor_table(coords)
     out = torch.zeros((600, 64), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ops.TBError) as e:
-        ops.sparse_submconv_range(f, nbr, w, b, 100, 200, out)
+        ops.sparse_submconv_range(f, nbr, w, b, 512, 200, out)      # past the end
     assert e.value.status == 1
     with pytest.raises(ops.TBError):
-        ops.sparse_submconv_range(f, nbr, w, b, 512, 200, out)      # past the end
+        ops.sparse_submconv_range(f, nbr, w, b, -1, 10, out)
 
 
 def _stack_both_ways(coords_np, ci, co, seed):

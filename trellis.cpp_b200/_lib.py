@@ -37,6 +37,12 @@ class C2SParams(ctypes.Structure):
                 ("conv1_w", _vp), ("conv1_b", _vp), ("conv2_w", _vp), ("conv2_b", _vp)]
 
 
+class ZSlab(ctypes.Structure):
+    """tb_zslab (include/tb_sparse.h)."""
+    _fields_ = [("z_lo", _i32), ("z_hi", _i32), ("n_local", _i64), ("n_owned", _i64), ("owned_begin", _i64),
+                ("n_halo_lo", _i64), ("n_halo_hi", _i64), ("n_edge_lo", _i64), ("n_edge_hi", _i64)]
+
+
 SIGNATURES = {
     "tb_status_string": (ctypes.c_char_p, [_st]),
     "tb_version": (ctypes.c_char_p, []),
@@ -78,6 +84,20 @@ SIGNATURES = {
     "tb_io_last_error": (ctypes.c_char_p, []),
     "tb_sparse_c2s": (_st, [_vp, _vp, _i64, _int, _vp, _int, _int, ctypes.POINTER(C2SParams), _vp, _int, _int,
                             _i64, _vp, _vp, _vp, ctypes.POINTER(_i64)]),
+    "tb_nccl_unique_id": (_st, [_vp]),
+    "tb_nccl_comm_create": (_st, [_vp, _int, _int, _int, ctypes.POINTER(_vp)]),
+    "tb_nccl_comm_destroy": (_st, [_vp]),
+    "tb_dist_create": (_st, [_vp, _vp, _int, _int, ctypes.POINTER(_vp)]),
+    "tb_dist_destroy": (_st, [_vp]),
+    "tb_dist_last_error": (ctypes.c_char_p, [_vp]),
+    "tb_dist_partition_zslab": (_st, [_vp, _vp, _i64, _int, ctypes.POINTER(ZSlab)]),
+    "tb_dist_local_rows": (_st, [_vp, _vp]),
+    "tb_dist_load_coords": (_st, [_vp, _vp]),
+    "tb_dist_build_map": (_st, [_vp]),
+    "tb_dist_local_map": (_st, [_vp, ctypes.POINTER(_vp)]),
+    "tb_dist_submconv": (_st, [_vp, _vp, _int, _vp, _vp, _int, _int, _int, _int, _vp]),
+    "tb_dist_count_valid_pairs": (_st, [_vp, ctypes.POINTER(_i64)]),
+    "tb_zslab_cuts": (_st, [_vp, _i32, _i32, _int, _vp]),
 }
 
 _lib = None

@@ -135,8 +135,8 @@ tb_status tb_submconv_range(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t 
                             tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
     if (!ctx) return TB_ERR_INVALID_ARG;
     if (n < 0 || ci <= 0 || co <= 0) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: n < 0 or channels <= 0");
-    if (row0 < 0 || nrows < 0 || row0 + nrows > n || row0 % 256 != 0)
-        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_range: need 0 <= row0, row0 % 256 == 0, row0 + nrows <= n");
+    if (row0 < 0 || nrows < 0 || row0 + nrows > n)
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv_range: need 0 <= row0 and row0 + nrows <= n");
     if (epi != TB_EPI_NONE && epi != TB_EPI_SILU) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: bad epilogue");
     if (dtype != TB_F32 && dtype != TB_F16 && dtype != TB_BF16)
         return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_submconv: bad dtype");

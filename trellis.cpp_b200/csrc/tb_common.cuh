@@ -105,7 +105,8 @@ tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t 
                             const void* feats, int ci, const void* weight, const float* bias, int co,
                             tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
 // The conv kernels compute output rows [row0, row0 + nrows) of an n-row map (tap stride and
-// sentinel n); row0 is a multiple of 256.
+// sentinel n); the tensor-core kernels run whole tiles from the one holding row0 and store only
+// the range's rows.
 tb_status tb_conv_f32_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
                              const float* feats, int ci, const float* weight, const float* bias, int co,
                              tb_epilogue epi, float* out);

@@ -95,6 +95,7 @@ struct BrickParams {
     int out_kind, epi;
     int ntiles, ncb, nkc, nb;  // ntiles: tiles of the range
     int tile0;                 // first tile of the range
+    int64_t row_begin;         // rows before it are computed (whole tiles) but not stored
     int64_t row_end;           // rows at or past it are not stored
     int nbst, nbst_log2;   // weight stages (2, 4 or 8)
     int brick_cap;         // rows per brick buffer (multiple of kBox)
@@ -427,7 +428,7 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
             if (threadIdx.x == 0) { TB_STAMP(4, it); TB_PROGRESS(6, it + 1); }
             tc_fence_after();
             const int64_t row = (int64_t)tile * kTileM + q * 32 + lane;
-            const bool valid = row < p.row_end;
+            const bool valid = row >= p.row_begin && row < p.row_end;
             uint8_t* orow = p.out + ((size_t)row * p.co + (size_t)cb * p.nb) * esize;
             const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
             const uint32_t d0 = lane_base + (uint32_t)(d * p.nb);
@@ -498,6 +499,7 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64
     p.out_kind = out_dtype == TB_F32 ? 0 : (out_dtype == TB_F16 ? 1 : 2);
     p.epi = epi;
     p.tile0 = (int)(row0 / kTileM);
+    p.row_begin = row0;
     p.row_end = row0 + nrows;
     p.ntiles = (int)((row0 + nrows + kTileM - 1) / kTileM) - p.tile0;
     p.ncb = co / nb;

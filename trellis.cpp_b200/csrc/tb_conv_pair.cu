@@ -90,7 +90,8 @@ struct PairParams {
     int out_kind, epi;
     int ntiles, npairs;    // npairs: end of the pair range (absolute)
     int pr0;               // first pair of the range (rows 256 * pr0 ...)
-    int64_t row_end;       // rows at or past it are computed (whole pairs) but not stored
+    int64_t row_begin;     // rows before it and at or past row_end are computed (whole pairs)
+    int64_t row_end;       // but not stored
     int ring_rows;               // multiple of kBox
     int nbr_bulk;                // map pointer 16-byte aligned: tiles fetch indices with bulk copies
     uint32_t w_tap_bytes;        // (co/2) rows x 128 B, rounded up to 1024
@@ -526,7 +527,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 mbar_arrive_cluster_relaxed(de + 8, 0);
             }
             const int64_t row = (int64_t)(2 * pr + (int)rank) * kTileM + q * 32 + lane;
-            if (row < p.row_end) {
+            if (row >= p.row_begin && row < p.row_end) {
                 uint8_t* orow = p.out + (size_t)row * p.co * esize;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -583,9 +584,10 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_
     p.out_kind = out_dtype == TB_F32 ? 0 : (out_dtype == TB_F16 ? 1 : 2);
     p.epi = epi;
     p.ntiles = (int)((n + kTileM - 1) / kTileM);
-    // output rows [row0, row0 + nrows): row0 is a multiple of 256 (one pair of tiles)
+    // output rows [row0, row0 + nrows): whole pairs of tiles from the one holding row0
     p.pr0 = (int)(row0 / (2 * kTileM));
     p.npairs = (int)((row0 + nrows + 2 * kTileM - 1) / (2 * kTileM));
+    p.row_begin = row0;
     p.row_end = row0 + nrows;
     const int nhalf = co / 2;
     p.w_tap_bytes = ((uint32_t)nhalf * 128u + 1023u) & ~1023u;

@@ -57,6 +57,7 @@ struct ConvParams {
     int epi;
     int ntiles, ncb, nkc;  // ntiles: tiles of the range
     int tile0;             // first tile of the range
+    int64_t row_begin;     // rows before it are computed (whole tiles) but not stored
     int64_t row_end;       // rows at or past it are not stored
     int kc;             // channels per chunk (16, 32 or 64)
     int nb;             // accumulator columns per work unit
@@ -267,7 +268,7 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ 
             if (threadIdx.x == 0) TB_STAMP(2, it);
             tc_fence_after();
             const int64_t pos = (int64_t)tile * kTileM + q * 32 + lane;
-            const bool valid = pos < p.row_end;
+            const bool valid = pos >= p.row_begin && pos < p.row_end;
             const int64_t row = (valid && p.perm) ? (int64_t)__ldg(p.perm + pos) : pos;
             uint8_t* orow = p.out + ((size_t)row * p.co + (size_t)cb * p.nb) * esize;
             for (int c0 = 0; c0 < p.nb; c0 += 16) {
@@ -340,6 +341,7 @@ tb_status tb_conv_tc_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t 
     p.out_kind = out_dtype == TB_F32 ? 0 : (out_dtype == TB_F16 ? 1 : 2);
     p.epi = epi;
     p.tile0 = (int)(row0 / kTileM);
+    p.row_begin = row0;
     p.row_end = row0 + nrows;
     p.ntiles = (int)((row0 + nrows + kTileM - 1) / kTileM) - p.tile0;
     p.ncb = co / nb;

@@ -7,19 +7,19 @@ The reference runs on one device and only chunks output rows within it
   planes, so every voxel belongs to exactly one rank). Rank r owns z in [z_lo, z_hi) and needs
   the planes z_lo-1 and z_hi of its neighbours as a halo: a 3x3x3 submanifold conv at an owned
   voxel reads only voxels within one plane.
-* The local rows are the owned rows and the two halo planes in ascending global order, so a
-  local neighbor map built over them gives every owned row exactly its global neighbors (tests
-  check this against the single-rank oracle), and a row's neighbors stay as close in the local
-  order as they are in the global one. (Halo rows appended after the owned rows put the
-  neighbors of every slab-boundary voxel at the far end of the array; the conv kernel streams
-  each tile's neighbor rows as contiguous ranges, and those stretched ranges made a rank's conv
-  up to 1.5x slower at 8 ranks.)
+* The local rows are the owned rows and the two halo planes ordered by z, each plane in the
+  input's order: [plane z_lo-1 | owned planes | plane z_hi]. A local neighbor map built over them
+  gives every owned row exactly its global neighbors (tests check this against the single-rank
+  oracle); the halo planes and the edge planes are contiguous ranges (received and sent in
+  place), and the interior planes, which need no halo, are one range.
 * :func:`exchange_halo` sends the boundary planes to the neighbouring ranks with point-to-point
   send/recv (NCCL over NVLink on GPUs, gloo in the CPU tests) into contiguous buffers and
   scatters them to the halo rows' local positions. Nothing else is communicated: no all-reduce,
   no all-gather.
-* :class:`SlabRunner` is the benchmark step on one rank: halo exchange of the input rows
-  overlapped with the local neighbor map, conv(SiLU), halo exchange of the intermediate rows, conv.
+* :class:`SlabRunner` is the benchmark step on one rank, through the C ABI (tb_dist_*): the slab's
+  neighbor map, conv(SiLU), conv, each conv exchanging its input's halo over NCCL while its
+  interior planes compute. :func:`plan_slabs` and :func:`exchange_halo` are the host-side
+  statement of the same plan and exchange, which the CPU tests run with gloo ranks.
 """
 from __future__ import annotations
 
@@ -36,10 +36,10 @@ class SlabPlan:
     world: int
     z_lo: int                  # owned planes: z_lo <= z < z_hi
     z_hi: int
-    owned: np.ndarray          # global row ids of owned voxels (ascending)
+    owned: np.ndarray          # global row ids of owned voxels, in local order (by z, then input order)
     halo_lo: np.ndarray        # global row ids of plane z_lo-1 (owned by rank-1), ascending
     halo_hi: np.ndarray        # global row ids of plane z_hi (owned by rank+1), ascending
-    local: np.ndarray          # global row ids of the local rows: owned + halo, ascending
+    local: np.ndarray          # global row ids of the local rows: owned + halo, ordered by z
     own_local: np.ndarray      # local positions of the owned rows
     send_lo: np.ndarray        # local positions of plane z_lo (sent to rank-1), ascending
     send_hi: np.ndarray        # local positions of plane z_hi-1 (sent to rank+1), ascending
@@ -55,7 +55,7 @@ class SlabPlan:
         return int(self.local.size)
 
     def local_rows(self) -> np.ndarray:
-        """Global row id of every local row (ascending)."""
+        """Global row id of every local row (by z, then input order)."""
         return self.local
 
 
@@ -91,7 +91,10 @@ def plan_slabs(coords: np.ndarray, world: int, rank: int) -> SlabPlan:
     owned = np.nonzero((z >= z_lo) & (z < z_hi))[0]
     halo_lo = np.nonzero(z == z_lo - 1)[0] if rank > 0 else np.zeros(0, np.int64)
     halo_hi = np.nonzero(z == z_hi)[0] if rank < world - 1 else np.zeros(0, np.int64)
-    local = np.sort(np.concatenate([owned, halo_lo, halo_hi]))
+    # local order: by plane, and within a plane the input order (a stable sort by z), as
+    # tb_dist_partition_zslab orders them: [plane z_lo-1 | plane z_lo .. z_hi-1 | plane z_hi]
+    sel = np.sort(np.concatenate([owned, halo_lo, halo_hi]))
+    local = sel[np.argsort(z[sel], kind="stable")]
     zl = z[local]
     # a sender packs its boundary plane in ascending global order, which is the order of the
     # receiver's halo positions for the same plane
@@ -101,6 +104,7 @@ def plan_slabs(coords: np.ndarray, world: int, rank: int) -> SlabPlan:
     recv_lo = np.nonzero(zl == z_lo - 1)[0] if rank > 0 else none
     recv_hi = np.nonzero(zl == z_hi)[0] if rank < world - 1 else none
     own_local = np.nonzero((zl >= z_lo) & (zl < z_hi))[0]
+    owned = local[own_local]
     return SlabPlan(rank, world, z_lo, z_hi, owned, halo_lo, halo_hi, local, own_local, send_lo, send_hi,
                     recv_lo, recv_hi)
 
@@ -158,60 +162,53 @@ def finish_halo(handle) -> None:
 
 
 class SlabRunner:
-    """The benchmark step on one rank of a NCCL group: map + conv(SiLU) + conv on a z-slab."""
+    """The benchmark step on one rank: map + conv(SiLU) + conv on a z-slab, through the C ABI's
+    tb_dist_* calls (the partition, the slab's neighbor map and convs whose halo exchange runs
+    inside the call over NCCL, overlapped with the interior planes).
 
-    launches_per_step = 0                 # set in __init__: map, packs and unpacks of 2 exchanges, 2 convs
+    Every rank builds the same global inputs (the generator is seeded alike), so the owned rows
+    can be checked against the single-GPU step (:meth:`check_against_single_gpu`)."""
 
-    def __init__(self, coords_np: np.ndarray, ci: int, device, generator):
+    launches_per_step = 0                 # set in __init__
+
+    def __init__(self, coords_np: np.ndarray, ci: int, device, generator, uid: bytes):
         from . import ops
         self.ops = ops
         self.rank = dist.get_rank()
         self.world = dist.get_world_size()
-        self.plan = plan_slabs(coords_np, self.world, self.rank)
-        moves = sum(int(a.size > 0) for a in (self.plan.send_lo, self.plan.send_hi, self.plan.recv_lo,
-                                              self.plan.recv_hi))
-        self.launches_per_step = ops.NBR_MAP_LAUNCHES + 2 * moves + 2
-        rows = self.plan.local_rows()
         self.device = device
-        self.coords = torch.from_numpy(np.ascontiguousarray(coords_np[rows])).to(device)
-        self.n_local = self.plan.n_local
-        self.n_owned = self.plan.n_owned
         self.ci = ci
-        # features of the owned rows are resident; halo rows are overwritten by the exchange each step
-        self.feats = torch.randn((self.n_local, ci), device=device, generator=generator).bfloat16()
-        self.nbr = torch.empty(27 * self.n_local, dtype=torch.int32, device=device)
+        self.coords_global = torch.from_numpy(np.ascontiguousarray(coords_np)).to(device)
+        self.n_total = coords_np.shape[0]
+        # the same global features on every rank (same seed); the rank's slab takes its rows
+        self.feats_global = torch.randn((self.n_total, ci), device=device, generator=generator).bfloat16()
+        self.dist = ops.Dist(device, self.rank, self.world, uid)
+        self.slab = self.dist.partition(self.coords_global)
+        self.rows = self.dist.local_rows().long()
+        self.n_local = int(self.slab.n_local)
+        self.n_owned = int(self.slab.n_owned)
+        self.owned = slice(int(self.slab.owned_begin), int(self.slab.owned_begin) + self.n_owned)
+        self.feats = self.feats_global[self.rows].contiguous()
         self.h = torch.zeros((self.n_local, ci), dtype=torch.bfloat16, device=device)
-        self.out = torch.empty((self.n_local, ci), dtype=torch.bfloat16, device=device)
-        self.idx = [torch.from_numpy(a.astype(np.int32)).to(device)
-                    for a in (self.plan.send_lo, self.plan.send_hi, self.plan.recv_lo, self.plan.recv_hi)]
-        self.own_local = torch.from_numpy(self.plan.own_local).to(device)
+        self.out = torch.zeros((self.n_local, ci), dtype=torch.bfloat16, device=device)
+        # our kernels per step: the map, and per conv the tap permutation plus up to three ranges
+        # (interior planes, the two edge planes)
+        self.launches_per_step = ops.NBR_MAP_LAUNCHES + 2 * 4
         self.graph = None
 
-    def _gather(self, x, idx):
-        return self.ops.gather_rows(x, idx)
-
-    def _scatter(self, x, idx, src):
-        return self.ops.scatter_rows(x, idx, src)
-
     def step(self, w1, w2):
-        ops = self.ops
-        # the feature halo does not depend on the map: its transfer overlaps the map build
-        pending = exchange_halo(self.plan, self.feats, self._gather, self._scatter, self.idx, wait=False)
-        ops.build_neighbor_table(self.coords, out=self.nbr)
-        finish_halo(pending)
-        ops.sparse_submconv(self.feats, self.nbr, w1, None, epi="silu", out=self.h)
-        exchange_halo(self.plan, self.h, self._gather, self._scatter, self.idx)
-        ops.sparse_submconv(self.h, self.nbr, w2, None, out=self.out)
+        self.dist.build_map()
+        self.dist.submconv(self.feats, w1, None, epi="silu", out=self.h)
+        self.dist.submconv(self.h, w2, None, out=self.out)
 
     def capture(self, w1, w2, warmup: int = 3) -> None:
-        """Record one step, both halo exchanges included, into a CUDA graph.
+        """Record one step (map, both convs and their NCCL halo exchanges) into a CUDA graph.
 
         With fewer voxels per rank the device work of a step shrinks to a few hundred
-        microseconds while issuing it from Python (about fourteen launches and two NCCL
-        exchanges per rank, with every rank's process on the same host) takes longer; replaying
-        the graph issues the whole step at once. The warm-up steps run on a side stream first so
-        that every buffer and NCCL connection exists before recording; the graph keeps the
-        buffers it records, so later replays reuse the same tensors."""
+        microseconds while issuing it from Python (about twenty launches and two NCCL groups per
+        rank, with every rank's process on one host) takes longer; replaying the graph issues the
+        whole step at once. Warm-up steps run on a side stream first so that every workspace and
+        NCCL connection exists before recording."""
         cur = torch.cuda.current_stream(self.device)
         side = torch.cuda.Stream(self.device)
         side.wait_stream(cur)
@@ -231,11 +228,31 @@ class SlabRunner:
 
     def count_valid_pairs(self) -> int:
         """Present (voxel, tap) pairs over the owned rows (the algorithmic work of one conv)."""
-        nb = self.nbr.view(27, self.n_local)[:, self.own_local]
-        return int((nb != self.n_local).sum().item())
+        return self.dist.count_valid_pairs()
+
+    def check_against_single_gpu(self, w1, w2) -> dict:
+        """The whole voxel set's step on this GPU alone (map, conv, conv), compared with the
+        owned rows of the sharded step; returns this rank's max|d|/max|ref| and bit-exact rows."""
+        ops = self.ops
+        n = self.n_total
+        nbr = ops.build_neighbor_table(self.coords_global)
+        h = ops.sparse_submconv(self.feats_global, nbr, w1, None, epi="silu")
+        ref = ops.sparse_submconv(h, nbr, w2, None)
+        mine = self.out[self.owned].float()
+        want = ref[self.rows[self.owned]].float()
+        same = (mine == want).all(dim=1)
+        d = (mine - want).abs().max()
+        scale = want.abs().max().clamp_min(1e-30)
+        ops.check_device()
+        res = {"rows_checked": int(self.n_owned), "rows_bit_exact": int(same.sum().item()),
+               "max_abs": float(d.item()), "max_ref": float(scale.item())}
+        del nbr, h, ref
+        assert n == self.coords_global.shape[0]
+        return res
 
     def close(self):
-        """Finish the device work and release the recorded graph; a graph that holds NCCL
-        calls must be gone before the process group is destroyed."""
+        """Finish the device work and release the recorded graph (it holds NCCL calls and must be
+        gone before the communicator), then the dist and its communicator."""
         torch.cuda.synchronize(self.device)
         self.graph = None
+        self.dist.close()

@@ -128,7 +128,7 @@ def sparse_submconv(feats: torch.Tensor, nbr: torch.Tensor, weight: torch.Tensor
 def sparse_submconv_range(feats: torch.Tensor, nbr: torch.Tensor, weight: torch.Tensor, bias, row0: int, nrows: int,
                           out: torch.Tensor, epi: str = "none") -> torch.Tensor:
     """Rows [row0, row0 + nrows) of :func:`sparse_submconv` written into ``out`` [N,Co] (the
-    reference's ``submconv_range``, src/sparse.cpp:64-79); row0 a multiple of 256."""
+    reference's ``submconv_range``, src/sparse.cpp:64-79); any row0."""
     _need_cuda(feats, nbr, weight, bias, out)
     n, ci = feats.shape
     co = weight.shape[0]
@@ -476,3 +476,123 @@ def read_slat(path: str):
                                coords.ctypes.data_as(ctypes.c_void_p), feats.ctypes.data_as(ctypes.c_void_p)),
               "tb_slat_read")
     return coords, feats, int(res.value)
+
+
+# ---- multi-GPU z-slabs (tb_dist_*) --------------------------------------------------------
+def zslab_cuts(counts: np.ndarray, z_min: int, world: int) -> np.ndarray:
+    """The slab cut of tb_zslab_cuts on the host: counts[i] = voxels of plane z_min + i; returns
+    int32 [world + 1] z boundaries (no GPU needed)."""
+    c = np.ascontiguousarray(counts, dtype=np.int64)
+    cuts = np.empty(world + 1, dtype=np.int32)
+    st = _lib.load().tb_zslab_cuts(ctypes.c_void_p(c.ctypes.data), c.size, int(z_min), int(world),
+                                   ctypes.c_void_p(cuts.ctypes.data))
+    check(st, "tb_zslab_cuts")
+    return cuts
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for :class:`Dist`; rank 0 makes it, every rank gets it."""
+    buf = (ctypes.c_uint8 * 128)()
+    check(_lib.load().tb_nccl_unique_id(ctypes.cast(buf, ctypes.c_void_p)), "tb_nccl_unique_id")
+    return bytes(buf)
+
+
+class Dist:
+    """One rank's share of a z-slab sharded voxel set (the tb_dist_* calls of the C ABI).
+
+    ``uid`` is the 128-byte id from :func:`nccl_unique_id` on rank 0, given to every rank; the
+    communicator is made by the library (tb_nccl_comm_create). Without ``uid`` nothing is
+    exchanged and the caller fills the halo rows (one process driving several slabs). Calls
+    enqueue on torch's current stream of ``device``."""
+
+    def __init__(self, device, rank: int, world: int, uid: bytes | None = None):
+        self.device = torch.device(device)
+        self.rank, self.world = rank, world
+        lib = _lib.load()
+        self.comm = ctypes.c_void_p()
+        if uid is not None and world > 1:
+            if len(uid) != 128:
+                raise ValueError("the NCCL unique id has 128 bytes")
+            idb = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+            check(lib.tb_nccl_comm_create(ctypes.cast(idb, ctypes.c_void_p), rank, world, self.device.index,
+                                          ctypes.byref(self.comm)), "tb_nccl_comm_create")
+        self.h = ctypes.c_void_p()
+        ctx = context(self.device)
+        check(lib.tb_dist_create(ctx, self.comm, rank, world, ctypes.byref(self.h)), "tb_dist_create", ctx)
+        self.slab = None
+
+    def _check(self, st, call):
+        if st != _lib.TB_OK:
+            d = _lib.load().tb_dist_last_error(self.h)
+            raise TBError(st, call, d.decode() if d else "")
+
+    def partition(self, coords: torch.Tensor) -> _lib.ZSlab:
+        """Plan this rank's slab of the global voxel set ``coords`` (int32 [N,3] or [N,4])."""
+        _need_cuda(coords)
+        context(self.device)
+        sl = _lib.ZSlab()
+        self._check(_lib.load().tb_dist_partition_zslab(self.h, _ptr(coords), coords.shape[0], coords.shape[1],
+                                                        ctypes.byref(sl)), "tb_dist_partition_zslab")
+        self.slab = sl
+        return sl
+
+    def local_rows(self) -> torch.Tensor:
+        """Global row ids of the local rows (int32 [n_local])."""
+        context(self.device)
+        out = torch.empty(max(1, self.slab.n_local), dtype=torch.int32, device=self.device)[: self.slab.n_local]
+        self._check(_lib.load().tb_dist_local_rows(self.h, _ptr(out)), "tb_dist_local_rows")
+        return out
+
+    def load_coords(self, coords_local: torch.Tensor) -> None:
+        _need_cuda(coords_local)
+        context(self.device)
+        self._check(_lib.load().tb_dist_load_coords(self.h, _ptr(coords_local)), "tb_dist_load_coords")
+
+    def build_map(self) -> None:
+        context(self.device)
+        self._check(_lib.load().tb_dist_build_map(self.h), "tb_dist_build_map")
+
+    def local_map(self) -> torch.Tensor:
+        """The local map ([27 * n_local] int32), a view of the dist-owned buffer (read only)."""
+        p = ctypes.c_void_p()
+        self._check(_lib.load().tb_dist_local_map(self.h, ctypes.byref(p)), "tb_dist_local_map")
+        return _device_view_int32(p.value, 27 * self.slab.n_local, self.device)
+
+    def submconv(self, feats: torch.Tensor, weight: torch.Tensor, bias=None, epi: str = "none", out_dtype=None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        """One conv on the local rows (halo exchange inside); owned rows of the result written."""
+        _need_cuda(feats, weight, bias)
+        n, ci = feats.shape
+        co = weight.shape[0]
+        if n != self.slab.n_local or weight.dtype != feats.dtype or weight.numel() != co * 27 * ci:
+            raise ValueError("feats must be [n_local, Ci] and weight [Co,27,Ci] of its dtype")
+        od = feats.dtype if out_dtype is None else out_dtype
+        if out is None:
+            out = torch.empty((n, co), dtype=od, device=feats.device)
+        context(self.device)
+        self._check(_lib.load().tb_dist_submconv(self.h, _ptr(feats), ci, _ptr(weight), _ptr(bias), co,
+                                                 _DT[feats.dtype], _DT[od], _EPI[epi], _ptr(out)),
+                    "tb_dist_submconv")
+        return out
+
+    def count_valid_pairs(self) -> int:
+        context(self.device)
+        v = ctypes.c_int64()
+        self._check(_lib.load().tb_dist_count_valid_pairs(self.h, ctypes.byref(v)), "tb_dist_count_valid_pairs")
+        return int(v.value)
+
+    def close(self) -> None:
+        lib = _lib.load()
+        if self.h:
+            lib.tb_dist_destroy(self.h)
+            self.h = ctypes.c_void_p()
+        if self.comm:
+            lib.tb_nccl_comm_destroy(self.comm)
+            self.comm = ctypes.c_void_p()
+
+
+def _device_view_int32(ptr: int, n: int, device) -> torch.Tensor:
+    """A torch int32 tensor over n elements of library-owned device memory (no copy, not owned)."""
+    class _Arr:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<i4", "data": (ptr, True), "version": 2}
+    return torch.as_tensor(_Arr(), device=device)
