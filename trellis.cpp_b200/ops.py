@@ -594,5 +594,5 @@ class Dist:
 def _device_view_int32(ptr: int, n: int, device) -> torch.Tensor:
     """A torch int32 tensor over n elements of library-owned device memory (no copy, not owned)."""
     class _Arr:
-        __cuda_array_interface__ = {"shape": (n,), "typestr": "<i4", "data": (ptr, True), "version": 2}
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<i4", "data": (ptr, False), "version": 2}
     return torch.as_tensor(_Arr(), device=device)
