@@ -160,14 +160,18 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- CPU legs
 def cpu_reference_step(coords, nbr_full, feats, wt1, wt2, sample, nthreads):
-    """One bounded CPU step of the reference algorithm (oracle port): the full neighbor map
-    (single-threaded, as src/sparse.cpp:21-39 is) and both convs on `sample` output rows.
-    Returns seconds per voxel."""
+    """One bounded CPU step of the reference algorithm: the full neighbor map, single-threaded as
+    src/sparse.cpp:21-39 is (the reference's own function compiled from its source where
+    oracle/_ref holds it, else the oracle port), and both convs (oracle port, fp32, all threads)
+    on `sample` output rows. Returns seconds per voxel."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     n = coords.shape[0]
     t0 = time.perf_counter()
-    oracle.build_neighbor_table(coords)
+    if oracle.ref_nbr_available():
+        oracle.ref_build_neighbor_table(coords)      # the reference's own std::unordered_map loop
+    else:
+        oracle.build_neighbor_table(coords)
     t_map = time.perf_counter() - t0
     row0 = (n - sample) // 2
     h = feats.copy()          # rows outside the sample stand in for the first conv's output
@@ -178,6 +182,13 @@ def cpu_reference_step(coords, nbr_full, feats, wt1, wt2, sample, nthreads):
     oracle.submconv_f32_mt_range(nbr_full, h, wt2, row0, sample, nthreads=nthreads)
     t_conv = time.perf_counter() - t0
     return t_map / n + t_conv / sample, t_map, t_conv
+
+
+def _map_kind():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    return ("the reference's own build_neighbor_table, compiled from src/sparse.cpp"
+            if oracle.ref_nbr_available() else "the oracle port of build_neighbor_table")
 
 
 def _cpu_inputs(coords):
@@ -219,8 +230,9 @@ def run_reference(args):
         "data": "synthetic (seeded noisy shell, random N(0,1) features, N(0,1/(27*64)) weights)",
         "config": {"workload": "c4: res-1024 noisy shell, map + conv(SiLU) + conv, C=64", "voxels": n},
         "cpu_baseline": {"value": value, "unit": "voxels/s", "cores": nthreads, "kind": "port",
-                         "sample": f"full single-threaded neighbor map over {n} voxels + both fp32 convs on "
-                                   f"{sample} output rows (threads={nthreads}); per-voxel times summed"},
+                         "sample": f"full single-threaded neighbor map over {n} voxels ({_map_kind()}) + both "
+                                   f"fp32 convs (oracle port) on {sample} output rows (threads={nthreads}); "
+                                   f"per-voxel times summed"},
         "e2e": {"value": value, "unit": "voxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     _emit(line)
@@ -460,9 +472,9 @@ def run_gpu(args):
         sample = min(n_total, 1 << 18)
         spv, t_map, t_conv = cpu_reference_step(coords_np, nbr_c, feats_c, wt1, wt2, sample, nthreads)
         cpu_baseline = {"value": 1.0 / spv, "unit": "voxels/s", "cores": nthreads, "kind": "port",
-                        "sample": f"oracle port: full single-threaded neighbor map ({n_total} voxels, "
-                                  f"{t_map:.2f} s) + both fp32 convs on {sample} rows with {nthreads} threads "
-                                  f"({t_conv:.2f} s); per-voxel times summed"}
+                        "sample": f"full single-threaded neighbor map ({n_total} voxels, {t_map:.2f} s; "
+                                  f"{_map_kind()}) + both fp32 convs (oracle port) on {sample} rows with "
+                                  f"{nthreads} threads ({t_conv:.2f} s); per-voxel times summed"}
     if world > 1:
         dist.barrier()              # the other ranks wait while rank 0 times the CPU baseline
 

@@ -18,6 +18,8 @@ Functions and the reference lines they follow (paths inside pwilkin/trellis.cpp)
 * :func:`dual_grid_mesh` -- ``src/dual_grid.cpp:16-56``
 * :func:`ref_dual_grid_mesh` -- the reference's own ``dual_grid_to_mesh``, compiled from its
   sources into ``oracle/_ref/`` (only where those sources were present at build time)
+* :func:`ref_build_neighbor_table` -- the reference's own ``build_neighbor_table``
+  (``src/sparse.cpp:21-39``, its ``std::unordered_map`` loop), compiled likewise
 """
 from __future__ import annotations
 
@@ -30,8 +32,10 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _SO = os.path.join(_HERE, "liboracle.so")
 REF_MESH_SO = os.path.join(_HERE, "_ref", "libref_dual_grid.so")
+REF_NBR_SO = os.path.join(_HERE, "_ref", "libref_nbr.so")
 _lib = None
 _ref_mesh = None
+_ref_nbr = None
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _u8p = ctypes.POINTER(ctypes.c_uint8)
@@ -302,3 +306,25 @@ def ref_dual_grid_mesh(coords: np.ndarray, feats7: np.ndarray, res: int):
     f = _ref_mesh.ref_dual_grid_mesh(_p(c, _i32p), n, _p(f7, _f32p), res, _p(verts, _f32p), _p(faces, _i32p),
                                      6 * n)
     return verts, faces[:f].copy()
+
+
+def ref_nbr_available() -> bool:
+    return os.path.exists(REF_NBR_SO)
+
+
+def ref_build_neighbor_table(coords: np.ndarray) -> np.ndarray:
+    """The reference's own ``trellis::build_neighbor_table`` (``oracle/_ref``), single-threaded:
+    tap-major int32 ``[27*N]``, sentinel N. Coordinates int32 [N,3] or [N,4] (batch ignored, as
+    the reference's (x,y,z) table has no batch)."""
+    global _ref_nbr
+    if _ref_nbr is None:
+        L = ctypes.CDLL(REF_NBR_SO)
+        L.ref_build_neighbor_table.restype = ctypes.c_int
+        L.ref_build_neighbor_table.argtypes = [_i32p, ctypes.c_int64, ctypes.c_int, _i32p]
+        _ref_nbr = L
+    c = np.ascontiguousarray(coords, dtype=np.int32)
+    n, stride = c.shape
+    out = np.empty(27 * n, dtype=np.int32)
+    if _ref_nbr.ref_build_neighbor_table(_p(c, _i32p), n, stride, _p(out, _i32p)) != 0:
+        raise ValueError("ref_build_neighbor_table failed")
+    return out

@@ -113,3 +113,14 @@ def test_block_layout_shuffled_shell_with_duplicates(tb):
     c = np.concatenate([c, c[rng.integers(0, c.shape[0], 20000)]])
     c = c[rng.permutation(c.shape[0])]
     assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+@pytest.mark.skipif(not oracle.ref_nbr_available(), reason="oracle/_ref not built (the reference is absent)")
+@pytest.mark.parametrize("name", ["c1", "c2"])
+def test_gpu_map_equals_the_reference_function(tb, name):
+    """The device map against the reference's own build_neighbor_table (src/sparse.cpp:21-39,
+    compiled from its source into oracle/_ref), bit for bit."""
+    from trellis_cpp_b200 import ops, synth
+    c = synth.coords_for(name)
+    got = ops.build_neighbor_table(torch.from_numpy(c).cuda()).cpu().numpy()
+    assert np.array_equal(got, oracle.ref_build_neighbor_table(c))

@@ -116,3 +116,19 @@ def test_convnext_tail_matches_reference(golden):
     h = h @ g["mlp.2.weight"].T.astype(np.float64) + g["mlp.2.bias"]
     h = h + g["feats"]
     assert max_rel(h, g["block_out"]) < 1e-5
+
+
+@pytest.mark.skipif(not oracle.ref_nbr_available(), reason="oracle/_ref not built (the reference is absent)")
+def test_oracle_map_equals_the_reference_function(tb, golden):
+    """The oracle's map against the reference's own build_neighbor_table (its std::unordered_map
+    loop, src/sparse.cpp:21-39, compiled from the reference's source): golden cases, negative and
+    aliasing coordinates, duplicates (the later row wins), and a 250K-voxel shell."""
+    from trellis_cpp_b200 import synth
+    rng = np.random.default_rng(9)
+    cases = [golden["submconv"]["coords"]] + [golden["nbr"][k] for k in golden["nbr"] if k.endswith("_coords")]
+    cases.append(rng.integers(-3, 4, (3000, 3)).astype(np.int32))                  # negatives, duplicates
+    big = rng.integers(0, 1 << 21, (2000, 3)).astype(np.int32)                       # keys alias past 2^20
+    cases.append(np.concatenate([big, big[:50] + np.array([1, 0, 0], np.int32)]))
+    cases.append(synth.coords_for("c2"))
+    for c in cases:
+        assert np.array_equal(oracle.build_neighbor_table(c), oracle.ref_build_neighbor_table(c))
