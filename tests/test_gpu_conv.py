@@ -64,7 +64,7 @@ def test_golden_half_modes(tb, golden, dtype):
 
 
 SHAPES = [(16, 16), (32, 32), (64, 64), (64, 128), (128, 64), (128, 128), (256, 256), (32, 128), (256, 32),
-          (64, 512), (512, 512), (64, 16), (192, 48), (64, 32)]
+          (64, 512), (512, 512), (64, 16), (192, 48), (64, 32), (32, 64)]
 
 
 @pytest.mark.parametrize("path", ["gather", "brick", "pair"])
@@ -73,8 +73,8 @@ SHAPES = [(16, 16), (32, 32), (64, 64), (64, 128), (128, 64), (128, 128), (256, 
 def test_channel_shapes(tb, ci, co, dtype, path):
     if path == "brick" and ci % 64:
         pytest.skip("the brick kernel takes ci multiples of 64")
-    if path == "pair" and not (ci == 64 and co in (32, 64)):
-        pytest.skip("the pair kernel takes ci == 64, co in {32, 64}")
+    if path == "pair" and not (ci in (32, 64) and co in (32, 64)):
+        pytest.skip("the pair kernel takes ci and co in {32, 64}")
     coords, feats, w, b = _problem(3000, ci, co, 20, ci * 7 + co, dtype)
     out, nbr = _run(coords, feats, w, b, dtype, out_dtype="f32", path=path)
     ref = oracle.submconv(nbr.cpu().numpy(), feats, w, b)
@@ -97,23 +97,24 @@ def test_silu_epilogue_and_low_precision_output(tb, dtype):
     assert max_rel(out, ref) < TOL[dtype]
 
 
-@pytest.mark.parametrize("path", ["gather", "brick", "pair"])
+@pytest.mark.parametrize("path,ci", [("gather", 64), ("brick", 64), ("pair", 64), ("pair", 32)])
 @pytest.mark.parametrize("n", [1, 2, 127, 128, 129, 255, 256, 257, 1000])
-def test_sizes_and_partial_tiles(tb, n, path):
-    coords, feats, w, b = _problem(n, 64, 64, 16, n, "bf16")
+def test_sizes_and_partial_tiles(tb, n, path, ci):
+    coords, feats, w, b = _problem(n, ci, 64, 16, n, "bf16")
     out, nbr = _run(coords, feats, w, b, "bf16", out_dtype="f32", path=path)
     ref = oracle.submconv(nbr.cpu().numpy(), feats, w, b)
     assert max_rel(out, ref) < 1e-4
 
 
+@pytest.mark.parametrize("ci", [64, 32])
 @pytest.mark.parametrize("misaligned", [False, True])
 @pytest.mark.parametrize("n", [1003, 2050, 4097, 6144])
-def test_pair_index_fetch_alignment(tb, n, misaligned):
+def test_pair_index_fetch_alignment(tb, n, misaligned, ci):
     # the pair kernel copies each tap's tile indices from the 16-byte boundary at or below
     # t * n + r0 (n % 4 selects the offset), and copies them element by element for the last
     # tiles or when the map itself is not 16-byte aligned (a view one int into a buffer)
     from trellis_cpp_b200 import ops
-    coords, feats, w, b = _problem(n, 64, 64, 24, n + 7, "bf16")
+    coords, feats, w, b = _problem(n, ci, 64, 24, n + 7, "bf16")
     c = torch.from_numpy(np.ascontiguousarray(coords, dtype=np.int32)).cuda()
     nbr = ops.build_neighbor_table(c)
     if misaligned:

@@ -21,7 +21,10 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cub/device/device_radix_sort.cuh>
+
 #include <algorithm>
+#include <climits>
 
 namespace {
 
@@ -178,10 +181,11 @@ k_row_norm(const void* __restrict__ src, const int32_t* __restrict__ rows, int64
 // out[m][ch] = o[m][ch] + x_flat[gidx[m] * K + ch / R]: the skip of src/sparse.cpp:307,322-323
 // (x viewed [8N][K], gathered by gidx, each of its K values repeated R times). One thread per 8
 // output channels.
+// With `orow` (a permutation), row m of o is stored as output row orow[m].
 template <int XK, int OK>
 __global__ void __launch_bounds__(256)
-k_c2s_skip(const float* __restrict__ o, const void* __restrict__ x, const int32_t* __restrict__ gidx, int64_t m,
-           int cout, int k, int r, void* __restrict__ out) {
+k_c2s_skip(const float* __restrict__ o, const void* __restrict__ x, const int32_t* __restrict__ gidx,
+           const int32_t* __restrict__ orow, int64_t m, int cout, int k, int r, void* __restrict__ out) {
     const int per_row = cout / 8;
     const int64_t total = m * per_row;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
@@ -192,7 +196,46 @@ k_c2s_skip(const float* __restrict__ o, const void* __restrict__ x, const int32_
         load8<0>(o, row * cout + c0, v);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] += load1<XK>(x, xb + (c0 + e) / r);
-        store8<OK>(out, row * cout + c0, v);
+        store8<OK>(out, (orow ? (int64_t)orow[row] : row) * cout + c0, v);
+    }
+}
+
+// Bounds of the children's coordinates: mm = {min b, min x, min y, min z, max b, max x, max y, max z}
+// (b = 0 for stride 3), for the compact sort key.
+__global__ void k_coord_bounds(const int32_t* __restrict__ c, int64_t m, int stride, int* __restrict__ mm) {
+    int lo[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX}, hi[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const int v = a < 4 - stride ? 0 : c[i * stride + a - (4 - stride)];
+            lo[a] = min(lo[a], v);
+            hi[a] = max(hi[a], v);
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        lo[a] = __reduce_min_sync(0xffffffffu, lo[a]);
+        hi[a] = __reduce_max_sync(0xffffffffu, hi[a]);
+    }
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            atomicMin(mm + a, lo[a]);
+            atomicMax(mm + 4 + a, hi[a]);
+        }
+}
+
+// key of child i = (b, x, y, z) relative to the minima, packed in sh[a]-shifted fields (the
+// reference's key order, src/sparse.cpp:25); val = i
+__global__ void k_child_keys(const int32_t* __restrict__ c, int64_t m, int stride, const int* __restrict__ mm,
+                             int sb, int sx, int sy, unsigned long long* __restrict__ keys, int32_t* __restrict__ vals) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x) {
+        const int32_t* p = c + i * stride;
+        const int o = stride - 3;
+        const unsigned long long b = o ? (unsigned long long)(uint32_t)(p[0] - mm[0]) : 0ull;
+        keys[i] = (b << sb) | ((unsigned long long)(uint32_t)(p[o] - mm[1]) << sx) |
+                  ((unsigned long long)(uint32_t)(p[o + 1] - mm[2]) << sy) | (unsigned long long)(uint32_t)(p[o + 2] - mm[3]);
+        vals[i] = (int32_t)i;
     }
 }
 
@@ -258,16 +301,16 @@ tb_status tb_to_subdiv_launch(tb_ctx* ctx, const void* x, tb_dtype dtype, int64_
 }
 
 tb_status tb_c2s_skip_launch(tb_ctx* ctx, const float* o, const void* x, tb_dtype x_dtype, const int32_t* gidx,
-                             int64_t m, int cin, int cout, tb_dtype out_dtype, void* out) {
+                             const int32_t* orow, int64_t m, int cin, int cout, tb_dtype out_dtype, void* out) {
     if (m == 0) return TB_OK;
     const int k = cin / 8, r = cout / k;
     const int grid = grid_for(ctx, m * (cout / 8), 256);
     const int xk = kind_of(x_dtype), ok = kind_of(out_dtype);
-    if (xk == 0 && ok == 0) k_c2s_skip<0, 0><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, m, cout, k, r, out);
-    else if (xk == 1 && ok == 0) k_c2s_skip<1, 0><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, m, cout, k, r, out);
-    else if (xk == 2 && ok == 0) k_c2s_skip<2, 0><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, m, cout, k, r, out);
-    else if (xk == 1 && ok == 1) k_c2s_skip<1, 1><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, m, cout, k, r, out);
-    else if (xk == 2 && ok == 2) k_c2s_skip<2, 2><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, m, cout, k, r, out);
+    if (xk == 0 && ok == 0) k_c2s_skip<0, 0><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, orow, m, cout, k, r, out);
+    else if (xk == 1 && ok == 0) k_c2s_skip<1, 0><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, orow, m, cout, k, r, out);
+    else if (xk == 2 && ok == 0) k_c2s_skip<2, 0><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, orow, m, cout, k, r, out);
+    else if (xk == 1 && ok == 1) k_c2s_skip<1, 1><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, orow, m, cout, k, r, out);
+    else if (xk == 2 && ok == 2) k_c2s_skip<2, 2><<<grid, 256, 0, ctx->stream>>>(o, x, gidx, orow, m, cout, k, r, out);
     else return tb_fail(ctx, TB_ERR_UNSUPPORTED, "c2s skip: unsupported dtype pair");
     TB_LAUNCH_CHECK(ctx, "k_c2s_skip");
     return TB_OK;
@@ -335,18 +378,74 @@ extern "C" tb_status tb_sparse_c2s(tb_ctx* ctx, const int32_t* coords, int64_t n
     if (s != TB_OK) return s;
     if (m == 0) return TB_OK;
     // ---- second half: sized by m
+    // The children come parent-major (the reference's order, which the outputs keep), so a
+    // 128-row tile's neighbours are spread over distant rows and the range-staged conv kernels
+    // run about 2x slower on them. The child half therefore works on the children sorted by the
+    // reference's key (a stable device radix sort on a compact key; one small read-back of the
+    // coordinate bounds): the map and conv2 see sorted rows, norm2 reads gidx in that order, and
+    // the skip kernel writes each row back to its place in the reference's order.
     const size_t nbr2_b = al((size_t)m * 27 * 4), hn_b = al((size_t)m * cout * es), o_b = al((size_t)m * cout * 4);
-    s = tb_ensure(ctx, &ctx->c2s_ws2, &ctx->c2s_ws2_bytes, nbr2_b + hn_b + o_b, "c2s child workspace");
+    const size_t key_b = al((size_t)m * 8), val_b = al((size_t)m * 4), cs_b = al((size_t)m * coord_stride * 4);
+    size_t cub_b = 0;
+    TB_CUDA_TRY(ctx, cub::DeviceRadixSort::SortPairs(nullptr, cub_b, (const unsigned long long*)nullptr,
+                                                     (unsigned long long*)nullptr, (const int32_t*)nullptr,
+                                                     (int32_t*)nullptr, (int)m, 0, 64, ctx->stream));
+    cub_b = al(cub_b);
+    s = tb_ensure(ctx, &ctx->c2s_ws2, &ctx->c2s_ws2_bytes,
+                  nbr2_b + hn_b + o_b + 2 * key_b + 3 * val_b + cs_b + cub_b + 256, "c2s child workspace");
     if (s != TB_OK) return s;
     uint8_t* b2 = reinterpret_cast<uint8_t*>(ctx->c2s_ws2);
     int32_t* nbr2 = reinterpret_cast<int32_t*>(b2);
     void* hn = b2 + nbr2_b;
     float* o = reinterpret_cast<float*>(b2 + nbr2_b + hn_b);
-    s = tb_row_norm_launch(ctx, h1, TB_F32, gidx, m, cout, nullptr, nullptr, 1, dtype, hn);
+    uint8_t* p2 = b2 + nbr2_b + hn_b + o_b;
+    auto* keys_in = reinterpret_cast<unsigned long long*>(p2);
+    auto* keys_out = reinterpret_cast<unsigned long long*>(p2 + key_b);
+    int32_t* iota = reinterpret_cast<int32_t*>(p2 + 2 * key_b);
+    int32_t* perm = reinterpret_cast<int32_t*>(p2 + 2 * key_b + val_b);
+    int32_t* gidx_s = reinterpret_cast<int32_t*>(p2 + 2 * key_b + 2 * val_b);
+    int32_t* child_s = reinterpret_cast<int32_t*>(p2 + 2 * key_b + 3 * val_b);
+    void* cub_tmp = p2 + 2 * key_b + 3 * val_b + cs_b;
+    int* mm = reinterpret_cast<int*>(p2 + 2 * key_b + 3 * val_b + cs_b + cub_b);
+    static const int mm0[8] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX, INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(mm, mm0, sizeof(mm0), cudaMemcpyHostToDevice, ctx->stream));
+    k_coord_bounds<<<grid_for(ctx, m, 256), 256, 0, ctx->stream>>>(child_coords, m, coord_stride, mm);
+    TB_LAUNCH_CHECK(ctx, "k_coord_bounds");
+    int bh[8];
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(bh, mm, sizeof(bh), cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    auto bits = [](int lo, int hi) {
+        const uint64_t span = (uint64_t)((int64_t)hi - lo);
+        int k = 0;
+        while (k < 33 && (span >> k) != 0) ++k;
+        return k;
+    };
+    const int bz = bits(bh[3], bh[7]), by = bits(bh[2], bh[6]), bx = bits(bh[1], bh[5]), bb = bits(bh[0], bh[4]);
+    const int total_bits = bb + bx + by + bz;
+    const bool sorted_path = total_bits <= 64;
+    const int32_t* cmap_coords = child_coords;
+    const int32_t* gsel = gidx;
+    const int32_t* orow = nullptr;
+    if (sorted_path) {
+        k_child_keys<<<grid_for(ctx, m, 256), 256, 0, ctx->stream>>>(child_coords, m, coord_stride, mm, bx + by + bz,
+                                                                    by + bz, bz, keys_in, iota);
+        TB_LAUNCH_CHECK(ctx, "k_child_keys");
+        size_t tmp = cub_b;
+        TB_CUDA_TRY(ctx, cub::DeviceRadixSort::SortPairs(cub_tmp, tmp, keys_in, keys_out, iota, perm, (int)m, 0,
+                                                         std::max(1, total_bits), ctx->stream));
+        s = tb_gather_rows(ctx, child_coords, perm, m, (int64_t)coord_stride * 4, child_s);
+        if (s != TB_OK) return s;
+        s = tb_gather_rows(ctx, gidx, perm, m, 4, gidx_s);
+        if (s != TB_OK) return s;
+        cmap_coords = child_s;
+        gsel = gidx_s;
+        orow = perm;
+    }
+    s = tb_row_norm_launch(ctx, h1, TB_F32, gsel, m, cout, nullptr, nullptr, 1, dtype, hn);
     if (s != TB_OK) return s;
-    s = tb_build_neighbor_map(ctx, child_coords, m, coord_stride, nbr2);
+    s = tb_build_neighbor_map(ctx, cmap_coords, m, coord_stride, nbr2);
     if (s != TB_OK) return s;
     s = tb_submconv(ctx, nbr2, m, hn, cout, prm->conv2_w, prm->conv2_b, cout, dtype, TB_F32, TB_EPI_NONE, o);
     if (s != TB_OK) return s;
-    return tb_c2s_skip_launch(ctx, o, feats, dtype, gidx, m, cin, cout, out_dtype, out);
+    return tb_c2s_skip_launch(ctx, o, feats, dtype, gsel, orow, m, cin, cout, out_dtype, out);
 }

@@ -33,7 +33,7 @@ struct tb_ctx {
     // dynamic shared memory already allowed per conv kernel on this device: the attribute is set
     // only when a launch needs more, so repeated launches (and launches recorded into a CUDA
     // graph) make no function-attribute call
-    size_t pair_smem_set = 0;
+    size_t pair_smem_set[2] = {0, 0};   // the pair kernel's Ci = 64 and Ci = 32 instances
     size_t brick_smem_set = 0;
     void* block_h = nullptr;       // fp32 conv output of tb_sparse_convnext
     size_t block_h_bytes = 0;

@@ -5,14 +5,17 @@
 // multiplied with f32 activations. Same math as src/sparse.cpp:64-79: per output row,
 // bias + sum over the 27 taps of W_t . x[nbr], absent taps reading zero.
 //
-// Tiling: a block computes 32 output rows x 64 output channels. For each tap it gathers
-// the 32 neighbor rows, 32 channels at a time, into shared memory next to the matching
-// 64x32 weight slice, and every thread accumulates 1 row x 8 channels in registers.
+// Tiling: a block of 256 threads computes 64 output rows x 64 output channels; each thread
+// holds a 4-row x 4-channel register tile. For each tap the block gathers its 64 neighbor rows,
+// up to 32 input channels at a time, into shared memory transposed ([k][row]) next to the
+// matching weight slice ([k][o]), so every k step is two 16-byte shared loads feeding 16 FMAs.
+// Each output element accumulates its taps in ascending order and, within a tap, its input
+// channels in ascending order, whichever block or range computes it.
 #include "tb_common.cuh"
 
 namespace {
 
-constexpr int BR = 32;   // rows per block
+constexpr int BR = 64;   // rows per block
 constexpr int BC = 64;   // output channels per block
 constexpr int BK = 32;   // input channels per step
 
@@ -21,54 +24,66 @@ k_submconv_f32(const int32_t* __restrict__ nbr, int64_t n, int64_t row0, int64_t
                const float* __restrict__ feats, int ci,
                const float* __restrict__ w, const float* __restrict__ bias, int co, int epi,
                float* __restrict__ out) {
-    __shared__ float xs[BR][BK + 1];
-    __shared__ float ws[BC][BK + 1];
+    // rows padded by 4 floats: the transposing stores (consecutive threads, consecutive k) spread
+    // over 8 banks instead of one, and every row stays 16-byte aligned for the float4 reads
+    __shared__ __align__(16) float xs[BK][BR + 4];     // gathered inputs, transposed
+    __shared__ __align__(16) float ws[BK][BC + 4];     // weight slice of one tap, [k][o]
     __shared__ int32_t rows[BR];
-    const int tx = threadIdx.x & 7;          // channel group: o = o0 + tx + 8*j
-    const int ty = threadIdx.x >> 3;         // row within block
+    const int tr = threadIdx.x >> 4;               // row group: rows 4 tr .. 4 tr + 3
+    const int tc = threadIdx.x & 15;               // channel group: channels 4 tc .. 4 tc + 3
     const int64_t r0 = row0 + (int64_t)blockIdx.x * BR;
     const int o0 = blockIdx.y * BC;
-    float acc[8];
+    float acc[4][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
     for (int t = 0; t < 27; ++t) {
         __syncthreads();
         if (threadIdx.x < BR) {
             const int64_t r = r0 + threadIdx.x;
-            rows[threadIdx.x] = r < n ? nbr[(int64_t)t * n + r] : (int32_t)n;
+            rows[threadIdx.x] = r < row_end ? nbr[(int64_t)t * n + r] : (int32_t)n;
         }
         __syncthreads();
         for (int k0 = 0; k0 < ci; k0 += BK) {
-            // gather 32 rows x 32 channels (zero for absent rows / channel tail)
+            // gather: thread reads channel k of row r (consecutive threads, consecutive channels)
             for (int idx = threadIdx.x; idx < BR * BK; idx += blockDim.x) {
                 const int r = idx / BK, k = idx % BK;
                 const int32_t src = rows[r];
-                xs[r][k] = (src != (int32_t)n && k0 + k < ci) ? feats[(int64_t)src * ci + k0 + k] : 0.f;
+                xs[k][r] = (src != (int32_t)n && k0 + k < ci) ? __ldg(feats + (int64_t)src * ci + k0 + k) : 0.f;
             }
             for (int idx = threadIdx.x; idx < BC * BK; idx += blockDim.x) {
                 const int o = idx / BK, k = idx % BK;
-                ws[o][k] = (o0 + o < co && k0 + k < ci) ? w[((int64_t)(o0 + o) * 27 + t) * ci + k0 + k] : 0.f;
+                ws[k][o] = (o0 + o < co && k0 + k < ci) ? __ldg(w + ((int64_t)(o0 + o) * 27 + t) * ci + k0 + k) : 0.f;
             }
             __syncthreads();
 #pragma unroll 8
             for (int k = 0; k < BK; ++k) {
-                const float xv = xs[ty][k];
+                const float4 xv = *reinterpret_cast<const float4*>(&xs[k][4 * tr]);
+                const float4 wv = *reinterpret_cast<const float4*>(&ws[k][4 * tc]);
+                const float xr[4] = {xv.x, xv.y, xv.z, xv.w};
+                const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[j] = fmaf(xv, ws[tx + 8 * j][k], acc[j]);
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xr[i], wr[j], acc[i][j]);
             }
             __syncthreads();
         }
     }
-    const int64_t r = r0 + ty;
-    if (r >= row_end) return;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int o = o0 + tx + 8 * j;
-        if (o >= co) continue;
-        float v = acc[j] + (bias ? bias[o] : 0.f);
-        if (epi == TB_EPI_SILU) v = tb_silu(v);
-        out[r * co + o] = v;
+    for (int i = 0; i < 4; ++i) {
+        const int64_t r = r0 + 4 * tr + i;
+        if (r >= row_end) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int o = o0 + 4 * tc + j;
+            if (o >= co) continue;
+            float v = acc[i][j] + (bias ? bias[o] : 0.f);
+            if (epi == TB_EPI_SILU) v = tb_silu(v);
+            out[r * co + o] = v;
+        }
     }
 }
 

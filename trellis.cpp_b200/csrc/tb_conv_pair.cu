@@ -1,4 +1,4 @@
-// Submanifold conv for Ci = 64 and Co in {32, 64} on CTA pairs, with the weights resident.
+// Submanifold conv for Ci in {32, 64} and Co in {32, 64} on CTA pairs, with the weights resident.
 //
 // Same neighbor handling as the brick kernel (tb_conv_brick.cu): in the reference's x-major
 // voxel order the neighbor rows of a 128-voxel tile form three contiguous row ranges, one per
@@ -21,6 +21,11 @@
 // 13-14 MMA issuers (even CTA only). Cross-CTA hand-offs: the odd CTA's builders and epilogue
 // arrive on the even CTA's barriers (mapa + release.cluster); MMA commits multicast to both.
 // Every wait is bounded (about 2 s) and aborts the CTA cleanly.
+//
+// Ci is a template parameter: a voxel row is 2 Ci bytes (128 B with the 128-byte TMA swizzle at
+// Ci = 64, 64 B with the 64-byte swizzle at Ci = 32), a tap of A takes Ci / 2 TMEM columns, and
+// at Ci = 32 twice as many two-tap units fit in the same TMEM columns, so the A pipeline is twice
+// as deep. Ci = 32 is the bandwidth-bound regime (BASELINE config 5 at C = 32).
 #include "tb_common.cuh"
 #include "tb_tc_ptx.cuh"
 
@@ -41,11 +46,27 @@ constexpr int kBox = 32;             // rows per TMA box
 constexpr int kNbrRow = kTileM + 4;     // one tap's indices, copied from a 16-byte aligned start
 constexpr int kNbrInts = 27 * kNbrRow;
 constexpr int kNB = 3;                  // neighbor-index buffers (two tiles fetched ahead)
-constexpr int kNU = 3;               // A unit slots per issuer (a unit is one or two taps, 64 columns)
 constexpr int kNR = 8;               // range descriptor ring
 constexpr uint32_t kACol0 = 128;     // first A column; issuer k accumulates in columns 64k..64k+co-1
-// nbrf[3] nbre[3] rngf[8] rnge[8] af[2][3] ae[2][3] df[2] de[2] wbar drain
-constexpr int kNumBars = kNB + kNB + kNR + kNR + 2 * kNU + 2 * kNU + 2 + 2 + 1 + 1;
+constexpr int kNUMax = 6;            // A unit slots per issuer at Ci = 32 (3 at Ci = 64)
+// nbrf[kNB] nbre[kNB] rngf[8] rnge[8] af[2][kNU] ae[2][kNU] df[2] de[2] wbar drain (sized for kNUMax)
+constexpr int kNumBars = kNB + kNB + kNR + kNR + 2 * kNUMax + 2 * kNUMax + 2 + 2 + 1 + 1;
+
+// Per-Ci geometry: row bytes, 16-byte chunks per row, TMEM columns per tap, K steps per tap, A
+// unit slots per issuer (384 A columns split over two issuers, two taps per unit).
+template <int CI>
+struct PairGeom {
+    static_assert(CI == 32 || CI == 64, "pair kernel: Ci 32 or 64");
+    static constexpr int kRB = 2 * CI;
+    static constexpr int kChunks = kRB / 16;
+    static constexpr int kTapCols = CI / 2;
+    static constexpr int kKSteps = CI / 16;
+    static constexpr int kUnitCols = 2 * kTapCols;
+    static constexpr int kNU = 192 / kUnitCols;
+    // 16-byte chunk c of ring row b after the TMA swizzle (128 B: bits 4-6 ^= bits 7-9; 64 B:
+    // bits 4-5 ^= bits 7-8 of the byte offset)
+    static __device__ __forceinline__ int slot(int c, int b) { return CI == 64 ? (c ^ (b & 7)) : (c ^ ((b >> 1) & 3)); }
+};
 
 // Pipeline tracing (compiled in with -DTB_TRACE): the first cluster stamps clock64 into p.trace
 // laid out as [role][kTraceCap] (clock64 is per SM, so compare stamps of one CTA only):
@@ -99,14 +120,17 @@ struct PairParams {
     long long* trace;            // TB_TRACE builds only
 };
 
+template <int CI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap fmap,
                 const PairParams p) {
+    using G = PairGeom<CI>;
+    constexpr int kNU = G::kNU;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* w_base = smem;                                                   // [27][w_tap_bytes]
     uint8_t* ring = w_base + 27 * (size_t)p.w_tap_bytes;                      // [ring_rows][128]
-    int32_t* s_nbr = reinterpret_cast<int32_t*>(ring + (size_t)p.ring_rows * 128);   // [kNB][27][kNbrRow]
+    int32_t* s_nbr = reinterpret_cast<int32_t*>(ring + (size_t)p.ring_rows * G::kRB);   // [kNB][27][kNbrRow]
     Range* s_rng = reinterpret_cast<Range*>(s_nbr + kNB * kNbrInts);          // [kNR]
     int32_t* s_alloc = reinterpret_cast<int32_t*>(s_rng + kNR);               // [kNR] loader-private
     uint64_t* bars = reinterpret_cast<uint64_t*>(s_alloc + kNR);
@@ -167,10 +191,10 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
 
     if (warp == kWarpLoader) {
         // ------------------------------------------------------------------ weights + loader
-        if (lane == 0) mbar_arrive_expect_tx(wbar, 27u * (uint32_t)nhalf * 128u);
+        if (lane == 0) mbar_arrive_expect_tx(wbar, 27u * (uint32_t)nhalf * (uint32_t)G::kRB);
         __syncwarp();
         if (lane < 27)
-            tma_load_2d(smem_u32(w_base + (size_t)lane * p.w_tap_bytes), &wmap, lane * 64, (int)rank * nhalf, wbar);
+            tma_load_2d(smem_u32(w_base + (size_t)lane * p.w_tap_bytes), &wmap, lane * CI, (int)rank * nhalf, wbar);
         // Neighbor indices of tile j go to buffer j % kNB. Tiles whose 27 copies stay inside the
         // map (and a 16-byte aligned map) use one bulk copy per tap; the last tiles copy
         // element by element with bounds checks. Either way nbrf completes when they landed.
@@ -282,7 +306,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                     s_rng[slot].lo = ghi >= 0 ? glo : 0;
                     s_rng[slot].len = held;
                     s_rng[slot].off = off;
-                    mbar_arrive_expect_tx(rngf + 8 * slot, (uint32_t)need * 128u);
+                    mbar_arrive_expect_tx(rngf + 8 * slot, (uint32_t)need * (uint32_t)G::kRB);
                     if (leader) TB_STAMP(0, k);
                 }
                 __syncwarp();
@@ -290,7 +314,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 for (int j = lane; j < nbox; j += 32) {
                     int row = off + j * kBox;
                     if (row >= p.ring_rows) row -= p.ring_rows;
-                    tma_load_2d(smem_u32(ring + (size_t)row * 128), &fmap, 0, glo + j * kBox, rngf + 8 * slot);
+                    tma_load_2d(smem_u32(ring + (size_t)row * G::kRB), &fmap, 0, glo + j * kBox, rngf + 8 * slot);
                 }
             }
             if (!ok) break;
@@ -314,8 +338,8 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         const int q = warp & 3;
         const int half = (warp - kWarpBuild0) >> 2;
         const int i = q * 32 + lane;
-        // this half's unit slots: columns kACol0 + 64 * (kNU * half + u), 32 per tap
-        const uint32_t a_lane = tmem_base + ((uint32_t)(q * 32) << 16) + kACol0 + 64u * kNU * (uint32_t)half;
+        // this half's unit slots: columns kACol0 + kUnitCols * (kNU * half + u), kTapCols per tap
+        const uint32_t a_lane = tmem_base + ((uint32_t)(q * 32) << 16) + kACol0 + (uint32_t)G::kUnitCols * kNU * (uint32_t)half;
         const uint32_t afh = af + 8 * kNU * half, aeh = ae + 8 * kNU * half;
         int u = 0, uph = 0;                 // unit slot and its phase
         bool ok = mbar_wait(wbar, 0, s_abort, p.err);   // this CTA's weight half has landed
@@ -352,27 +376,27 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                     if (tr0) TB_STAMP(8, seq0 + t);
                     // both taps' 32 rows of A in registers before the slot wait: ring row, missing
                     // (zero) or, for a row outside the held range, global memory
-                    uint32_t rv[2][32];
+                    uint32_t rv[2][G::kTapCols];
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         if (e == 1 && !has2) break;
                         const int32_t v = vrow[2 * j + e];
                         if (v == sentinel) {
 #pragma unroll
-                            for (int c = 0; c < 32; ++c) rv[e][c] = 0u;
+                            for (int c = 0; c < G::kTapCols; ++c) rv[e][c] = 0u;
                         } else if ((uint32_t)(v - rlo) < (uint32_t)rlen) {
                             int b = roff + (v - rlo);
                             if (b >= p.ring_rows) b -= p.ring_rows;
-                            const uint8_t* rowp = ring + (size_t)b * 128;
+                            const uint8_t* rowp = ring + (size_t)b * G::kRB;
 #pragma unroll
-                            for (int c = 0; c < 8; ++c) {
-                                const uint4 x = *reinterpret_cast<const uint4*>(rowp + ((c ^ (b & 7)) << 4));
+                            for (int c = 0; c < G::kChunks; ++c) {
+                                const uint4 x = *reinterpret_cast<const uint4*>(rowp + (G::slot(c, b) << 4));
                                 rv[e][4 * c] = x.x; rv[e][4 * c + 1] = x.y; rv[e][4 * c + 2] = x.z; rv[e][4 * c + 3] = x.w;
                             }
                         } else {
-                            const uint4* gp = reinterpret_cast<const uint4*>(p.feats + (size_t)v * 128);
+                            const uint4* gp = reinterpret_cast<const uint4*>(p.feats + (size_t)v * G::kRB);
 #pragma unroll
-                            for (int c = 0; c < 8; ++c) {
+                            for (int c = 0; c < G::kChunks; ++c) {
                                 const uint4 x = __ldg(gp + c);
                                 rv[e][4 * c] = x.x; rv[e][4 * c + 1] = x.y; rv[e][4 * c + 2] = x.z; rv[e][4 * c + 3] = x.w;
                             }
@@ -396,7 +420,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
 #endif
 #ifdef TB_TRACE
                     if (tr0) {
-                        asm volatile("" :: "r"(rv[0][31]), "r"(rv[1][31]));   // the gathered rows have arrived
+                        asm volatile("" :: "r"(rv[0][G::kTapCols - 1]), "r"(rv[1][G::kTapCols - 1]));   // rows arrived
                         TB_STAMP(6, s1);
                     }
 #endif
@@ -404,9 +428,14 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                     if (!mbar_wait_cluster_relaxed(aeh + 8 * u, (uint32_t)(uph ^ 1), s_abort, p.err)) { ok = false; break; }
                     tc_fence_after();
                     if (tr0) TB_STAMP(9, s1);
-                    tmem_st_x32(a_lane + 64u * (uint32_t)u, rv[0]);
+                    const uint32_t ua = a_lane + (uint32_t)G::kUnitCols * (uint32_t)u;
+                    if constexpr (CI == 64) tmem_st_x32(ua, rv[0]);
+                    else tmem_st_x16(ua, rv[0]);
                     if (tr0) TB_STAMP(11, s1);
-                    if (has2) tmem_st_x32(a_lane + 64u * (uint32_t)u + 32u, rv[1]);
+                    if (has2) {
+                        if constexpr (CI == 64) tmem_st_x32(ua + (uint32_t)G::kTapCols, rv[1]);
+                        else tmem_st_x16(ua + (uint32_t)G::kTapCols, rv[1]);
+                    }
                     tmem_wait_st();
                     if (tr0) TB_STAMP(12, s1);
                     tc_fence_before();
@@ -436,7 +465,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         // per MMA plus about 80 per commit from a lone active lane.
         const int mi = warp - kWarpMma0;
         if (leader) {
-            const uint64_t wdesc0 = smem_desc<128>(smem_u32(w_base));
+            const uint64_t wdesc0 = smem_desc<G::kRB>(smem_u32(w_base));
             const uint32_t wstep = p.w_tap_bytes >> 4;
             // issuer mi takes the taps whose sequence number (27 * tile + tap) has parity mi, in
             // the units its builder half writes them: per tap group, taps t0, t0 + 2 | t0 + 4,
@@ -444,7 +473,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             int it = 0, u = 0, uph = 0;
             bool ok = true;
             const uint32_t dt = tmem_base + 64u * (uint32_t)mi;
-            const uint32_t a_base = tmem_base + kACol0 + 64u * kNU * (uint32_t)mi;
+            const uint32_t a_base = tmem_base + kACol0 + (uint32_t)G::kUnitCols * kNU * (uint32_t)mi;
             const uint32_t afh = af + 8 * kNU * mi, aeh = ae + 8 * kNU * mi;
             for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
                 // the epilogue has read this issuer's accumulator for the previous tile
@@ -461,18 +490,17 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                         if (lane == 0) TB_STAMP(2, seq0 + t);
                         tc_fence_after();
                         if (elect_one()) {
-                            const uint32_t at = a_base + 64u * (uint32_t)u;
+                            // K = 16 per MMA: 8 TMEM columns of A, 32 bytes (2 descriptor units) of B
+                            const uint32_t at = a_base + (uint32_t)G::kUnitCols * (uint32_t)u;
                             const uint64_t bd = wdesc0 + (uint64_t)(wstep * (uint32_t)t);
-                            tc_mma_ts_pair(dt, at, bd, p.idesc, acc);
-                            tc_mma_ts_pair(dt, at + 8, bd + 2, p.idesc, 1u);
-                            tc_mma_ts_pair(dt, at + 16, bd + 4, p.idesc, 1u);
-                            tc_mma_ts_pair(dt, at + 24, bd + 6, p.idesc, 1u);
+#pragma unroll
+                            for (int ks = 0; ks < G::kKSteps; ++ks)
+                                tc_mma_ts_pair(dt, at + 8u * ks, bd + 2u * ks, p.idesc, ks == 0 ? acc : 1u);
                             if (has2) {
                                 const uint64_t bd2 = bd + (uint64_t)(2u * wstep);
-                                tc_mma_ts_pair(dt, at + 32, bd2, p.idesc, 1u);
-                                tc_mma_ts_pair(dt, at + 40, bd2 + 2, p.idesc, 1u);
-                                tc_mma_ts_pair(dt, at + 48, bd2 + 4, p.idesc, 1u);
-                                tc_mma_ts_pair(dt, at + 56, bd2 + 6, p.idesc, 1u);
+#pragma unroll
+                                for (int ks = 0; ks < G::kKSteps; ++ks)
+                                    tc_mma_ts_pair(dt, at + (uint32_t)G::kTapCols + 8u * ks, bd2 + 2u * ks, p.idesc, 1u);
                             }
                             tc_commit_pair(aeh + 8 * u, 0x3);
                         }
@@ -554,13 +582,13 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
 extern long long* g_trace_buffer;
 #endif
 
-bool tb_conv_pair_supported(int ci, int co) { return ci == 64 && (co == 64 || co == 32); }
+bool tb_conv_pair_supported(int ci, int co) { return (ci == 64 || ci == 32) && (co == 64 || co == 32); }
 
 tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
                               const void* feats, int ci, const void* weight, const float* bias, int co,
                               tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
     if (!tb_conv_pair_supported(ci, co))
-        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "pair conv needs ci == 64 and co in {32, 64}");
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "pair conv needs ci and co in {32, 64}");
     if (!ctx->encode_tiled) {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -590,7 +618,8 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_
     p.row_begin = row0;
     p.row_end = row0 + nrows;
     const int nhalf = co / 2;
-    p.w_tap_bytes = ((uint32_t)nhalf * 128u + 1023u) & ~1023u;
+    const uint32_t rb = 2u * (uint32_t)ci;      // bytes per voxel row
+    p.w_tap_bytes = ((uint32_t)nhalf * rb + 1023u) & ~1023u;
     const uint32_t fmt = dtype == TB_BF16 ? 1u : 0u;
     // D f32, A/B format, K-major, N = co, M = 256 (the pair)
     p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(co >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
@@ -599,46 +628,49 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_
     const size_t fixed = 27 * (size_t)p.w_tap_bytes + kNB * (size_t)kNbrInts * 4 + kNR * sizeof(Range) + kNR * 4 +
                          8 * kNumBars + 16 + 1024;
     const size_t budget = (size_t)ctx->max_smem_optin;
-    if (budget < fixed + 256 * 128) return tb_fail(ctx, TB_ERR_UNSUPPORTED, "pair conv: shared memory too small");
-    int ring = (int)((budget - fixed) / 128);
+    if (budget < fixed + 256 * (size_t)rb) return tb_fail(ctx, TB_ERR_UNSUPPORTED, "pair conv: shared memory too small");
+    int ring = (int)((budget - fixed) / rb);
     ring = ring / kBox * kBox;
     p.ring_rows = ring;
-    const size_t smem = fixed + (size_t)ring * 128;
+    const size_t smem = fixed + (size_t)ring * rb;
 
     CUtensorMap wmap, fmap;
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType dt = dtype == TB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUtensorMapSwizzle swz = ci == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     {
         const cuuint64_t gdim[2] = {(cuuint64_t)27 * ci, (cuuint64_t)co};
         const cuuint64_t gstride[1] = {(cuuint64_t)27 * ci * 2};
-        const cuuint32_t box[2] = {64, (cuuint32_t)nhalf};
+        const cuuint32_t box[2] = {(cuuint32_t)ci, (cuuint32_t)nhalf};
         CUresult cr = reinterpret_cast<EncodeTiledFn>(ctx->encode_tiled)(
             &wmap, dt, 2, const_cast<void*>(weight), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the weight view");
     }
     {
         const cuuint64_t gdim[2] = {(cuuint64_t)ci, (cuuint64_t)n};
         const cuuint64_t gstride[1] = {(cuuint64_t)ci * 2};
-        const cuuint32_t box[2] = {64, (cuuint32_t)kBox};
+        const cuuint32_t box[2] = {(cuuint32_t)ci, (cuuint32_t)kBox};
         CUresult cr = reinterpret_cast<EncodeTiledFn>(ctx->encode_tiled)(
             &fmap, dt, 2, const_cast<void*>(feats), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the feature view");
     }
     const int nclusters = std::max(1, std::min(p.npairs - p.pr0, ctx->num_sms / 2));
     cudaError_t e = cudaSuccess;
-    if (smem > ctx->pair_smem_set) {
-        e = cudaFuncSetAttribute(k_submconv_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kern = ci == 64 ? k_submconv_pair<64> : k_submconv_pair<32>;
+    size_t& smem_set = ctx->pair_smem_set[ci == 64 ? 0 : 1];
+    if (smem > smem_set) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_submconv_pair)");
-        ctx->pair_smem_set = smem;
+        smem_set = smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * nclusters);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx->stream;
-    e = cudaLaunchKernelEx(&cfg, k_submconv_pair, wmap, fmap, p);
+    e = cudaLaunchKernelEx(&cfg, kern, wmap, fmap, p);
     if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaLaunchKernelEx(k_submconv_pair)");
     TB_LAUNCH_CHECK(ctx, "k_submconv_pair");
     return TB_OK;
