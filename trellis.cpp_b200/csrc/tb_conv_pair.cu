@@ -118,6 +118,8 @@ struct PairParams {
     uint32_t w_tap_bytes;        // (co/2) rows x 128 B, rounded up to 1024
     uint32_t idesc;
     long long* trace;            // TB_TRACE builds only
+    long long wait_limit;        // clock cycles a bounded wait may take (about 2 s)
+    int withhold;                // test hook: the even CTA's first epilogue warp withholds one arrive
 };
 
 template <int CI>
@@ -239,7 +241,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             const int64_t r0 = (int64_t)(2 * pr + (int)rank) * kTileM;
             const int nvalid = p.n - r0 < kTileM ? (int)(p.n - r0) : kTileM;
             if (leader && lane == 0) TB_STAMP(10, it);
-            if (!mbar_wait(nbrf + 8 * buf, (uint32_t)ph, s_abort, p.err)) { ok = false; break; }
+            if (!mbar_wait(nbrf + 8 * buf, (uint32_t)ph, s_abort, p.err, p.wait_limit)) { ok = false; break; }
             if (leader && lane == 0) TB_STAMP(10, it + 2048);
             const int32_t* rows = s_nbr + buf * kNbrInts;
             // per tap group: min and max present neighbor row over the tile's valid rows (lane
@@ -282,7 +284,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 const int need = (held + kBox - 1) / kBox * kBox;
                 const int slot = k & (kNR - 1);
                 // descriptor slot free (range k-8 built), then enough ring rows free
-                if (!mbar_wait(rnge + 8 * slot, ((k >> 3) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
+                if (!mbar_wait(rnge + 8 * slot, ((k >> 3) & 1) ^ 1, s_abort, p.err, p.wait_limit)) { ok = false; break; }
                 // ranges at least kNR behind are built (that is what the wait above saw): reclaim
                 // them without waiting, so the loop below only waits on the last kNR - 1 ranges,
                 // whose barriers cannot have moved a phase further yet
@@ -291,7 +293,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                     ++koldest;
                 }
                 while (used + need > p.ring_rows && ok) {
-                    if (!mbar_wait(rnge + 8 * (koldest & (kNR - 1)), (koldest >> 3) & 1, s_abort, p.err)) { ok = false; break; }
+                    if (!mbar_wait(rnge + 8 * (koldest & (kNR - 1)), (koldest >> 3) & 1, s_abort, p.err, p.wait_limit)) { ok = false; break; }
                     used -= s_alloc[koldest & (kNR - 1)];
                     ++koldest;
                 }
@@ -322,7 +324,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             const int prf = pr + (kNB - 1) * ncl;
             if (prf < p.npairs) {
                 if (leader && lane == 0) TB_STAMP(14, 1024 + it);
-                if (!mbar_wait(nbre + 8 * fbuf, (uint32_t)(fph ^ 1), s_abort, p.err)) { ok = false; break; }
+                if (!mbar_wait(nbre + 8 * fbuf, (uint32_t)(fph ^ 1), s_abort, p.err, p.wait_limit)) { ok = false; break; }
                 if (leader && lane == 0) TB_STAMP(14, 2048 + it);
                 fetch_nbr(prf, fbuf);
                 if (++fbuf == kNB) { fbuf = 0; fph ^= 1; }
@@ -342,10 +344,15 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         const uint32_t a_lane = tmem_base + ((uint32_t)(q * 32) << 16) + kACol0 + (uint32_t)G::kUnitCols * kNU * (uint32_t)half;
         const uint32_t afh = af + 8 * kNU * half, aeh = ae + 8 * kNU * half;
         int u = 0, uph = 0;                 // unit slot and its phase
-        bool ok = mbar_wait(wbar, 0, s_abort, p.err);   // this CTA's weight half has landed
+        // every wait's result is made warp-uniform: the TMEM stores that follow are warp-collective,
+        // and a lane that timed out must not leave the others to run them alone
+        bool ok = __all_sync(0xffffffffu, mbar_wait(wbar, 0, s_abort, p.err, p.wait_limit));   // weights landed
         int it = 0, k = 0, buf = 0, ph = 0;
         for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
-            if (!mbar_wait(nbrf + 8 * buf, (uint32_t)ph, s_abort, p.err)) { ok = false; break; }
+            if (!__all_sync(0xffffffffu, mbar_wait(nbrf + 8 * buf, (uint32_t)ph, s_abort, p.err, p.wait_limit))) {
+                ok = false;
+                break;
+            }
             const int32_t* rows = s_nbr + buf * kNbrInts;
             const int64_t r0 = (int64_t)(2 * pr + (int)rank) * kTileM;
             const bool row_valid = r0 + i < p.n;     // rows past the map end are never stored
@@ -353,7 +360,10 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
 #pragma unroll 1
             for (int g = 0; g < 3 && ok; ++g, ++k) {
                 const int slot = k & (kNR - 1);
-                if (!mbar_wait(rngf + 8 * slot, (k >> 3) & 1, s_abort, p.err)) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, mbar_wait(rngf + 8 * slot, (k >> 3) & 1, s_abort, p.err, p.wait_limit))) {
+                    ok = false;
+                    break;
+                }
                 if (leader && half == 0 && q == 0 && lane == 0) TB_STAMP(5, k);
                 const int rlo = s_rng[slot].lo, rlen = s_rng[slot].len, roff = s_rng[slot].off;
                 // this group's taps with stage parity == half, two at a time: taps t0, t0 + 2 |
@@ -425,7 +435,11 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                     }
 #endif
                     // the unit slot's previous taps have been multiplied
-                    if (!mbar_wait_cluster_relaxed(aeh + 8 * u, (uint32_t)(uph ^ 1), s_abort, p.err)) { ok = false; break; }
+                    if (!__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(aeh + 8 * u, (uint32_t)(uph ^ 1), s_abort, p.err,
+                                                                           p.wait_limit))) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     if (tr0) TB_STAMP(9, s1);
                     const uint32_t ua = a_lane + (uint32_t)G::kUnitCols * (uint32_t)u;
@@ -477,7 +491,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             const uint32_t afh = af + 8 * kNU * mi, aeh = ae + 8 * kNU * mi;
             for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
                 // the epilogue has read this issuer's accumulator for the previous tile
-                ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(de + 8 * mi, (uint32_t)((it & 1) ^ 1), s_abort, p.err));
+                ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(de + 8 * mi, (uint32_t)((it & 1) ^ 1), s_abort, p.err, p.wait_limit));
                 if (!ok) break;
                 if (lane == 0) TB_STAMP(7, 2 * it + mi);
                 const int seq0 = 27 * it;
@@ -485,7 +499,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 for (int g = 0; g < 3 && ok; ++g) {
                     for (int t = 9 * g + ((mi ^ (seq0 + 9 * g)) & 1); t < 9 * g + 9; t += 4) {
                         const bool has2 = t + 2 < 9 * g + 9;
-                        ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(afh + 8 * u, (uint32_t)uph, s_abort, p.err));
+                        ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(afh + 8 * u, (uint32_t)uph, s_abort, p.err, p.wait_limit));
                         if (!ok) break;
                         if (lane == 0) TB_STAMP(2, seq0 + t);
                         tc_fence_after();
@@ -528,8 +542,8 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         const size_t esize = p.out_kind == 0 ? 4 : 2;
         for (int pr = p.pr0 + cid; pr < p.npairs; pr += ncl, ++it) {
             const uint32_t dph = (uint32_t)(it & 1);
-            bool ok = mbar_wait_cluster_relaxed(df, dph, s_abort, p.err);
-            if (ok) ok = mbar_wait_cluster_relaxed(df + 8, dph, s_abort, p.err);
+            bool ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(df, dph, s_abort, p.err, p.wait_limit));
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(df + 8, dph, s_abort, p.err, p.wait_limit));
             if (!ok) break;
             if (leader && q == 0 && lane == 0) TB_STAMP(4, it);
             tc_fence_after();
@@ -550,7 +564,9 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
+            // (the test hook leaves the first tile's accumulator-free barrier one arrive short, so
+            // the issuers' next waits run out and every role leaves through the abort path)
+            if (lane == 0 && !(p.withhold && it == 0 && leader && q == 0)) {
                 mbar_arrive_cluster_relaxed(de, 0);
                 mbar_arrive_cluster_relaxed(de + 8, 0);
             }
@@ -582,6 +598,16 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
 extern long long* g_trace_buffer;
 #endif
 
+// Test hook (not declared in the public header): make the next pair-kernel launches withhold one
+// epilogue arrive and give up waiting after `limit_cycles` (about 1 ms at 2e6), so a test can
+// run the bounded-wait abort path without hanging anything; on = 0 restores the defaults.
+static long long g_pair_wait_limit = kWaitCycles;
+static int g_pair_withhold = 0;
+extern "C" void tb_debug_pair_withhold_arrive(int on, long long limit_cycles) {
+    g_pair_withhold = on ? 1 : 0;
+    g_pair_wait_limit = on && limit_cycles > 0 ? limit_cycles : kWaitCycles;
+}
+
 bool tb_conv_pair_supported(int ci, int co) { return (ci == 64 || ci == 32) && (co == 64 || co == 32); }
 
 tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
@@ -602,6 +628,8 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_
 #ifdef TB_TRACE
     p.trace = g_trace_buffer;
 #endif
+    p.wait_limit = g_pair_wait_limit;
+    p.withhold = g_pair_withhold;
     p.nbr = nbr;
     p.feats = reinterpret_cast<const uint8_t*>(feats);
     p.bias = bias;

@@ -43,13 +43,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // loop re-polls without a sleep: try_wait already suspends the thread in hardware while the phase
 // is open, and a __nanosleep between polls added microseconds to hand-offs that missed the first
 // poll.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          long long limit = kWaitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > limit) {
             *abort_flag = 1;
             atomicCAS(err, 0, TB_DEVERR_WAIT_TIMEOUT);
             return false;
@@ -249,13 +250,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
     return ok != 0;
 }
 // Bounded cluster-scope wait (arrivals may come from the peer CTA).
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          long long limit = kWaitCycles) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try_wait_cluster(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > limit) {
             *abort_flag = 1;
             atomicCAS(err, 0, TB_DEVERR_WAIT_TIMEOUT);
             return false;
@@ -275,13 +277,13 @@ __device__ __forceinline__ bool mbar_try_wait_cluster_relaxed(uint32_t bar, uint
     return ok != 0;
 }
 __device__ __forceinline__ bool mbar_wait_cluster_relaxed(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                                          int* err) {
+                                                          int* err, long long limit = kWaitCycles) {
     if (mbar_try_wait_cluster_relaxed(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try_wait_cluster_relaxed(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > limit) {
             *abort_flag = 1;
             atomicCAS(err, 0, TB_DEVERR_WAIT_TIMEOUT);
             return false;
