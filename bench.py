@@ -1259,6 +1259,20 @@ def run_configs_line(args):
     return 0
 
 
+def run_one_config(args):
+    """`--op config --config NAME`: one BASELINE configuration's conv alone (for profiling)."""
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _load_package()
+    if args.config == "c3":
+        r = measure_c2s(dev, max(3, args.steps), max(3, args.warmup), cpu=not args.no_cpu)
+    else:
+        r = measure_conv_config(args.config, dev, max(3, args.steps), max(3, args.warmup), cpu=not args.no_cpu)
+    _emit({"metric": f"configuration {args.config}", "n_gpus": 1, "configs": {args.config: r}})
+    return 0
+
+
 def run_configs(dev, steps, warmup, cpu=True):
     """Every BASELINE configuration other than the headline C4 step (see CFG_TABLE), C3's C2S
     block, and the C4 conv on decoder-ordered and Morton-ordered rows."""
@@ -1295,17 +1309,19 @@ def main():
     ap.add_argument("--workload", default=WORKLOAD, choices=["c4", "c4s"],
                     help="c4 (default, the benchmark) or c4s (half scale, for profiler captures)")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config entries of the headline line")
-    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s", "decode", "mesh", "configs"],
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c5_32", "c5_512"],
+                    help="the configuration of --op config")
+    ap.add_argument("--op", default="stack", choices=["stack", "convnext", "c2s", "decode", "mesh", "configs", "config"],
                     help="stack (default, the benchmark: map + conv x2), convnext (one ConvNeXt block), c2s "
                          "(one C2S up-block), decode (the sparse decoder UNet) or mesh (dual_grid_to_mesh)")
     args = ap.parse_args()
-    if args.op in ("convnext", "c2s", "decode", "mesh", "configs"):
+    if args.op in ("convnext", "c2s", "decode", "mesh", "configs", "config"):
         if args.impl == "reference" or args.gpus != 1:
             print(json.dumps({"impl": args.impl, "unavailable": f"--op {args.op} is a single-GPU measurement of "
                               "our kernels; its CPU baseline is in the line's cpu_baseline"}))
             return 0
         return {"convnext": run_convnext, "c2s": run_c2s, "decode": run_decode, "mesh": run_mesh,
-                "configs": run_configs_line}[args.op](args)
+                "configs": run_configs_line, "config": run_one_config}[args.op](args)
     if args.impl == "reference":
         return run_reference(args)
     return run_gpu(args)
