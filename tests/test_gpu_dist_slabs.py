@@ -19,7 +19,7 @@ def _global_tap(tl):
     return ((tl // 3) % 3) * 9 + (tl % 3) * 3 + tl // 9
 
 
-@pytest.mark.parametrize("name,world", [("c2", 1), ("c2", 2), ("c2", 5), ("c1", 8), ("c5_32", 3)])
+@pytest.mark.parametrize("name,world", [("c2", 1), ("c2", 2), ("c2", 5), ("c1", 8), ("c1", 16), ("c1", 30), ("c5_32", 3)])
 def test_slab_partition_map_and_conv(tb, name, world):
     from trellis_cpp_b200 import dist as tbdist, ops, synth
     coords_np = synth.coords_for(name)

@@ -119,6 +119,11 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_
                               const void* feats, int ci, const void* weight, const float* bias, int co,
                               tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
 bool tb_conv_pair_supported(int ci, int co);
+// The pair kernel over two row ranges in one launch ([row0, row0 + nrows) and
+// [row0b, row0b + nrowsb); nrowsb may be 0): the two edge planes of a slab.
+tb_status tb_conv_pair_launch2(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows, int64_t row0b,
+                               int64_t nrowsb, const void* feats, int ci, const void* weight, const float* bias, int co,
+                               tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
 tb_status tb_convnext_tail_launch(tb_ctx* ctx, int64_t n, int c, const void* h, tb_dtype h_dtype, const void* x,
                                   const float* nw, const float* nb, const void* w1, const float* b1, const void* w2,
                                   const float* b2, tb_dtype dtype, tb_dtype out_dtype, void* out);

@@ -109,10 +109,12 @@ struct PairParams {
     int64_t n;
     int co;
     int out_kind, epi;
-    int ntiles, npairs;    // npairs: end of the pair range (absolute)
-    int pr0;               // first pair of the range (rows 256 * pr0 ...)
-    int64_t row_begin;     // rows before it and at or past row_end are computed (whole pairs)
-    int64_t row_end;       // but not stored
+    int ntiles;
+    // Pairs of tiles to compute: pair pr0 + v for v < npa, then prb0 + (v - npa) for v < nv (a
+    // second, disjoint range, or none). Whole pairs are computed; only rows inside
+    // [row_begin, row_end) or [row_begin_b, row_end_b) are stored.
+    int pr0, npa, prb0, nv;
+    int64_t row_begin, row_end, row_begin_b, row_end_b;
     int ring_rows;               // multiple of kBox
     int nbr_bulk;                // map pointer 16-byte aligned: tiles fetch indices with bulk copies
     uint32_t w_tap_bytes;        // (co/2) rows x 128 B, rounded up to 1024
@@ -121,6 +123,9 @@ struct PairParams {
     long long wait_limit;        // clock cycles a bounded wait may take (about 2 s)
     int withhold;                // test hook: the even CTA's first epilogue warp withholds one arrive
 };
+
+// the pair of tiles of work item v
+__device__ __forceinline__ int pair_at(const PairParams& p, int v) { return v < p.npa ? p.pr0 + v : p.prb0 + (v - p.npa); }
 
 template <int CI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -231,13 +236,14 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         // the first kNB - 1 tiles' indices
         {
             int j = 0;
-            for (int prj = p.pr0 + cid; prj < p.npairs && j < kNB - 1; prj += ncl, ++j) fetch_nbr(prj, j);
+            for (int vj = cid; vj < p.nv && j < kNB - 1; vj += ncl, ++j) fetch_nbr(pair_at(p, vj), j);
         }
         int it = 0, k = 0, koldest = 0, head = 0, used = 0;
         int buf = 0, ph = 0;                     // consumer side of the index buffers
         int fbuf = kNB - 1, fph = 0;             // next fetch: tile it + kNB - 1
         bool ok = true;
-        for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
+        for (int v = cid; v < p.nv && ok; v += ncl, ++it) {
+            const int pr = pair_at(p, v);
             const int64_t r0 = (int64_t)(2 * pr + (int)rank) * kTileM;
             const int nvalid = p.n - r0 < kTileM ? (int)(p.n - r0) : kTileM;
             if (leader && lane == 0) TB_STAMP(10, it);
@@ -321,12 +327,12 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             }
             if (!ok) break;
             // indices of tile it + kNB - 1 into the buffer of tile it - 1, once its builders are done
-            const int prf = pr + (kNB - 1) * ncl;
-            if (prf < p.npairs) {
+            const int vf = v + (kNB - 1) * ncl;
+            if (vf < p.nv) {
                 if (leader && lane == 0) TB_STAMP(14, 1024 + it);
                 if (!mbar_wait(nbre + 8 * fbuf, (uint32_t)(fph ^ 1), s_abort, p.err, p.wait_limit)) { ok = false; break; }
                 if (leader && lane == 0) TB_STAMP(14, 2048 + it);
-                fetch_nbr(prf, fbuf);
+                fetch_nbr(pair_at(p, vf), fbuf);
                 if (++fbuf == kNB) { fbuf = 0; fph ^= 1; }
             }
         }
@@ -348,7 +354,8 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         // and a lane that timed out must not leave the others to run them alone
         bool ok = __all_sync(0xffffffffu, mbar_wait(wbar, 0, s_abort, p.err, p.wait_limit));   // weights landed
         int it = 0, k = 0, buf = 0, ph = 0;
-        for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
+        for (int v = cid; v < p.nv && ok; v += ncl, ++it) {
+            const int pr = pair_at(p, v);
             if (!__all_sync(0xffffffffu, mbar_wait(nbrf + 8 * buf, (uint32_t)ph, s_abort, p.err, p.wait_limit))) {
                 ok = false;
                 break;
@@ -489,7 +496,8 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             const uint32_t dt = tmem_base + 64u * (uint32_t)mi;
             const uint32_t a_base = tmem_base + kACol0 + (uint32_t)G::kUnitCols * kNU * (uint32_t)mi;
             const uint32_t afh = af + 8 * kNU * mi, aeh = ae + 8 * kNU * mi;
-            for (int pr = p.pr0 + cid; pr < p.npairs && ok; pr += ncl, ++it) {
+            for (int v = cid; v < p.nv && ok; v += ncl, ++it) {
+            const int pr = pair_at(p, v);
                 // the epilogue has read this issuer's accumulator for the previous tile
                 ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(de + 8 * mi, (uint32_t)((it & 1) ^ 1), s_abort, p.err, p.wait_limit));
                 if (!ok) break;
@@ -540,7 +548,8 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
         const int q = warp;
         int it = 0;
         const size_t esize = p.out_kind == 0 ? 4 : 2;
-        for (int pr = p.pr0 + cid; pr < p.npairs; pr += ncl, ++it) {
+        for (int v = cid; v < p.nv; v += ncl, ++it) {
+            const int pr = pair_at(p, v);
             const uint32_t dph = (uint32_t)(it & 1);
             bool ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(df, dph, s_abort, p.err, p.wait_limit));
             if (ok) ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(df + 8, dph, s_abort, p.err, p.wait_limit));
@@ -571,7 +580,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 mbar_arrive_cluster_relaxed(de + 8, 0);
             }
             const int64_t row = (int64_t)(2 * pr + (int)rank) * kTileM + q * 32 + lane;
-            if (row >= p.row_begin && row < p.row_end) {
+            if ((row >= p.row_begin && row < p.row_end) || (row >= p.row_begin_b && row < p.row_end_b)) {
                 uint8_t* orow = p.out + (size_t)row * p.co * esize;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -613,6 +622,12 @@ bool tb_conv_pair_supported(int ci, int co) { return (ci == 64 || ci == 32) && (
 tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows,
                               const void* feats, int ci, const void* weight, const float* bias, int co,
                               tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
+    return tb_conv_pair_launch2(ctx, nbr, n, row0, nrows, 0, 0, feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
+}
+
+tb_status tb_conv_pair_launch2(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_t row0, int64_t nrows, int64_t row0b,
+                               int64_t nrowsb, const void* feats, int ci, const void* weight, const float* bias, int co,
+                               tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
     if (!tb_conv_pair_supported(ci, co))
         return tb_fail(ctx, TB_ERR_UNSUPPORTED, "pair conv needs ci and co in {32, 64}");
     if (!ctx->encode_tiled) {
@@ -640,11 +655,26 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_
     p.out_kind = out_dtype == TB_F32 ? 0 : (out_dtype == TB_F16 ? 1 : 2);
     p.epi = epi;
     p.ntiles = (int)((n + kTileM - 1) / kTileM);
-    // output rows [row0, row0 + nrows): whole pairs of tiles from the one holding row0
-    p.pr0 = (int)(row0 / (2 * kTileM));
-    p.npairs = (int)((row0 + nrows + 2 * kTileM - 1) / (2 * kTileM));
+    // output rows [row0, row0 + nrows) (and [row0b, row0b + nrowsb)): whole pairs of tiles from the
+    // one holding the first row; two ranges whose pairs meet become one run of pairs
+    auto pairs_of = [](int64_t r0, int64_t nr, int& a, int& b) {
+        a = (int)(r0 / (2 * kTileM));
+        b = (int)((r0 + nr + 2 * kTileM - 1) / (2 * kTileM));
+    };
+    int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+    pairs_of(row0, nrows, a0, a1);
+    if (nrows <= 0) a1 = a0;
+    if (nrowsb > 0) pairs_of(row0b, nrowsb, b0, b1);
+    if (nrowsb > 0 && b0 < a0) { std::swap(a0, b0); std::swap(a1, b1); }
+    if (nrowsb > 0 && b0 <= a1) { a1 = std::max(a1, b1); b0 = b1 = 0; }
+    p.pr0 = a0;
+    p.npa = a1 - a0;
+    p.prb0 = b0;
+    p.nv = p.npa + (b1 - b0);
     p.row_begin = row0;
-    p.row_end = row0 + nrows;
+    p.row_end = row0 + std::max<int64_t>(nrows, 0);
+    p.row_begin_b = nrowsb > 0 ? row0b : 0;
+    p.row_end_b = nrowsb > 0 ? row0b + nrowsb : 0;
     const int nhalf = co / 2;
     const uint32_t rb = 2u * (uint32_t)ci;      // bytes per voxel row
     p.w_tap_bytes = ((uint32_t)nhalf * rb + 1023u) & ~1023u;
@@ -684,7 +714,8 @@ tb_status tb_conv_pair_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64_
             swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the feature view");
     }
-    const int nclusters = std::max(1, std::min(p.npairs - p.pr0, ctx->num_sms / 2));
+    if (p.nv <= 0) return TB_OK;
+    const int nclusters = std::max(1, std::min(p.nv, ctx->num_sms / 2));
     cudaError_t e = cudaSuccess;
     auto kern = ci == 64 ? k_submconv_pair<64> : k_submconv_pair<32>;
     size_t& smem_set = ctx->pair_smem_set[ci == 64 ? 0 : 1];

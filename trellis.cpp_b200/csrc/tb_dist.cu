@@ -518,6 +518,12 @@ tb_status tb_dist_submconv(tb_dist* d, void* feats, int ci, const void* weight, 
         return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: bad dtype");
     const tb_zslab& sl = d->slab;
     if (sl.n_local == 0) return TB_OK;
+    if (out_dtype != TB_F32 && out_dtype != dtype)
+        return dfail(d, TB_ERR_UNSUPPORTED, "tb_dist_submconv: out_dtype must be TB_F32 or the operand dtype");
+    if (epi != TB_EPI_NONE && epi != TB_EPI_SILU) return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: bad epilogue");
+    if (!tb_aligned16(feats) || !tb_aligned16(weight) || !tb_aligned16(out) || (bias && !tb_aligned16(bias)))
+        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: feats/weight/bias/out must be 16-byte aligned");
+    if (feats == out) return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: out must not alias feats");
     tb_ctx* ctx = d->ctx;
     cudaStream_t st = ctx->stream;
     TB_DCUDA(d, cudaSetDevice(ctx->device));
@@ -580,6 +586,14 @@ tb_status tb_dist_submconv(tb_dist* d, void* feats, int ci, const void* weight, 
     }
     if (any) TB_DCUDA(d, cudaStreamWaitEvent(st, d->ev_join, 0));
     if (one_plane) return conv(ob, sl.n_owned);
+    // the two edge planes: one launch of the pair kernel where it serves the shape
+    const bool pair = dtype != TB_F32 && tb_conv_pair_supported(ci, co) &&
+                      (ctx->conv_path == TB_CONV_AUTO || ctx->conv_path == TB_CONV_PAIR);
+    if (pair && sl.n_edge_lo > 0 && sl.n_edge_hi > 0) {
+        tb_status cs = tb_conv_pair_launch2(ctx, (const int32_t*)d->nbr, sl.n_local, ob, sl.n_edge_lo, oe - sl.n_edge_hi,
+                                            sl.n_edge_hi, feats, ci, d->wperm, bias, co, dtype, out_dtype, epi, out);
+        return cs == TB_OK ? TB_OK : dfail(d, cs, std::string("tb_dist_submconv: ") + ctx->last_error);
+    }
     s = conv(ob, sl.n_edge_lo);
     if (s != TB_OK) return s;
     return conv(oe - sl.n_edge_hi, sl.n_edge_hi);
