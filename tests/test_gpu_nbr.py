@@ -124,3 +124,33 @@ def test_gpu_map_equals_the_reference_function(tb, name):
     c = synth.coords_for(name)
     got = ops.build_neighbor_table(torch.from_numpy(c).cuda()).cpu().numpy()
     assert np.array_equal(got, oracle.ref_build_neighbor_table(c))
+
+
+def _big_cases():
+    """Inputs of 300k voxels: duplicates (the later row wins), batches, voxels on every face of
+    the bounding box, a negative coordinate (which sends the build to the voxel hash), and a
+    bounding box of ~1e15 cells."""
+    rng = np.random.default_rng(12)
+    n = 300_000
+    dup = rng.integers(0, 64, (n, 3)).astype(np.int32)                     # ~1.1x duplicated, box faces hit
+    bat = np.concatenate([rng.integers(0, 5, (n, 1)), rng.integers(100, 160, (n, 3))], 1).astype(np.int32)
+    far = random_voxels(n, 70, 13)
+    far[::1000] += np.array([900_000, 0, 0], np.int32)                         # bounding box of ~1e15 cells
+    bad = random_voxels(n, 70, 14)
+    bad[5] = [-3, 4, 5]                                                       # negative: the voxel hash builds it
+    return [("duplicates", dup), ("batches", bat), ("huge box", far), ("negative", bad)]
+
+
+@pytest.mark.parametrize("case", ["duplicates", "batches", "huge box", "negative"])
+def test_large_builds_all_layouts(tb, case):
+    c = dict(_big_cases())[case]
+    assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+def test_builds_in_a_row_are_independent(tb):
+    """Builds in a row on different voxel sets of one context: each must match the oracle, so
+    the buckets an earlier build wrote cannot leak into a later one."""
+    from trellis_cpp_b200 import synth
+    sets = [synth.coords_for("c5_32")[:400_000], random_voxels(280_000, 80, 15), synth.coords_for("c5_32")[::7]]
+    for c in sets + sets[:1]:
+        assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
