@@ -9,9 +9,10 @@ features and weights resident in HBM. Metric: active voxels/s (whole job).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 N > 1 (torchrun, one rank per GPU): the voxels are cut into z-slabs at voxel-count
-quantiles; each rank owns one slab plus a one-voxel halo exchanged over NCCL (send/recv)
-before each conv, builds its local neighbor map and computes its owned rows. Total work is
-fixed as N grows ("scaling": "strong").
+quantiles; each rank owns one slab and holds two planes of each neighbour, exchanged over NCCL
+(send/recv) once per step while it builds its local neighbor map; conv 1 computes its owned rows
+and the nearest halo plane on each side, conv 2 its owned rows. Total work is fixed as N grows
+("scaling": "strong").
 
 `--impl reference` times the reference algorithm's CPU implementation (the oracle port in
 oracle/, all host threads) on a bounded sample of the same workload.
@@ -299,7 +300,7 @@ def run_gpu(args):
         step()
     torch.cuda.synchronize()
     if world > 1:
-        # each rank replays one CUDA graph per step (map, both convs with their NCCL halo exchanges)
+        # each rank replays one CUDA graph per step (the NCCL halo exchange beside the map, both convs)
         runner.capture(w1, w2)
         step = runner.replay
     if nbr_for_flops is not None:
@@ -363,17 +364,19 @@ def run_gpu(args):
 
     parity = None
     if world > 1:
-        # per-rank times of the map and of each conv (eager steps after the timed replays; a conv
-        # call includes its halo exchange, overlapped with the interior planes), slowest rank
+        # per-rank times of the map (with the halo exchange beside it) and of each conv (eager steps
+        # after the timed replays; conv 1 also computes the nearest halo plane on each side), slowest rank
+        w1l, w2l = runner.local_weight(w1), runner.local_weight(w2)
         evs = []
         for _ in range(max(3, min(args.steps, 10))):
             e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
             e[0].record()
+            runner.dist.exchange(runner.feats)
             runner.dist.build_map()
             e[1].record()
-            runner.dist.submconv(runner.feats, w1, None, epi="silu", out=runner.h)
+            runner.dist.submconv_grow(1, runner.feats, w1l, None, epi="silu", out=runner.h)
             e[2].record()
-            runner.dist.submconv(runner.h, w2, None, out=runner.out)
+            runner.dist.submconv_grow(0, runner.h, w2l, None, out=runner.out)
             e[3].record()
             evs.append(e)
         torch.cuda.synchronize()
@@ -387,7 +390,7 @@ def run_gpu(args):
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                     "frac": achieved / peak_tf, "traffic": None, "peak_source": f"{peak_kind} bf16_tflops (burst)",
                     "kernel": "k_submconv_pair (per GPU: one conv's owned-row FLOPs / the slowest rank's conv "
-                              "time, halo exchange included)", "flops_per_launch": flops_gpu}
+                              "time; conv 1 also recomputes one halo plane per side)", "flops_per_launch": flops_gpu}
         kernel_stats = {"conv_ms_slowest_rank": conv_ms_max, "map_ms_slowest_rank": map_ms_max,
                         "conv_ms_this_rank": conv_ms, "map_ms_this_rank": map_ms}
         # every owned row against the single-GPU step of the whole shell, run on each rank's GPU
@@ -429,7 +432,7 @@ def run_gpu(args):
 
     if world > 1 and not args.no_e2e:
         # end to end per rank: this rank's local coordinates and owned features from pinned host
-        # memory, the slab's map and both convs (halo exchanges inside), owned output rows back
+        # memory, the halo exchange beside the slab's map, both convs, owned output rows back
         rows_np = runner.rows.cpu().numpy()
         coords_loc_h = torch.from_numpy(np.ascontiguousarray(coords_np[rows_np])).pin_memory()
         feats_own_h = runner.feats[runner.owned].cpu().pin_memory()
@@ -463,7 +466,8 @@ def run_gpu(args):
         e2e = {"value": n_total / (e2e_ms / 1e3), "unit": "voxels/s", "h2d_bytes_per_step": int(nb[0].item()),
                "d2h_bytes_per_step": int(nb[1].item()), "steps": k_e2e, "ms_per_step": e2e_ms,
                "call": "per rank: pinned H2D of local coords + owned features, tb_dist_load_coords, "
-                       "tb_dist_build_map, tb_dist_submconv x2, D2H of owned rows (CUDA events, slowest rank)"}
+                       "tb_dist_exchange + tb_dist_build_map, tb_dist_submconv_grow x2, D2H of owned rows "
+                       "(CUDA events, slowest rank)"}
 
     cpu_baseline = None
     if rank == 0 and not args.no_cpu:

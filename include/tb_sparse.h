@@ -305,7 +305,7 @@ tb_status tb_gather_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int6
 tb_status tb_scatter_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int64_t m,
                           int64_t row_bytes, void* out);
 
-/* ---- multi-GPU sharded convs: z-slabs with a one-plane NCCL halo --------------------------
+/* ---- multi-GPU sharded convs: z-slabs with an NCCL halo -----------------------------------
  * No reference counterpart: the reference is single-GPU (src/sparse.cpp:94-118 only chunks
  * output rows on one device). These calls let its per-stage caller (src/shape_decoder.cpp:91-113:
  * build_neighbor_table, then the stage's sparse_submconv calls) run one process per GPU: each rank
@@ -322,12 +322,18 @@ tb_status tb_scatter_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int
  *   stream of its own; it owns neither ctx nor the communicator. With nccl_comm NULL nothing is
  *   exchanged: the caller puts the halo rows into feats before each tb_dist_submconv (one process
  *   driving several slabs, or world == 1).
+ * tb_dist_set_halo_planes: H, the planes of each neighbour a rank holds (1 by default, at most
+ *   TB_DIST_MAX_HALO); set before tb_dist_partition_zslab. A conv at an owned voxel reads one
+ *   plane beyond the slab; a stack of L convs whose intermediate results are not exchanged
+ *   (tb_dist_submconv_grow) reads L planes beyond it.
  * tb_dist_partition_zslab: every rank passes the same voxel set (device coords [n][stride]). The
  *   z axis is cut into `world` slabs of whole planes at voxel-count quantiles (tb_zslab_cuts);
- *   this rank owns z_lo <= z < z_hi and holds the neighbours' planes z_lo-1 and z_hi as a halo.
- *   Its local rows are [plane z_lo-1 | owned planes in z order | plane z_hi], each plane in the
- *   input's order, so the owned rows are local rows [owned_begin, owned_begin + n_owned).
- *   Synchronises (two small read-backs). Fails when the voxels span fewer z planes than ranks.
+ *   this rank owns z_lo <= z < z_hi and holds the neighbours' planes z_lo-H .. z_lo-1 and
+ *   z_hi .. z_hi+H-1 as a halo. Its local rows are [lower halo planes | owned planes | upper halo
+ *   planes], in z order and within a plane in the input's order, so the owned rows are local rows
+ *   [owned_begin, owned_begin + n_owned). Synchronises (two small read-backs). Fails when the
+ *   voxels span fewer z planes than ranks, and with TB_ERR_UNSUPPORTED when H > 1 and a slab
+ *   holds fewer than H planes (its neighbours' halos would reach past it).
  * tb_dist_local_rows: the global row of every local row (device int32 [n_local]), to gather a
  *   stage's features into local order (tb_gather_rows) and scatter owned outputs back.
  * tb_dist_load_coords: replace the local coordinates with coords_local (device [n_local][stride],
@@ -339,20 +345,33 @@ tb_status tb_scatter_rows(tb_ctx* ctx, const void* src, const int32_t* rows, int
  * tb_dist_submconv: one conv of tb_submconv's semantics on the local rows: feats [n_local][ci]
  *   holds the input's owned rows; the call fills its halo rows from the neighbours (NCCL send/recv
  *   of the edge planes, on the communication stream) while the interior planes are computed, then
- *   computes the two edge planes. out [n_local][co]: owned rows written, halo rows untouched;
+ *   computes the edge planes. out [n_local][co]: owned rows written, halo rows untouched;
  *   feats's halo rows are overwritten. Same dtype and shape rules as tb_submconv. Rows match the
  *   single-GPU conv up to fp32 accumulation order.
+ * tb_dist_exchange: the halo exchange alone: feats [n_local] rows of row_bytes (a multiple of
+ *   16) get the neighbours' edge planes in their halo rows. Enqueued on the communication stream
+ *   after the work already on ctx's stream, so work enqueued next on ctx's stream (the map build)
+ *   overlaps it; the next conv on the dist waits for it.
+ * tb_dist_local_weight: the weight [co][27][ci] with its taps in the local map's order (the
+ *   permutation tb_dist_submconv applies on every call), for tb_dist_submconv_grow.
+ * tb_dist_submconv_grow: a conv with no exchange over the owned rows and the `grow` halo planes
+ *   nearest the slab on each side (0 <= grow < H); feats's rows those outputs read -- up to grow + 1
+ *   halo planes -- must hold the neighbours' rows (tb_dist_exchange, or an earlier
+ *   tb_dist_submconv_grow with a larger grow). weight_local from tb_dist_local_weight. Other rows
+ *   of out are untouched. A stack of L convs then needs one exchange of L planes: conv l runs with
+ *   grow = L - 1 - l, recomputing the halo rows the next conv reads instead of exchanging them.
  * tb_dist_count_valid_pairs: present (voxel, tap) pairs over the owned rows; synchronises.
  * tb_dist_local_map: the dist-owned local map (device int32 [27][n_local]) after build_map. */
 typedef struct tb_dist tb_dist;
 typedef struct tb_zslab {
     int32_t z_lo, z_hi;             /* owned planes: z_lo <= z < z_hi */
-    int64_t n_local;                /* local rows: halo plane z_lo-1, owned planes, halo plane z_hi */
+    int64_t n_local;                /* local rows: lower halo planes, owned planes, upper halo planes */
     int64_t n_owned;
     int64_t owned_begin;            /* owned rows are local rows [owned_begin, owned_begin + n_owned) */
-    int64_t n_halo_lo, n_halo_hi;   /* rows of planes z_lo-1 and z_hi (received) */
-    int64_t n_edge_lo, n_edge_hi;   /* rows of planes z_lo and z_hi-1 (sent) */
+    int64_t n_halo_lo, n_halo_hi;   /* rows of planes z_lo-H .. z_lo-1 and z_hi .. z_hi+H-1 (received) */
+    int64_t n_edge_lo, n_edge_hi;   /* rows of planes z_lo .. z_lo+H-1 and z_hi-H .. z_hi-1 (sent) */
 } tb_zslab;
+#define TB_DIST_MAX_HALO 8
 
 tb_status tb_nccl_unique_id(uint8_t* id /* [128] */);
 tb_status tb_nccl_comm_create(const uint8_t* id /* [128] */, int rank, int world, int device, void** comm);
@@ -360,6 +379,7 @@ tb_status tb_nccl_comm_destroy(void* comm);
 tb_status tb_dist_create(tb_ctx* ctx, void* nccl_comm, int rank, int world, tb_dist** out);
 tb_status tb_dist_destroy(tb_dist* d);
 const char* tb_dist_last_error(const tb_dist* d);
+tb_status tb_dist_set_halo_planes(tb_dist* d, int planes);
 tb_status tb_dist_partition_zslab(tb_dist* d, const int32_t* coords, int64_t n, int coord_stride, tb_zslab* slab);
 tb_status tb_dist_local_rows(tb_dist* d, int32_t* rows);
 tb_status tb_dist_load_coords(tb_dist* d, const int32_t* coords_local);
@@ -367,6 +387,11 @@ tb_status tb_dist_build_map(tb_dist* d);
 tb_status tb_dist_local_map(const tb_dist* d, const int32_t** nbr);
 tb_status tb_dist_submconv(tb_dist* d, void* feats, int ci, const void* weight, const float* bias, int co,
                            tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out);
+tb_status tb_dist_exchange(tb_dist* d, void* feats, int64_t row_bytes);
+tb_status tb_dist_local_weight(tb_dist* d, const void* weight, int ci, int co, tb_dtype dtype, void* weight_local);
+tb_status tb_dist_submconv_grow(tb_dist* d, int grow, const void* feats, int ci, const void* weight_local,
+                                const float* bias, int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi,
+                                void* out);
 tb_status tb_dist_count_valid_pairs(tb_dist* d, int64_t* pairs);
 /* The slab cut on the host (what tb_dist_partition_zslab computes from its histogram): counts
  * [nz] = voxels of plane z_min + i; cuts [world + 1]: cuts[0] the first occupied plane,

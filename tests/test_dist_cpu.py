@@ -80,6 +80,87 @@ def test_slab_halo_exchange_and_conv(world):
         assert np.array_equal(allo, np.arange(allo.size)), "slabs must partition the voxels"
 
 
+def _worker_deep_halo(rank, world, init_file, result_dir):
+    """Two stacked convs with a two-plane halo and no exchange between them: the first conv also
+    computes the nearest halo plane on each side, which is all the second conv reads beyond the
+    slab (the step SlabRunner runs through tb_dist_exchange / tb_dist_submconv_grow)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from conftest import load_package
+    load_package()
+    import oracle
+    from trellis_cpp_b200 import dist as tbdist, synth
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+    try:
+        coords = synth.coords_for("c1")
+        n = coords.shape[0]
+        rng = np.random.default_rng(5)
+        feats = rng.standard_normal((n, 8)).astype(np.float32)
+        w1 = (rng.standard_normal((8, 27, 8)) / 15).astype(np.float32)
+        w2 = (rng.standard_normal((8, 27, 8)) / 15).astype(np.float32)
+        plan = tbdist.plan_slabs(coords, world, rank, halo=2)
+        gather = lambda t, idx: t.index_select(0, idx.long()).contiguous()   # noqa: E731
+        scatter = lambda t, idx, src: t.index_copy_(0, idx.long(), src)       # noqa: E731
+        x = torch.full((plan.n_local, 8), float("nan"), dtype=torch.float32)
+        x[torch.from_numpy(plan.own_local)] = torch.from_numpy(feats[plan.owned])
+        tbdist.exchange_halo(plan, x, gather, scatter)
+        zl = coords[plan.local_rows(), -1]
+        ok_halo = np.array_equal(x.numpy(), feats[plan.local_rows()])
+        ok_halo = ok_halo and (rank == 0 or set(zl[plan.recv_lo]) == {plan.z_lo - 2, plan.z_lo - 1})
+        nbr_local = oracle.build_neighbor_table(coords[plan.local_rows()])
+        # conv 1 on the owned rows and the nearest halo plane; every other row of h stays NaN
+        grow1 = (zl >= plan.z_lo - (1 if rank > 0 else 0)) & (zl < plan.z_hi + (1 if rank < world - 1 else 0))
+        h_all = oracle.submconv(nbr_local, x.numpy(), w1, silu=True).astype(np.float32)
+        h = np.full_like(h_all, np.nan)
+        h[grow1] = h_all[grow1]
+        out_local = oracle.submconv(nbr_local, h, w2)[plan.own_local]
+        nbr_g = oracle.build_neighbor_table(coords)
+        hg = oracle.submconv(nbr_g, feats, w1, silu=True).astype(np.float32)
+        out_global = oracle.submconv(nbr_g, hg, w2)[plan.owned]
+        np.savez(os.path.join(result_dir, f"r{rank}.npz"), owned=plan.owned, ok_halo=ok_halo,
+                 ok_conv=np.array_equal(out_local, out_global))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_two_plane_halo_two_convs(world):
+    with tempfile.TemporaryDirectory() as d:
+        init_file = os.path.join(d, "pg")
+        mp.start_processes(_worker_deep_halo, args=(world, init_file, d), nprocs=world, start_method="spawn")
+        owned = []
+        for r in range(world):
+            res = np.load(os.path.join(d, f"r{r}.npz"))
+            assert bool(res["ok_halo"]), f"rank {r}: halo rows differ"
+            assert bool(res["ok_conv"]), f"rank {r}: the two-conv stack differs from the single-rank stack"
+            owned.append(res["owned"])
+        assert np.array_equal(np.sort(np.concatenate(owned)), np.arange(sum(o.size for o in owned)))
+
+
+def test_deep_halo_plan(tb):
+    """halo=2: the rank holds two planes of each neighbour, sends its two edge planes, and a slab
+    thinner than the halo is refused."""
+    from trellis_cpp_b200 import dist as tbdist, synth
+    coords = synth.coords_for("c2")
+    z = coords[:, -1]
+    world = 4
+    plans = [tbdist.plan_slabs(coords, world, r, halo=2) for r in range(world)]
+    for r, pl in enumerate(plans):
+        zl = z[pl.local_rows()]
+        if r > 0:
+            assert set(zl[pl.recv_lo]) == {pl.z_lo - 2, pl.z_lo - 1}
+            assert set(zl[pl.send_lo]) == {pl.z_lo, pl.z_lo + 1}
+            # what rank r-1 sends up is what rank r receives from below, row for row
+            prev = plans[r - 1]
+            assert np.array_equal(prev.local_rows()[prev.send_hi], pl.local_rows()[pl.recv_lo])
+        if r < world - 1:
+            assert set(zl[pl.recv_hi]) == {pl.z_hi, pl.z_hi + 1}
+    rng = np.random.default_rng(6)
+    c = rng.integers(0, 6, (500, 3)).astype(np.int32)      # 6 planes over 4 ranks: slabs of 1-2 planes
+    with pytest.raises(ValueError):
+        tbdist.plan_slabs(c, 4, 0, halo=2)
+
+
 def test_slab_bounds_balanced(tb):
     from trellis_cpp_b200 import dist as tbdist, synth
     coords = synth.coords_for("c2")

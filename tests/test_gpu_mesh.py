@@ -80,7 +80,9 @@ def test_mesh_batch_column(tb, mesh_golden):
     assert np.array_equal(v3, v4) and np.array_equal(f3, f4)
 
 
-@pytest.mark.parametrize("res,dups", [(96, 0), (160, 2000)])
+# dups -1: rows left in ascending coordinate order (the map's sorted layout); 0: shuffled; > 0:
+# that many duplicate rows appended
+@pytest.mark.parametrize("res,dups", [(96, 0), (160, 2000), (128, -1)])
 def test_mesh_large_shell(tb, res, dups):
     rng = np.random.default_rng(res)
     g = np.arange(res)
@@ -88,7 +90,10 @@ def test_mesh_large_shell(tb, res, dups):
     r = np.sqrt((x - res / 2) ** 2 + (y - res / 2) ** 2 + (z - res / 2) ** 2)
     keep = np.abs(r - res * 0.4) < 1.0
     c = np.stack([x[keep], y[keep], z[keep]], 1).astype(np.int32)
-    c = c[rng.permutation(len(c))] if dups == 0 else np.concatenate([c, c[rng.integers(0, len(c), dups)]])
+    if dups == 0:
+        c = c[rng.permutation(len(c))]
+    elif dups > 0:
+        c = np.concatenate([c, c[rng.integers(0, len(c), dups)]])
     f7 = (rng.standard_normal((len(c), 7)) * 2).astype(np.float32)
     verts, faces = _run(c, f7, res)
     rv, rf, gap = oracle.dual_grid_mesh(c, f7, res)

@@ -154,3 +154,62 @@ def test_builds_in_a_row_are_independent(tb):
     sets = [synth.coords_for("c5_32")[:400_000], random_voxels(280_000, 80, 15), synth.coords_for("c5_32")[::7]]
     for c in sets + sets[:1]:
         assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+# Rows in ascending (batch, x, y, z) order build the map from a table of (batch, x, y) columns
+# (the sorted layout); rows in any other order, coordinates outside [0, 2^20 - 2] or a bounding
+# box with more columns than the table holds go to the block layout. These cases sit on either
+# side of each condition and must all give the reference's map.
+def _sorted(c):
+    c = np.asarray(c, np.int64)
+    k = (c[:, 0] << 60) | (c[:, 1] << 40) | (c[:, 2] << 20) | c[:, 3] if c.shape[1] == 4 else \
+        (c[:, 0] << 40) | (c[:, 1] << 20) | c[:, 2]
+    return c[np.argsort(k, kind="stable")].astype(np.int32)
+
+
+def _sorted_cases():
+    rng = np.random.default_rng(21)
+    dup_col = np.concatenate([rng.integers(0, 3, (4000, 1)), rng.integers(0, 9, (4000, 3))], 1)
+    dup_col[:1500] = [1, 4, 4, 5]                        # one voxel 1500 times: the binary-search path
+    long_cols = np.concatenate([np.zeros((6000, 1), np.int64), rng.integers(0, 2, (6000, 2)),
+                                rng.integers(0, 4000, (6000, 1))], 1)       # 4 columns of ~1500 rows
+    top = (1 << 20) - 2
+    edges = np.array([[0, 0, 0, 0], [0, 0, 0, 1], [0, 0, 1, 0], [0, 1, 0, 0], [0, top, top, top],
+                      [0, top - 1, top, top], [0, top, top - 1, top], [0, top, top, top - 1],
+                      [15, 0, 0, 0], [15, 0, 0, 1]])                      # 2^40 columns: block layout
+    small_box = np.concatenate([rng.integers(0, 16, (3000, 1)), rng.integers(0, 6, (3000, 3))], 1)
+    return {"duplicates": _sorted(dup_col), "long columns": _sorted(long_cols),
+            "huge box": _sorted(edges), "batches 0-15": _sorted(small_box),
+            "3-column coords": _sorted(random_voxels(5000, 20, 22))}
+
+
+@pytest.mark.parametrize("case", ["duplicates", "long columns", "huge box", "batches 0-15", "3-column coords"])
+def test_sorted_layout(tb, case):
+    c = _sorted_cases()[case]
+    assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+@pytest.mark.parametrize("change", ["one pair swapped", "negative coordinate", "batch 16", "last row first"])
+def test_sorted_layout_rejections(tb, change):
+    from trellis_cpp_b200 import synth
+    c = synth.coords_for("c2").copy()
+    if change == "one pair swapped":
+        c[[1000, 1001]] = c[[1001, 1000]]
+    elif change == "negative coordinate":
+        c[0, 1] = -1
+    elif change == "batch 16":
+        c[-1, 0] = 16
+    else:
+        c = np.concatenate([c[-1:], c[:-1]])
+    assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+
+
+def test_sorted_and_unsorted_builds_alternate(tb):
+    """The sorted layout's column table and the block layout's buckets share memory: builds that
+    alternate between the layouts on one context must each match the oracle."""
+    from trellis_cpp_b200 import synth
+    s = synth.coords_for("c2")
+    u = s[np.random.default_rng(23).permutation(s.shape[0])]
+    for c in (s, u, s, u[:7000], s[:9000]):
+        assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
+

@@ -97,6 +97,10 @@ SIGNATURES = {
     "tb_dist_local_map": (_st, [_vp, ctypes.POINTER(_vp)]),
     "tb_dist_submconv": (_st, [_vp, _vp, _int, _vp, _vp, _int, _int, _int, _int, _vp]),
     "tb_dist_count_valid_pairs": (_st, [_vp, ctypes.POINTER(_i64)]),
+    "tb_dist_set_halo_planes": (_st, [_vp, _int]),
+    "tb_dist_exchange": (_st, [_vp, _vp, _i64]),
+    "tb_dist_local_weight": (_st, [_vp, _vp, _int, _int, _int, _vp]),
+    "tb_dist_submconv_grow": (_st, [_vp, _int, _vp, _int, _vp, _vp, _int, _int, _int, _int, _vp]),
     "tb_zslab_cuts": (_st, [_vp, _i32, _i32, _int, _vp]),
 }
 

@@ -48,20 +48,24 @@ constexpr int kNbrInts = 27 * kNbrRow;
 constexpr int kNB = 3;                  // neighbor-index buffers (two tiles fetched ahead)
 constexpr int kNR = 8;               // range descriptor ring
 constexpr uint32_t kACol0 = 128;     // first A column; issuer k accumulates in columns 64k..64k+co-1
-constexpr int kNUMax = 6;            // A unit slots per issuer at Ci = 32 (3 at Ci = 64)
+constexpr int kPairTPU64 = 2;         // taps per A unit at Ci = 64
+constexpr int kPairTPU32 = 4;         // taps per A unit at Ci = 32
+constexpr int kNUMax = 6;            // A unit slots per issuer (192 TMEM columns / unit width)
 // nbrf[kNB] nbre[kNB] rngf[8] rnge[8] af[2][kNU] ae[2][kNU] df[2] de[2] wbar drain (sized for kNUMax)
 constexpr int kNumBars = kNB + kNB + kNR + kNR + 2 * kNUMax + 2 * kNUMax + 2 + 2 + 1 + 1;
 
 // Per-Ci geometry: row bytes, 16-byte chunks per row, TMEM columns per tap, K steps per tap, A
 // unit slots per issuer (384 A columns split over two issuers, two taps per unit).
-template <int CI>
+template <int CI, int TPU>
 struct PairGeom {
     static_assert(CI == 32 || CI == 64, "pair kernel: Ci 32 or 64");
+    static_assert(TPU >= 2 && TPU <= 5 && TPU * (CI / 2) <= 96, "pair kernel: taps per A unit");
+    static constexpr int kTPU = TPU;                   // taps per A unit (one wait, one commit)
     static constexpr int kRB = 2 * CI;
     static constexpr int kChunks = kRB / 16;
     static constexpr int kTapCols = CI / 2;
     static constexpr int kKSteps = CI / 16;
-    static constexpr int kUnitCols = 2 * kTapCols;
+    static constexpr int kUnitCols = TPU * kTapCols;
     static constexpr int kNU = 192 / kUnitCols;
     // 16-byte chunk c of ring row b after the TMA swizzle (128 B: bits 4-6 ^= bits 7-9; 64 B:
     // bits 4-5 ^= bits 7-8 of the byte offset)
@@ -127,11 +131,11 @@ struct PairParams {
 // the pair of tiles of work item v
 __device__ __forceinline__ int pair_at(const PairParams& p, int v) { return v < p.npa ? p.pr0 + v : p.prb0 + (v - p.npa); }
 
-template <int CI>
+template <int CI, int TPU>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap fmap,
                 const PairParams p) {
-    using G = PairGeom<CI>;
+    using G = PairGeom<CI, TPU>;
     constexpr int kNU = G::kNU;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -373,31 +377,30 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 }
                 if (leader && half == 0 && q == 0 && lane == 0) TB_STAMP(5, k);
                 const int rlo = s_rng[slot].lo, rlen = s_rng[slot].len, roff = s_rng[slot].off;
-                // this group's taps with stage parity == half, two at a time: taps t0, t0 + 2 |
-                // t0 + 4, t0 + 6 | t0 + 8 (those inside the group). The lane's neighbor rows of all
-                // of them are read first, so each unit's row loads wait on one load latency only.
+                // this group's taps with stage parity == half (t0, t0 + 2, ..., t0 + 8, those inside
+                // the group), TPU of them per unit. The lane's neighbor rows of all of them are read
+                // first, so each unit's row loads wait on one load latency only.
                 const int t0 = 9 * g + ((half ^ (seq0 + 9 * g)) & 1);
+                const int tend = 9 * g + 9;
                 int32_t vrow[5];
 #pragma unroll
                 for (int e = 0; e < 5; ++e) {
                     const int tt = t0 + 2 * e;
-                    vrow[e] = (tt < 9 * g + 9 && row_valid) ? rows[tt * kNbrRow + ((tt * n4) & 3) + i] : sentinel;
+                    vrow[e] = (tt < tend && row_valid) ? rows[tt * kNbrRow + ((tt * n4) & 3) + i] : sentinel;
                 }
 #pragma unroll
-                for (int j = 0; j < 3; ++j) {
-                    const int t = t0 + 4 * j;
-                    if (t >= 9 * g + 9 || !ok) break;
-                    const int t2 = t + 2;
-                    const bool has2 = t2 < 9 * g + 9;
+                for (int j = 0; j < (5 + TPU - 1) / TPU; ++j) {
+                    const int t = t0 + 2 * TPU * j;
+                    if (t >= tend || !ok) break;
                     const bool tr0 = leader && half == 0 && q == 0 && lane == 0;
                     if (tr0) TB_STAMP(8, seq0 + t);
-                    // both taps' 32 rows of A in registers before the slot wait: ring row, missing
+                    // the unit's rows of A in registers before the slot wait: ring row, missing
                     // (zero) or, for a row outside the held range, global memory
-                    uint32_t rv[2][G::kTapCols];
+                    uint32_t rv[TPU][G::kTapCols];
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        if (e == 1 && !has2) break;
-                        const int32_t v = vrow[2 * j + e];
+                    for (int e = 0; e < TPU; ++e) {
+                        if (TPU * j + e >= 5 || t + 2 * e >= tend) break;
+                        const int32_t v = vrow[TPU * j + e];
                         if (v == sentinel) {
 #pragma unroll
                             for (int c = 0; c < G::kTapCols; ++c) rv[e][c] = 0u;
@@ -419,14 +422,13 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                             }
                         }
                     }
-                    [[maybe_unused]] const int s1 = seq0 + t, s2 = seq0 + t2;
 #ifdef TB_TRACE
                     if (p.trace) {
                         int nring = 0, nglob = 0, nmiss = 0;
 #pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            if (e == 1 && !has2) break;
-                            const int tv = e == 0 ? t : t2;
+                        for (int e = 0; e < TPU; ++e) {
+                            if (TPU * j + e >= 5 || t + 2 * e >= tend) break;
+                            const int tv = t + 2 * e;
                             const int32_t v = row_valid ? rows[tv * kNbrRow + ((tv * n4) & 3) + i] : sentinel;
                             const unsigned m1 = __ballot_sync(0xffffffffu, v == sentinel);
                             const unsigned m2 = __ballot_sync(0xffffffffu, v != sentinel && (uint32_t)(v - rlo) < (uint32_t)rlen);
@@ -434,11 +436,9 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                         }
                         if (lane == 0) { TB_COUNT(0, nring); TB_COUNT(1, nglob); TB_COUNT(2, nmiss); }
                     }
-#endif
-#ifdef TB_TRACE
                     if (tr0) {
-                        asm volatile("" :: "r"(rv[0][G::kTapCols - 1]), "r"(rv[1][G::kTapCols - 1]));   // rows arrived
-                        TB_STAMP(6, s1);
+                        asm volatile("" :: "r"(rv[0][G::kTapCols - 1]));   // rows arrived
+                        TB_STAMP(6, seq0 + t);
                     }
 #endif
                     // the unit slot's previous taps have been multiplied
@@ -448,25 +448,26 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                         break;
                     }
                     tc_fence_after();
-                    if (tr0) TB_STAMP(9, s1);
+                    if (tr0) TB_STAMP(9, seq0 + t);
                     const uint32_t ua = a_lane + (uint32_t)G::kUnitCols * (uint32_t)u;
-                    if constexpr (CI == 64) tmem_st_x32(ua, rv[0]);
-                    else tmem_st_x16(ua, rv[0]);
-                    if (tr0) TB_STAMP(11, s1);
-                    if (has2) {
-                        if constexpr (CI == 64) tmem_st_x32(ua + (uint32_t)G::kTapCols, rv[1]);
-                        else tmem_st_x16(ua + (uint32_t)G::kTapCols, rv[1]);
+#pragma unroll
+                    for (int e = 0; e < TPU; ++e) {
+                        if (TPU * j + e >= 5 || t + 2 * e >= tend) break;
+                        if constexpr (CI == 64) tmem_st_x32(ua + (uint32_t)(e * G::kTapCols), rv[e]);
+                        else tmem_st_x16(ua + (uint32_t)(e * G::kTapCols), rv[e]);
+                        if (tr0 && e == 0) TB_STAMP(11, seq0 + t);
                     }
                     tmem_wait_st();
-                    if (tr0) TB_STAMP(12, s1);
+                    if (tr0) TB_STAMP(12, seq0 + t);
                     tc_fence_before();
                     __syncwarp();
-                    if (tr0) TB_STAMP(13, s1);
+                    if (tr0) TB_STAMP(13, seq0 + t);
                     if (lane == 0) {
                         mbar_arrive_cluster_relaxed(afh + 8 * u, 0);
                         if (q == 0) {
-                            TB_STAMP(leader ? 1 : 3, s1);
-                            if (has2) TB_STAMP(leader ? 1 : 3, s2);
+#pragma unroll
+                            for (int e = 0; e < TPU; ++e)
+                                if (t + 2 * e < tend) TB_STAMP(leader ? 1 : 3, seq0 + t + 2 * e);
                         }
                     }
                     if (++u == kNU) { u = 0; uph ^= 1; }
@@ -489,8 +490,8 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
             const uint64_t wdesc0 = smem_desc<G::kRB>(smem_u32(w_base));
             const uint32_t wstep = p.w_tap_bytes >> 4;
             // issuer mi takes the taps whose sequence number (27 * tile + tap) has parity mi, in
-            // the units its builder half writes them: per tap group, taps t0, t0 + 2 | t0 + 4,
-            // t0 + 6 | t0 + 8 (those inside the group); one wait and one commit per unit
+            // the units its builder half writes them: per tap group, taps t0, t0 + 2, ..., t0 + 8
+            // (those inside the group), TPU per unit; one wait and one commit per unit
             int it = 0, u = 0, uph = 0;
             bool ok = true;
             const uint32_t dt = tmem_base + 64u * (uint32_t)mi;
@@ -505,24 +506,24 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
                 const int seq0 = 27 * it;
                 uint32_t acc = 0;
                 for (int g = 0; g < 3 && ok; ++g) {
-                    for (int t = 9 * g + ((mi ^ (seq0 + 9 * g)) & 1); t < 9 * g + 9; t += 4) {
-                        const bool has2 = t + 2 < 9 * g + 9;
+                    for (int t = 9 * g + ((mi ^ (seq0 + 9 * g)) & 1); t < 9 * g + 9; t += 2 * TPU) {
                         ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(afh + 8 * u, (uint32_t)uph, s_abort, p.err, p.wait_limit));
                         if (!ok) break;
                         if (lane == 0) TB_STAMP(2, seq0 + t);
                         tc_fence_after();
                         if (elect_one()) {
-                            // K = 16 per MMA: 8 TMEM columns of A, 32 bytes (2 descriptor units) of B
+                            // K = 16 per MMA: 8 TMEM columns of A, 32 bytes (2 descriptor units) of B;
+                            // the unit's taps t, t + 2, ... sit kTapCols columns apart
                             const uint32_t at = a_base + (uint32_t)G::kUnitCols * (uint32_t)u;
                             const uint64_t bd = wdesc0 + (uint64_t)(wstep * (uint32_t)t);
 #pragma unroll
-                            for (int ks = 0; ks < G::kKSteps; ++ks)
-                                tc_mma_ts_pair(dt, at + 8u * ks, bd + 2u * ks, p.idesc, ks == 0 ? acc : 1u);
-                            if (has2) {
-                                const uint64_t bd2 = bd + (uint64_t)(2u * wstep);
+                            for (int e = 0; e < TPU; ++e) {
+                                if (t + 2 * e >= 9 * g + 9) break;
 #pragma unroll
                                 for (int ks = 0; ks < G::kKSteps; ++ks)
-                                    tc_mma_ts_pair(dt, at + (uint32_t)G::kTapCols + 8u * ks, bd2 + 2u * ks, p.idesc, 1u);
+                                    tc_mma_ts_pair(dt, at + (uint32_t)(e * G::kTapCols) + 8u * ks,
+                                                   bd + (uint64_t)(2u * (uint32_t)e * wstep) + 2u * ks, p.idesc,
+                                                   (e == 0 && ks == 0) ? acc : 1u);
                             }
                             tc_commit_pair(aeh + 8 * u, 0x3);
                         }
@@ -717,7 +718,9 @@ tb_status tb_conv_pair_launch2(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64
     if (p.nv <= 0) return TB_OK;
     const int nclusters = std::max(1, std::min(p.nv, ctx->num_sms / 2));
     cudaError_t e = cudaSuccess;
-    auto kern = ci == 64 ? k_submconv_pair<64> : k_submconv_pair<32>;
+    // taps per A unit: at Ci = 32 a tap is half as wide, and four-tap units halve the per-unit
+    // hand-offs (waits, fences, commits) that bound the kernel at that width
+    auto kern = ci == 64 ? k_submconv_pair<64, kPairTPU64> : k_submconv_pair<32, kPairTPU32>;
     size_t& smem_set = ctx->pair_smem_set[ci == 64 ? 0 : 1];
     if (smem > smem_set) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

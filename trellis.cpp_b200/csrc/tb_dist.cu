@@ -179,6 +179,11 @@ struct tb_dist {
     // the plan
     bool planned = false, mapped = false;
     int stride = 3;
+    int halo = 1;                 // planes held per side (tb_dist_set_halo_planes)
+    int64_t halo_rows_lo[TB_DIST_MAX_HALO] = {};   // rows of plane z_lo - 1 - k
+    int64_t halo_rows_hi[TB_DIST_MAX_HALO] = {};   // rows of plane z_hi + k
+    int64_t plane_rows_lo = 0, plane_rows_hi = 0;  // rows of the owned planes z_lo and z_hi - 1
+    bool exchange_pending = false;                 // ev_join marks an exchange the next conv waits for
     tb_zslab slab{};
     void* rows = nullptr;         // int32 [n_local]: the global row of each local row
     void* coords = nullptr;       // int32 [n_local][stride]: local coordinates, (z, x, y) order
@@ -401,22 +406,38 @@ tb_status tb_dist_partition_zslab(tb_dist* d, const int32_t* coords, int64_t n, 
     std::vector<int32_t> cuts((size_t)d->world + 1);
     if (tb_zslab_cuts(counts.data(), (int32_t)nz, zr[0], d->world, cuts.data()) != TB_OK)
         return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_partition_zslab: fewer occupied z planes than ranks");
+    const int H = d->halo;
+    if (H > 1 && d->world > 1)          // every rank checks every slab, so all ranks fail alike
+        for (int r = 0; r < d->world; ++r)
+            if (cuts[(size_t)r + 1] - cuts[(size_t)r] < H)
+                return dfail(d, TB_ERR_UNSUPPORTED, "tb_dist_partition_zslab: a slab holds fewer planes than the halo");
     auto plane = [&](int64_t z) -> int64_t { return (z >= zr[0] && z <= zr[1]) ? counts[(size_t)(z - zr[0])] : 0; };
     tb_zslab sl{};
     sl.z_lo = cuts[(size_t)d->rank];
     sl.z_hi = cuts[(size_t)d->rank + 1];
     const bool has_lo = d->rank > 0, has_hi = d->rank < d->world - 1;
-    sl.n_halo_lo = has_lo ? plane((int64_t)sl.z_lo - 1) : 0;
-    sl.n_halo_hi = has_hi ? plane(sl.z_hi) : 0;
-    sl.n_edge_lo = plane(sl.z_lo);
-    sl.n_edge_hi = plane((int64_t)sl.z_hi - 1);
+    for (int k = 0; k < TB_DIST_MAX_HALO; ++k) {
+        d->halo_rows_lo[k] = has_lo && k < H ? plane((int64_t)sl.z_lo - 1 - k) : 0;
+        d->halo_rows_hi[k] = has_hi && k < H ? plane((int64_t)sl.z_hi + k) : 0;
+    }
+    const int he = std::min<int>(H, sl.z_hi - sl.z_lo);    // edge planes (a one-rank slab may be thin)
+    for (int k = 0; k < H; ++k) {
+        sl.n_halo_lo += d->halo_rows_lo[k];
+        sl.n_halo_hi += d->halo_rows_hi[k];
+    }
+    for (int k = 0; k < he; ++k) {
+        sl.n_edge_lo += plane((int64_t)sl.z_lo + k);
+        sl.n_edge_hi += plane((int64_t)sl.z_hi - 1 - k);
+    }
+    d->plane_rows_lo = plane(sl.z_lo);
+    d->plane_rows_hi = plane((int64_t)sl.z_hi - 1);
     sl.n_owned = 0;
     for (int64_t z = sl.z_lo; z < sl.z_hi; ++z) sl.n_owned += plane(z);
     sl.owned_begin = sl.n_halo_lo;
     sl.n_local = sl.n_halo_lo + sl.n_owned + sl.n_halo_hi;
     // 3. the local rows: every row sorted stably by its plane index (rows outside the slab last)
-    const int32_t plane0 = sl.z_lo - (has_lo ? 1 : 0);
-    const uint32_t nplanes = (uint32_t)((int64_t)sl.z_hi + (has_hi ? 1 : 0) - plane0);
+    const int32_t plane0 = sl.z_lo - (has_lo ? H : 0);
+    const uint32_t nplanes = (uint32_t)((int64_t)sl.z_hi + (has_hi ? H : 0) - plane0);
     int end_bit = 1;
     while (end_bit < 32 && (1u << end_bit) <= nplanes) ++end_bit;
     k_slab_keys<<<grid_for(n, sms), 256, 0, st>>>(coords, n, coord_stride, plane0, nplanes, keys_in, vals_in);
@@ -508,70 +529,110 @@ tb_status tb_dist_count_valid_pairs(tb_dist* d, int64_t* pairs) {
     return TB_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// The arguments of a dist conv, checked alike by tb_dist_submconv and tb_dist_submconv_grow.
+tb_status dist_conv_args(tb_dist* d, const char* who, const void* feats, int ci, const void* weight,
+                         const float* bias, int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi,
+                         const void* out) {
+    const std::string w(who);
+    if (!d->mapped) return dfail(d, TB_ERR_INVALID_ARG, w + ": build the local map first");
+    if (!feats || !weight || !out || ci <= 0 || co <= 0)
+        return dfail(d, TB_ERR_INVALID_ARG, w + ": null pointer or channels <= 0");
+    if (dtype != TB_F32 && dtype != TB_F16 && dtype != TB_BF16) return dfail(d, TB_ERR_INVALID_ARG, w + ": bad dtype");
+    if (out_dtype != TB_F32 && out_dtype != dtype)
+        return dfail(d, TB_ERR_UNSUPPORTED, w + ": out_dtype must be TB_F32 or the operand dtype");
+    if (epi != TB_EPI_NONE && epi != TB_EPI_SILU) return dfail(d, TB_ERR_INVALID_ARG, w + ": bad epilogue");
+    if (!tb_aligned16(feats) || !tb_aligned16(weight) || !tb_aligned16(out) || (bias && !tb_aligned16(bias)))
+        return dfail(d, TB_ERR_INVALID_ARG, w + ": feats/weight/bias/out must be 16-byte aligned");
+    if (feats == out) return dfail(d, TB_ERR_INVALID_ARG, w + ": out must not alias feats");
+    return TB_OK;
+}
+
+// w_local = the weight with its taps in local order
+tb_status dist_permute(tb_dist* d, const void* weight, int ci, int co, tb_dtype dtype, void* w_local) {
+    const int64_t welems = (int64_t)co * 27 * ci;
+    tb_ctx* ctx = d->ctx;
+    if (tb_dtype_size(dtype) == 4)
+        k_permute_taps<uint32_t><<<grid_for(welems, ctx->num_sms), 256, 0, ctx->stream>>>(
+            reinterpret_cast<const uint32_t*>(weight), co, ci, reinterpret_cast<uint32_t*>(w_local));
+    else
+        k_permute_taps<uint16_t><<<grid_for(welems, ctx->num_sms), 256, 0, ctx->stream>>>(
+            reinterpret_cast<const uint16_t*>(weight), co, ci, reinterpret_cast<uint16_t*>(w_local));
+    TB_DCUDA(d, cudaGetLastError());
+    return TB_OK;
+}
+
+// The halo exchange of the edge planes of f (rows of row_bytes) on the communication stream, after
+// the work already on ctx's stream; ev_join marks its end and the next conv waits for it. Nothing
+// moves without a communicator (the caller has filled the halo rows).
+tb_status dist_exchange(tb_dist* d, uint8_t* f, size_t row_bytes) {
+    const tb_zslab& sl = d->slab;
+    const int64_t ob = sl.owned_begin, oe = sl.owned_begin + sl.n_owned;
+    const bool lo = d->rank > 0, hi = d->rank < d->world - 1;
+    const bool any = d->comm && ((lo && (sl.n_edge_lo || sl.n_halo_lo)) || (hi && (sl.n_edge_hi || sl.n_halo_hi)));
+    if (!any) return TB_OK;
+    NcclApi& api = nccl();
+    TB_DCUDA(d, cudaEventRecord(d->ev_fork, d->ctx->stream));
+    TB_DCUDA(d, cudaStreamWaitEvent(d->comm_stream, d->ev_fork, 0));
+    ncclResult_t r = api.group_start();
+    if (r != ncclSuccess) return dnccl(d, r, "ncclGroupStart");
+    // a plane that is empty on one side is empty on the other (it is the same plane), so both
+    // ranks skip the same transfers
+    if (lo && sl.n_edge_lo && r == ncclSuccess)
+        r = api.send(f + (size_t)ob * row_bytes, (size_t)sl.n_edge_lo * row_bytes, ncclUint8, d->rank - 1, d->comm,
+                     d->comm_stream);
+    if (lo && sl.n_halo_lo && r == ncclSuccess)
+        r = api.recv(f, (size_t)sl.n_halo_lo * row_bytes, ncclUint8, d->rank - 1, d->comm, d->comm_stream);
+    if (hi && sl.n_edge_hi && r == ncclSuccess)
+        r = api.send(f + (size_t)(oe - sl.n_edge_hi) * row_bytes, (size_t)sl.n_edge_hi * row_bytes, ncclUint8,
+                     d->rank + 1, d->comm, d->comm_stream);
+    if (hi && sl.n_halo_hi && r == ncclSuccess)
+        r = api.recv(f + (size_t)oe * row_bytes, (size_t)sl.n_halo_hi * row_bytes, ncclUint8, d->rank + 1, d->comm,
+                     d->comm_stream);
+    const ncclResult_t r2 = api.group_end();
+    if (r != ncclSuccess) return dnccl(d, r, "ncclSend/ncclRecv");
+    if (r2 != ncclSuccess) return dnccl(d, r2, "ncclGroupEnd");
+    TB_DCUDA(d, cudaEventRecord(d->ev_join, d->comm_stream));
+    d->exchange_pending = true;
+    return TB_OK;
+}
+
+// ctx's stream waits for the exchange in flight, if any
+tb_status dist_join(tb_dist* d) {
+    if (!d->exchange_pending) return TB_OK;
+    TB_DCUDA(d, cudaStreamWaitEvent(d->ctx->stream, d->ev_join, 0));
+    d->exchange_pending = false;
+    return TB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 tb_status tb_dist_submconv(tb_dist* d, void* feats, int ci, const void* weight, const float* bias, int co,
                            tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi, void* out) {
     if (!d) return TB_ERR_INVALID_ARG;
-    if (!d->mapped) return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: build the local map first");
-    if (!feats || !weight || !out || ci <= 0 || co <= 0)
-        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: null pointer or channels <= 0");
-    if (dtype != TB_F32 && dtype != TB_F16 && dtype != TB_BF16)
-        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: bad dtype");
+    tb_status s = dist_conv_args(d, "tb_dist_submconv", feats, ci, weight, bias, co, dtype, out_dtype, epi, out);
+    if (s != TB_OK) return s;
     const tb_zslab& sl = d->slab;
     if (sl.n_local == 0) return TB_OK;
-    if (out_dtype != TB_F32 && out_dtype != dtype)
-        return dfail(d, TB_ERR_UNSUPPORTED, "tb_dist_submconv: out_dtype must be TB_F32 or the operand dtype");
-    if (epi != TB_EPI_NONE && epi != TB_EPI_SILU) return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: bad epilogue");
-    if (!tb_aligned16(feats) || !tb_aligned16(weight) || !tb_aligned16(out) || (bias && !tb_aligned16(bias)))
-        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: feats/weight/bias/out must be 16-byte aligned");
-    if (feats == out) return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv: out must not alias feats");
     tb_ctx* ctx = d->ctx;
-    cudaStream_t st = ctx->stream;
     TB_DCUDA(d, cudaSetDevice(ctx->device));
     // the weight with its taps in local order
     const size_t esz = tb_dtype_size(dtype);
-    const size_t wbytes = (size_t)co * 27 * ci * esz;
-    tb_status s = dgrow(d, &d->wperm, &d->wperm_bytes, wbytes);
+    s = dgrow(d, &d->wperm, &d->wperm_bytes, (size_t)co * 27 * ci * esz);
     if (s != TB_OK) return s;
-    const int64_t welems = (int64_t)co * 27 * ci;
-    if (esz == 4)
-        k_permute_taps<uint32_t><<<grid_for(welems, ctx->num_sms), 256, 0, st>>>(
-            reinterpret_cast<const uint32_t*>(weight), co, ci, reinterpret_cast<uint32_t*>(d->wperm));
-    else
-        k_permute_taps<uint16_t><<<grid_for(welems, ctx->num_sms), 256, 0, st>>>(
-            reinterpret_cast<const uint16_t*>(weight), co, ci, reinterpret_cast<uint16_t*>(d->wperm));
-    TB_DCUDA(d, cudaGetLastError());
-
-    // the halo exchange of the input's edge planes, on the communication stream
-    const size_t row_bytes = (size_t)ci * esz;
-    uint8_t* f = reinterpret_cast<uint8_t*>(feats);
+    s = dist_permute(d, weight, ci, co, dtype, d->wperm);
+    if (s != TB_OK) return s;
+    s = dist_join(d);                 // an earlier tb_dist_exchange may still write these rows
+    if (s != TB_OK) return s;
+    s = dist_exchange(d, reinterpret_cast<uint8_t*>(feats), (size_t)ci * esz);
+    if (s != TB_OK) return s;
     const int64_t ob = sl.owned_begin, oe = sl.owned_begin + sl.n_owned;
-    const bool lo = d->rank > 0, hi = d->rank < d->world - 1;
-    // without a communicator the caller has filled the halo rows itself
-    const bool any = d->comm && ((lo && (sl.n_edge_lo || sl.n_halo_lo)) || (hi && (sl.n_edge_hi || sl.n_halo_hi)));
-    if (any) {
-        NcclApi& api = nccl();
-        TB_DCUDA(d, cudaEventRecord(d->ev_fork, st));
-        TB_DCUDA(d, cudaStreamWaitEvent(d->comm_stream, d->ev_fork, 0));
-        ncclResult_t r = api.group_start();
-        if (r != ncclSuccess) return dnccl(d, r, "ncclGroupStart");
-        // a plane that is empty on one side is empty on the other (it is the same plane), so
-        // both ranks skip the same transfers
-        if (lo && sl.n_edge_lo && r == ncclSuccess)
-            r = api.send(f + (size_t)ob * row_bytes, (size_t)sl.n_edge_lo * row_bytes, ncclUint8, d->rank - 1, d->comm,
-                         d->comm_stream);
-        if (lo && sl.n_halo_lo && r == ncclSuccess)
-            r = api.recv(f, (size_t)sl.n_halo_lo * row_bytes, ncclUint8, d->rank - 1, d->comm, d->comm_stream);
-        if (hi && sl.n_edge_hi && r == ncclSuccess)
-            r = api.send(f + (size_t)(oe - sl.n_edge_hi) * row_bytes, (size_t)sl.n_edge_hi * row_bytes, ncclUint8,
-                         d->rank + 1, d->comm, d->comm_stream);
-        if (hi && sl.n_halo_hi && r == ncclSuccess)
-            r = api.recv(f + (size_t)oe * row_bytes, (size_t)sl.n_halo_hi * row_bytes, ncclUint8, d->rank + 1, d->comm,
-                         d->comm_stream);
-        const ncclResult_t r2 = api.group_end();
-        if (r != ncclSuccess) return dnccl(d, r, "ncclSend/ncclRecv");
-        if (r2 != ncclSuccess) return dnccl(d, r2, "ncclGroupEnd");
-        TB_DCUDA(d, cudaEventRecord(d->ev_join, d->comm_stream));
-    }
+    const int64_t e_lo = d->plane_rows_lo, e_hi = d->plane_rows_hi;   // the planes that read the halo
     auto conv = [&](int64_t r0, int64_t nr) -> tb_status {
         if (nr <= 0) return TB_OK;
         tb_status cs = tb_submconv_range(ctx, (const int32_t*)d->nbr, sl.n_local, r0, nr, feats, ci, d->wperm, bias,
@@ -581,22 +642,81 @@ tb_status tb_dist_submconv(tb_dist* d, void* feats, int ci, const void* weight, 
     // the interior planes (z_lo + 1 .. z_hi - 2) read only owned rows: they run while the halo moves
     const bool one_plane = sl.z_hi - sl.z_lo == 1;
     if (!one_plane) {
-        s = conv(ob + sl.n_edge_lo, sl.n_owned - sl.n_edge_lo - sl.n_edge_hi);
+        s = conv(ob + e_lo, sl.n_owned - e_lo - e_hi);
         if (s != TB_OK) return s;
     }
-    if (any) TB_DCUDA(d, cudaStreamWaitEvent(st, d->ev_join, 0));
+    s = dist_join(d);
+    if (s != TB_OK) return s;
     if (one_plane) return conv(ob, sl.n_owned);
     // the two edge planes: one launch of the pair kernel where it serves the shape
     const bool pair = dtype != TB_F32 && tb_conv_pair_supported(ci, co) &&
                       (ctx->conv_path == TB_CONV_AUTO || ctx->conv_path == TB_CONV_PAIR);
-    if (pair && sl.n_edge_lo > 0 && sl.n_edge_hi > 0) {
-        tb_status cs = tb_conv_pair_launch2(ctx, (const int32_t*)d->nbr, sl.n_local, ob, sl.n_edge_lo, oe - sl.n_edge_hi,
-                                            sl.n_edge_hi, feats, ci, d->wperm, bias, co, dtype, out_dtype, epi, out);
+    if (pair && e_lo > 0 && e_hi > 0) {
+        tb_status cs = tb_conv_pair_launch2(ctx, (const int32_t*)d->nbr, sl.n_local, ob, e_lo, oe - e_hi, e_hi, feats,
+                                            ci, d->wperm, bias, co, dtype, out_dtype, epi, out);
         return cs == TB_OK ? TB_OK : dfail(d, cs, std::string("tb_dist_submconv: ") + ctx->last_error);
     }
-    s = conv(ob, sl.n_edge_lo);
+    s = conv(ob, e_lo);
     if (s != TB_OK) return s;
-    return conv(oe - sl.n_edge_hi, sl.n_edge_hi);
+    return conv(oe - e_hi, e_hi);
+}
+
+tb_status tb_dist_set_halo_planes(tb_dist* d, int planes) {
+    if (!d) return TB_ERR_INVALID_ARG;
+    if (planes < 1 || planes > TB_DIST_MAX_HALO)
+        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_set_halo_planes: planes must be in [1, TB_DIST_MAX_HALO]");
+    d->halo = planes;
+    d->planned = d->mapped = false;
+    return TB_OK;
+}
+
+tb_status tb_dist_exchange(tb_dist* d, void* feats, int64_t row_bytes) {
+    if (!d) return TB_ERR_INVALID_ARG;
+    if (!d->planned) return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_exchange: no partition yet");
+    if (!feats || row_bytes <= 0 || (row_bytes & 15) || !tb_aligned16(feats))
+        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_exchange: null or unaligned feats, or row_bytes not a multiple of 16");
+    if (d->slab.n_local == 0) return TB_OK;
+    TB_DCUDA(d, cudaSetDevice(d->ctx->device));
+    tb_status s = dist_join(d);
+    if (s != TB_OK) return s;
+    return dist_exchange(d, reinterpret_cast<uint8_t*>(feats), (size_t)row_bytes);
+}
+
+tb_status tb_dist_local_weight(tb_dist* d, const void* weight, int ci, int co, tb_dtype dtype, void* weight_local) {
+    if (!d) return TB_ERR_INVALID_ARG;
+    if (!weight || !weight_local || ci <= 0 || co <= 0 || weight == weight_local)
+        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_local_weight: null or aliasing pointers, or channels <= 0");
+    if (dtype != TB_F32 && dtype != TB_F16 && dtype != TB_BF16)
+        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_local_weight: bad dtype");
+    TB_DCUDA(d, cudaSetDevice(d->ctx->device));
+    return dist_permute(d, weight, ci, co, dtype, weight_local);
+}
+
+tb_status tb_dist_submconv_grow(tb_dist* d, int grow, const void* feats, int ci, const void* weight_local,
+                                const float* bias, int co, tb_dtype dtype, tb_dtype out_dtype, tb_epilogue epi,
+                                void* out) {
+    if (!d) return TB_ERR_INVALID_ARG;
+    tb_status s = dist_conv_args(d, "tb_dist_submconv_grow", feats, ci, weight_local, bias, co, dtype, out_dtype,
+                                 epi, out);
+    if (s != TB_OK) return s;
+    if (grow < 0 || grow >= d->halo)
+        return dfail(d, TB_ERR_INVALID_ARG, "tb_dist_submconv_grow: grow must be in [0, halo planes)");
+    const tb_zslab& sl = d->slab;
+    if (sl.n_local == 0) return TB_OK;
+    tb_ctx* ctx = d->ctx;
+    TB_DCUDA(d, cudaSetDevice(ctx->device));
+    s = dist_join(d);
+    if (s != TB_OK) return s;
+    // owned rows and the `grow` nearest halo planes on each side: one contiguous local range
+    int64_t r0 = sl.owned_begin, r1 = sl.owned_begin + sl.n_owned;
+    for (int k = 0; k < grow; ++k) {
+        r0 -= d->halo_rows_lo[k];
+        r1 += d->halo_rows_hi[k];
+    }
+    if (r1 <= r0) return TB_OK;
+    tb_status cs = tb_submconv_range(ctx, (const int32_t*)d->nbr, sl.n_local, r0, r1 - r0, feats, ci, weight_local,
+                                     bias, co, dtype, out_dtype, epi, out);
+    return cs == TB_OK ? TB_OK : dfail(d, cs, std::string("tb_dist_submconv_grow: ") + ctx->last_error);
 }
 
 }  // extern "C"

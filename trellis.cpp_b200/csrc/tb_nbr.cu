@@ -5,7 +5,12 @@
 // duplicate overwrites) and then does 27 lookups per voxel into a tap-major [27*N] table
 // whose absent entries hold N.
 //
-// Block layout (the default): voxels are grouped in 4x4x4 coordinate blocks. A hash table maps
+// Sorted layout (rows already in ascending (batch, x, y, z) order, as every caller in this
+// library and the reference's generators give them): a dense table of the row range of each
+// (batch, x, y) column of the bounding box, and per voxel a search of its 9 neighbouring columns
+// for z - 1, z, z + 1. Built with plain stores; no hashing. Details at the kernels below.
+//
+// Block layout (any row order): voxels are grouped in 4x4x4 coordinate blocks. A hash table maps
 // each block to a 64-entry bucket of rows indexed by the voxel's position in the block, so a
 // voxel's 27 lookups need at most 8 block probes (mostly its own block) and read buckets that
 // neighbouring voxels read too; in the usual x-major voxel order the table and buckets stay in
@@ -29,6 +34,7 @@
 #include "tb_common.cuh"
 
 #include <algorithm>
+#include <climits>
 #include <mutex>
 
 namespace {
@@ -129,8 +135,14 @@ constexpr int32_t kMaxCoord = (1 << 20) - 2;
 struct BlockCtl {
     unsigned int nblocks;   // buckets handed out
     int fallback;           // 1: build with the voxel hash instead
-    int pad[2];
+    int unsorted;           // 1: rows out of (batch, x, y, z) order, or a coordinate outside the block range
+    int sorted;             // 1: the sorted layout builds the map (decided by k_srt_clear)
+    int block_on;           // 1 - sorted: the gate of the block table's clear
+    int lo_inv[3];          // kMaxCoord - minimum of batch, x, y (atomicMax from zero)
+    int hi[3];              // maximum of batch, x, y
+    int pad;
 };
+static_assert(sizeof(BlockCtl) % 16 == 0, "the bucket pool after BlockCtl takes 16-byte stores");
 
 __device__ __forceinline__ uint64_t block_key(int32_t b, int32_t bx, int32_t by, int32_t bz) {
     return tb_key3(bx, by, bz) ^ ((uint64_t)(uint32_t)b << 60);
@@ -179,6 +191,7 @@ constexpr int kInsPer = 4;      // voxels per thread in the insert kernels
 // of these dependent round trips, not by bandwidth.
 __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int stride, Slot* __restrict__ t,
                              uint64_t mask, BlockCtl* __restrict__ ctl, unsigned int pool_blocks) {
+    if (ctl->sorted) return;
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * kInsPer;
     uint64_t k[kInsPer], h[kInsPer];
@@ -249,7 +262,7 @@ __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int 
 }
 
 __global__ void k_pool_clear(int32_t* __restrict__ pool, const BlockCtl* __restrict__ ctl) {
-    if (ctl->fallback) return;
+    if (ctl->fallback || ctl->sorted) return;
     const uint64_t total = (uint64_t)ctl->nblocks * 16;            // int4 words
     uint64_t j = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -261,7 +274,7 @@ __global__ void k_pool_clear(int32_t* __restrict__ pool, const BlockCtl* __restr
 // table probes are in flight together.
 __global__ void k_vox_insert(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t,
                              uint64_t mask, const BlockCtl* __restrict__ ctl, int32_t* __restrict__ pool) {
-    if (ctl->fallback) return;
+    if (ctl->fallback || ctl->sorted) return;
     const int64_t i0 = (int64_t)blockIdx.x * blockDim.x * kInsPer + threadIdx.x;
     uint64_t k[kInsPer], h[kInsPer];
     int loc[kInsPer];
@@ -300,7 +313,7 @@ __global__ void __launch_bounds__(kLookupThreads)
 k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t, uint64_t mask,
              const BlockCtl* __restrict__ ctl, const int32_t* __restrict__ pool, int32_t* __restrict__ nbr) {
     __shared__ int s_base[8][kLookupThreads];
-    if (ctl->fallback) return;
+    if (ctl->fallback || ctl->sorted) return;
     const int64_t i = blockIdx.x * (int64_t)kLookupThreads + threadIdx.x;
     if (i >= n) return;
     int32_t b, x, y, z;
@@ -339,6 +352,219 @@ k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Sl
         int32_t r = -1;
         if (bb >= 0) r = __ldg(pool + bb + (px[kd] | py[kh] | pz[kw]));
         nbr[(int64_t)j * n + i] = r >= 0 ? r : (int32_t)n;
+    }
+}
+
+// ---- sorted layout ---------------------------------------------------------------------------
+// When the rows are in ascending (batch, x, y, z) order (equal coordinates adjacent), every
+// (batch, x, y) column of voxels is a contiguous run of rows with z ascending. A dense table over
+// the columns of the bounding box holds each column's row range, built with plain stores from
+// the column boundaries of the row order (no hashing, no atomics), and a lookup finds z - 1, z
+// and z + 1 in the 9 columns (x + dx, y + dy) by a binary search and a short scan. It applies
+// when the block layout's coordinate range holds (so no two coordinates share a key and out-of-
+// grid neighbours are absent), the rows are in that order, and the box has at most col_cap
+// columns; the rows' z values are copied to a compact array so that a column's scan reads one
+// or two sectors. All three conditions are decided on the device; when one fails, the block
+// layout builds the map as before.
+
+constexpr int kSrtScan = 8;   // rows a column scan walks before it resolves the rest by binary search
+
+__device__ __forceinline__ uint64_t srt_key(int32_t b, int32_t x, int32_t y, int32_t z) {
+    return ((uint64_t)(uint32_t)b << 60) | ((uint64_t)(uint32_t)x << 40) | ((uint64_t)(uint32_t)y << 20) |
+           (uint64_t)(uint32_t)z;
+}
+
+struct SrtBox {
+    int32_t b0, x0, y0, x1, y1;
+    int64_t nx, ny;
+};
+
+__device__ __forceinline__ SrtBox srt_box(const BlockCtl* ctl) {
+    SrtBox bx;
+    bx.b0 = kMaxCoord - ctl->lo_inv[0];
+    bx.x0 = kMaxCoord - ctl->lo_inv[1];
+    bx.y0 = kMaxCoord - ctl->lo_inv[2];
+    bx.x1 = ctl->hi[1];
+    bx.y1 = ctl->hi[2];
+    bx.nx = (int64_t)bx.x1 - bx.x0 + 1;
+    bx.ny = (int64_t)bx.y1 - bx.y0 + 1;
+    return bx;
+}
+
+__device__ __forceinline__ int64_t srt_col(const SrtBox& bx, int32_t b, int32_t x, int32_t y) {
+    return ((int64_t)(b - bx.b0) * bx.nx + (x - bx.x0)) * bx.ny + (y - bx.y0);
+}
+
+__device__ __forceinline__ int warp_min(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ int warp_max(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Range and order check, the (batch, x, y) bounding box and the compact z array. Grid-stride
+// with one set of atomics per block.
+__global__ void __launch_bounds__(256) k_srt_check(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                   BlockCtl* __restrict__ ctl, int32_t* __restrict__ zc) {
+    __shared__ int s_red[8][7];
+    int bad = 0;
+    int lo[3] = {INT_MAX, INT_MAX, INT_MAX}, hi[3] = {INT_MIN, INT_MIN, INT_MIN};
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int32_t b, x, y, z;
+        read_coords(coords + i * stride, stride, b, x, y, z);
+        if ((uint32_t)x > (uint32_t)kMaxCoord || (uint32_t)y > (uint32_t)kMaxCoord ||
+            (uint32_t)z > (uint32_t)kMaxCoord || (uint32_t)b > 15u)
+            bad = 1;
+        zc[i] = z;
+        if (i > 0) {
+            int32_t pb, px, py, pz;
+            read_coords(coords + (i - 1) * stride, stride, pb, px, py, pz);
+            if (srt_key(pb, px, py, pz) > srt_key(b, x, y, z)) bad = 1;
+        }
+        lo[0] = min(lo[0], b); lo[1] = min(lo[1], x); lo[2] = min(lo[2], y);
+        hi[0] = max(hi[0], b); hi[1] = max(hi[1], x); hi[2] = max(hi[2], y);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    bad = __any_sync(0xffffffffu, bad);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) { lo[k] = warp_min(lo[k]); hi[k] = warp_max(hi[k]); }
+    if (lane == 0) {
+        s_red[warp][0] = bad;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) { s_red[warp][1 + k] = lo[k]; s_red[warp][4 + k] = hi[k]; }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+            bad |= s_red[w][0];
+#pragma unroll
+            for (int k = 0; k < 3; ++k) { lo[k] = min(lo[k], s_red[w][1 + k]); hi[k] = max(hi[k], s_red[w][4 + k]); }
+        }
+        if (bad) ctl->unsorted = 1;
+        if (lo[0] <= hi[0]) {          // the block saw at least one row; with bad unset they are in range
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                atomicMax(&ctl->lo_inv[k], kMaxCoord - max(0, min(lo[k], kMaxCoord)));
+                atomicMax(&ctl->hi[k], max(0, min(hi[k], kMaxCoord)));
+            }
+        }
+    }
+}
+
+// Decides the layout, then clears the column table of the bounding box.
+__global__ void k_srt_clear(BlockCtl* __restrict__ ctl, int2* __restrict__ cols, uint64_t col_cap) {
+    const SrtBox bx = srt_box(ctl);
+    const int64_t nb = (int64_t)ctl->hi[0] - bx.b0 + 1;
+    const bool applies = !ctl->unsorted && nb > 0 && bx.nx > 0 && bx.ny > 0 &&
+                         (uint64_t)nb * (uint64_t)bx.nx * (uint64_t)bx.ny <= col_cap;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        ctl->sorted = applies ? 1 : 0;
+        ctl->block_on = applies ? 0 : 1;
+    }
+    if (!applies) return;
+    const uint64_t cells = (uint64_t)nb * (uint64_t)bx.nx * (uint64_t)bx.ny;
+    for (uint64_t c = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; c < cells; c += (uint64_t)gridDim.x * blockDim.x)
+        cols[c] = make_int2(0, 0);
+}
+
+// cols[column] = {first row, last row + 1} from the column boundaries of the row order.
+__global__ void k_srt_fill(const int32_t* __restrict__ coords, int64_t n, int stride,
+                           const BlockCtl* __restrict__ ctl, int2* __restrict__ cols) {
+    if (!ctl->sorted) return;
+    const SrtBox bx = srt_box(ctl);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int32_t b, x, y, z;
+        read_coords(coords + i * stride, stride, b, x, y, z);
+        const int64_t c = srt_col(bx, b, x, y);
+        bool first = i == 0, last = i == n - 1;
+        if (!first) {
+            int32_t pb, px, py, pz;
+            read_coords(coords + (i - 1) * stride, stride, pb, px, py, pz);
+            first = srt_col(bx, pb, px, py) != c;
+        }
+        if (!last) {
+            int32_t qb, qx, qy, qz;
+            read_coords(coords + (i + 1) * stride, stride, qb, qx, qy, qz);
+            last = srt_col(bx, qb, qx, qy) != c;
+        }
+        if (first) cols[c].x = (int)i;
+        if (last) cols[c].y = (int)(i + 1);
+    }
+}
+
+// First k in [lo, hi) with zc[k] > v (hi when none).
+__device__ __forceinline__ int srt_upper(const int32_t* __restrict__ zc, int lo, int hi, int v) {
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(zc + mid) <= v) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+// The last rows of z - 1, z and z + 1 (the reference's later duplicate wins) among the column
+// rows [s, e), whose z values ascend; -1 where absent.
+__device__ __forceinline__ void srt_col_find(const int32_t* __restrict__ zc, int s, int e, int z,
+                                             int& rm, int& r0, int& rp) {
+    rm = r0 = rp = -1;
+    int lo = s, hi = e;                       // first row with z' >= z - 1
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(zc + mid) < z - 1) lo = mid + 1; else hi = mid;
+    }
+    int k = lo;
+    for (int step = 0; step < kSrtScan; ++step, ++k) {
+        if (k >= e) return;
+        const int d = __ldg(zc + k) - z;
+        if (d > 1) return;
+        if (d < 0) rm = k; else if (d == 0) r0 = k; else rp = k;
+    }
+    if (k >= e || __ldg(zc + k) > z + 1) return;
+    // more than kSrtScan rows hold z - 1 .. z + 1 (duplicates): the last of each by binary search
+    const int pm = srt_upper(zc, lo, e, z - 1), p0 = srt_upper(zc, pm, e, z), pp = srt_upper(zc, p0, e, z + 1);
+    rm = pm > lo && __ldg(zc + pm - 1) == z - 1 ? pm - 1 : -1;
+    r0 = p0 > pm && __ldg(zc + p0 - 1) == z ? p0 - 1 : -1;
+    rp = pp > p0 && __ldg(zc + pp - 1) == z + 1 ? pp - 1 : -1;
+}
+
+// Slot of a tap in the tap list (-1 when the list does not hold it).
+template <int NT>
+__device__ __forceinline__ constexpr int slot_of_tap(int tap) {
+    for (int j = 0; j < NT; ++j)
+        if (tap_at<NT>(j) == tap) return j;
+    return -1;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(256)
+k_srt_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const BlockCtl* __restrict__ ctl,
+             const int2* __restrict__ cols, const int32_t* __restrict__ zc, int32_t* __restrict__ nbr) {
+    if (!ctl->sorted) return;
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const SrtBox bx = srt_box(ctl);
+    int32_t b, x, y, z;
+    read_coords(coords + i * stride, stride, b, x, y, z);
+#pragma unroll
+    for (int kd = 0; kd < 3; ++kd) {
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+            const int jm = slot_of_tap<NT>(kd * 9 + kh * 3), j0 = slot_of_tap<NT>(kd * 9 + kh * 3 + 1),
+                      jp = slot_of_tap<NT>(kd * 9 + kh * 3 + 2);
+            if (jm < 0 && j0 < 0 && jp < 0) continue;
+            const int32_t xx = x + kd - 1, yy = y + kh - 1;
+            int rm = -1, r0 = -1, rp = -1;
+            if (xx >= bx.x0 && xx <= bx.x1 && yy >= bx.y0 && yy <= bx.y1) {
+                const int2 se = __ldg(cols + srt_col(bx, b, xx, yy));
+                if (se.y > se.x) srt_col_find(zc, se.x, se.y, z, rm, r0, rp);
+            }
+            if (jm >= 0) nbr[(int64_t)jm * n + i] = rm >= 0 ? rm : (int32_t)n;
+            if (j0 >= 0) nbr[(int64_t)j0 * n + i] = r0 >= 0 ? r0 : (int32_t)n;
+            if (jp >= 0) nbr[(int64_t)jp * n + i] = rp >= 0 ? rp : (int32_t)n;
+        }
     }
 }
 
@@ -450,8 +676,9 @@ size_t tb_nbr_workspace_bytes(int64_t n) {
 
 namespace {
 
-// Block layout first; its kernels and the voxel-hash kernels read BlockCtl::fallback, so
-// exactly one of the two writes the map.
+// Sorted layout first, then the block layout, then the voxel hash: each later layout's kernels
+// return at once unless the earlier ones did not apply (BlockCtl::sorted, BlockCtl::fallback),
+// so exactly one writes the map.
 template <int NT>
 tb_status nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws) {
     const uint64_t cap = tb_hash_capacity(n);                   // voxel-hash table (fallback)
@@ -464,10 +691,26 @@ tb_status nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int st
     int32_t* pool = reinterpret_cast<int32_t*>(after + sizeof(BlockCtl));
     const int tpb = 256;
     TB_CUDA_TRY(ctx, cudaMemsetAsync(ctl, 0, sizeof(BlockCtl), ctx->stream));
-    const int clear_blocks = (int)std::min<uint64_t>((cap_b + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
-    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap_b, reinterpret_cast<int*>(t + cap), nullptr);
-    TB_LAUNCH_CHECK(ctx, "k_hash_clear");
     const int64_t blocks = (n + tpb - 1) / tpb;
+    // sorted layout: its column table takes the bucket pool's memory and the compact z array the
+    // voxel-hash table's; the block and voxel-hash layouts run only when it does not apply and
+    // then overwrite both
+    const int grid_stride_blocks = (int)std::min<int64_t>(blocks, (int64_t)ctx->num_sms * 8);
+    int2* cols = reinterpret_cast<int2*>(pool);
+    int32_t* zc = reinterpret_cast<int32_t*>(t);
+    const uint64_t col_cap = pool_blocks * 64 * sizeof(int32_t) / sizeof(int2);
+    k_srt_check<<<grid_stride_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, ctl, zc);
+    TB_LAUNCH_CHECK(ctx, "k_srt_check");
+    k_srt_clear<<<ctx->num_sms * 8, tpb, 0, ctx->stream>>>(ctl, cols, col_cap);
+    TB_LAUNCH_CHECK(ctx, "k_srt_clear");
+    k_srt_fill<<<grid_stride_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, ctl, cols);
+    TB_LAUNCH_CHECK(ctx, "k_srt_fill");
+    k_srt_lookup<NT><<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, ctl, cols, zc, nbr);
+    TB_LAUNCH_CHECK(ctx, "k_srt_lookup");
+    // block layout
+    const int clear_blocks = (int)std::min<uint64_t>((cap_b + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
+    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap_b, reinterpret_cast<int*>(t + cap), &ctl->block_on);
+    TB_LAUNCH_CHECK(ctx, "k_hash_clear");
     const int64_t ins_blocks = (n + (int64_t)tpb * kInsPer - 1) / ((int64_t)tpb * kInsPer);
     k_blk_insert<<<(unsigned)ins_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, (unsigned)pool_blocks);
     TB_LAUNCH_CHECK(ctx, "k_blk_insert");

@@ -1,24 +1,26 @@
-"""Multi-GPU z-slab sharding of a voxel set with one-voxel halos over NCCL.
+"""Multi-GPU z-slab sharding of a voxel set with halos of whole z planes over NCCL.
 
 The reference runs on one device and only chunks output rows within it
 (src/sparse.cpp:94-118); this module splits the voxels across ranks (one process per GPU).
 
 * :func:`plan_slabs` cuts the z axis into `world` slabs at voxel-count quantiles (whole z
-  planes, so every voxel belongs to exactly one rank). Rank r owns z in [z_lo, z_hi) and needs
-  the planes z_lo-1 and z_hi of its neighbours as a halo: a 3x3x3 submanifold conv at an owned
-  voxel reads only voxels within one plane.
-* The local rows are the owned rows and the two halo planes ordered by z, each plane in the
-  input's order: [plane z_lo-1 | owned planes | plane z_hi]. A local neighbor map built over them
-  gives every owned row exactly its global neighbors (tests check this against the single-rank
-  oracle); the halo planes and the edge planes are contiguous ranges (received and sent in
-  place), and the interior planes, which need no halo, are one range.
+  planes, so every voxel belongs to exactly one rank). Rank r owns z in [z_lo, z_hi) and holds
+  `halo` planes of each neighbour: a 3x3x3 submanifold conv at an owned voxel reads only voxels
+  within one plane, and two stacked convs read two planes when the first conv's halo rows are
+  recomputed locally instead of exchanged.
+* The local rows are the owned rows and the halo planes ordered by z, each plane in the input's
+  order: [lower halo planes | owned planes | upper halo planes]. A local neighbor map built over
+  them gives every owned row exactly its global neighbors (tests check this against the
+  single-rank oracle); the halo planes and the edge planes are contiguous ranges (received and
+  sent in place), and the interior planes, which need no halo, are one range.
 * :func:`exchange_halo` sends the boundary planes to the neighbouring ranks with point-to-point
   send/recv (NCCL over NVLink on GPUs, gloo in the CPU tests) into contiguous buffers and
   scatters them to the halo rows' local positions. Nothing else is communicated: no all-reduce,
   no all-gather.
-* :class:`SlabRunner` is the benchmark step on one rank, through the C ABI (tb_dist_*): the slab's
-  neighbor map, conv(SiLU), conv, each conv exchanging its input's halo over NCCL while its
-  interior planes compute. :func:`plan_slabs` and :func:`exchange_halo` are the host-side
+* :class:`SlabRunner` is the benchmark step on one rank, through the C ABI (tb_dist_*): one NCCL
+  exchange of the input's two-plane halo, overlapped with the slab's neighbor map, then
+  conv(SiLU) over the owned rows and the nearest halo plane on each side, then conv over the
+  owned rows (no exchange between the convs). :func:`plan_slabs` and :func:`exchange_halo` are the host-side
   statement of the same plan and exchange, which the CPU tests run with gloo ranks.
 """
 from __future__ import annotations
@@ -37,14 +39,14 @@ class SlabPlan:
     z_lo: int                  # owned planes: z_lo <= z < z_hi
     z_hi: int
     owned: np.ndarray          # global row ids of owned voxels, in local order (by z, then input order)
-    halo_lo: np.ndarray        # global row ids of plane z_lo-1 (owned by rank-1), ascending
-    halo_hi: np.ndarray        # global row ids of plane z_hi (owned by rank+1), ascending
+    halo_lo: np.ndarray        # global row ids of the lower halo planes (owned by rank-1), ascending
+    halo_hi: np.ndarray        # global row ids of the upper halo planes (owned by rank+1), ascending
     local: np.ndarray          # global row ids of the local rows: owned + halo, ordered by z
     own_local: np.ndarray      # local positions of the owned rows
-    send_lo: np.ndarray        # local positions of plane z_lo (sent to rank-1), ascending
-    send_hi: np.ndarray        # local positions of plane z_hi-1 (sent to rank+1), ascending
-    recv_lo: np.ndarray        # local positions of plane z_lo-1 (received from rank-1)
-    recv_hi: np.ndarray        # local positions of plane z_hi (received from rank+1)
+    send_lo: np.ndarray        # local positions of the lowest owned planes (sent to rank-1), ascending
+    send_hi: np.ndarray        # local positions of the highest owned planes (sent to rank+1), ascending
+    recv_lo: np.ndarray        # local positions of the lower halo planes (received from rank-1)
+    recv_hi: np.ndarray        # local positions of the upper halo planes (received from rank+1)
 
     @property
     def n_owned(self) -> int:
@@ -83,26 +85,31 @@ def slab_bounds(z: np.ndarray, world: int) -> np.ndarray:
     return cuts
 
 
-def plan_slabs(coords: np.ndarray, world: int, rank: int) -> SlabPlan:
-    """Slab of `rank` for coords [N,3] (x,y,z) or [N,4] (b,x,y,z); z is the last column."""
+def plan_slabs(coords: np.ndarray, world: int, rank: int, halo: int = 1) -> SlabPlan:
+    """Slab of `rank` for coords [N,3] (x,y,z) or [N,4] (b,x,y,z); z is the last column. The rank
+    holds `halo` planes of each neighbour (planes z_lo-halo .. z_lo-1 and z_hi .. z_hi+halo-1)
+    and sends its `halo` edge planes on each side; with halo > 1 every slab must hold at least
+    `halo` planes, so that a halo never reaches past the neighbouring slab."""
     z = np.asarray(coords)[:, -1].astype(np.int64)
     cuts = slab_bounds(z, world)
+    if halo > 1 and world > 1 and int(np.min(np.diff(cuts))) < halo:
+        raise ValueError(f"a slab holds fewer than {halo} planes")
     z_lo, z_hi = int(cuts[rank]), int(cuts[rank + 1])
     owned = np.nonzero((z >= z_lo) & (z < z_hi))[0]
-    halo_lo = np.nonzero(z == z_lo - 1)[0] if rank > 0 else np.zeros(0, np.int64)
-    halo_hi = np.nonzero(z == z_hi)[0] if rank < world - 1 else np.zeros(0, np.int64)
+    none = np.zeros(0, np.int64)
+    halo_lo = np.nonzero((z >= z_lo - halo) & (z < z_lo))[0] if rank > 0 else none
+    halo_hi = np.nonzero((z >= z_hi) & (z < z_hi + halo))[0] if rank < world - 1 else none
     # local order: by plane, and within a plane the input order (a stable sort by z), as
-    # tb_dist_partition_zslab orders them: [plane z_lo-1 | plane z_lo .. z_hi-1 | plane z_hi]
+    # tb_dist_partition_zslab orders them: [lower halo planes | plane z_lo .. z_hi-1 | upper halo planes]
     sel = np.sort(np.concatenate([owned, halo_lo, halo_hi]))
     local = sel[np.argsort(z[sel], kind="stable")]
     zl = z[local]
-    # a sender packs its boundary plane in ascending global order, which is the order of the
-    # receiver's halo positions for the same plane
-    none = np.zeros(0, np.int64)
-    send_lo = np.nonzero(zl == z_lo)[0] if rank > 0 else none
-    send_hi = np.nonzero(zl == z_hi - 1)[0] if rank < world - 1 else none
-    recv_lo = np.nonzero(zl == z_lo - 1)[0] if rank > 0 else none
-    recv_hi = np.nonzero(zl == z_hi)[0] if rank < world - 1 else none
+    # a sender packs its boundary planes in local order (by z, then ascending global row), which is
+    # the order of the receiver's halo positions for the same planes
+    send_lo = np.nonzero((zl >= z_lo) & (zl < z_lo + halo))[0] if rank > 0 else none
+    send_hi = np.nonzero((zl >= z_hi - halo) & (zl < z_hi))[0] if rank < world - 1 else none
+    recv_lo = np.nonzero(zl < z_lo)[0] if rank > 0 else none
+    recv_hi = np.nonzero(zl >= z_hi)[0] if rank < world - 1 else none
     own_local = np.nonzero((zl >= z_lo) & (zl < z_hi))[0]
     owned = local[own_local]
     return SlabPlan(rank, world, z_lo, z_hi, owned, halo_lo, halo_hi, local, own_local, send_lo, send_hi,
@@ -163,13 +170,17 @@ def finish_halo(handle) -> None:
 
 class SlabRunner:
     """The benchmark step on one rank: map + conv(SiLU) + conv on a z-slab, through the C ABI's
-    tb_dist_* calls (the partition, the slab's neighbor map and convs whose halo exchange runs
-    inside the call over NCCL, overlapped with the interior planes).
+    tb_dist_* calls. The slab holds two halo planes per side; one NCCL exchange of the input's
+    halo runs while the slab's neighbor map is built, conv 1 computes the owned rows and the
+    nearest halo plane on each side (the rows conv 2 reads beyond the slab), and conv 2 the
+    owned rows: no exchange between the convs, and each conv is one launch.
 
     Every rank builds the same global inputs (the generator is seeded alike), so the owned rows
     can be checked against the single-GPU step (:meth:`check_against_single_gpu`)."""
 
     launches_per_step = 0                 # set in __init__
+
+    halo_planes = 2
 
     def __init__(self, coords_np: np.ndarray, ci: int, device, generator, uid: bytes):
         from . import ops
@@ -182,7 +193,7 @@ class SlabRunner:
         self.n_total = coords_np.shape[0]
         # the same global features on every rank (same seed); the rank's slab takes its rows
         self.feats_global = torch.randn((self.n_total, ci), device=device, generator=generator).bfloat16()
-        self.dist = ops.Dist(device, self.rank, self.world, uid)
+        self.dist = ops.Dist(device, self.rank, self.world, uid, halo_planes=self.halo_planes)
         self.slab = self.dist.partition(self.coords_global)
         self.rows = self.dist.local_rows().long()
         self.n_local = int(self.slab.n_local)
@@ -191,15 +202,25 @@ class SlabRunner:
         self.feats = self.feats_global[self.rows].contiguous()
         self.h = torch.zeros((self.n_local, ci), dtype=torch.bfloat16, device=device)
         self.out = torch.zeros((self.n_local, ci), dtype=torch.bfloat16, device=device)
-        # our kernels per step: the map, and per conv the tap permutation plus up to three ranges
-        # (interior planes, the two edge planes)
-        self.launches_per_step = ops.NBR_MAP_LAUNCHES + 2 * 4
+        # our kernels per step: the map and one launch per conv (NCCL's kernel is not counted)
+        self.launches_per_step = ops.NBR_MAP_LAUNCHES + 2
         self.graph = None
+        self._wl = {}
+
+    def local_weight(self, w):
+        """w with its taps in the slab map's order, made once per weight tensor (as a model
+        would at load time)."""
+        key = (w.data_ptr(), tuple(w.shape), w.dtype)
+        if key not in self._wl:
+            self._wl[key] = self.dist.local_weight(w)
+        return self._wl[key]
 
     def step(self, w1, w2):
+        w1l, w2l = self.local_weight(w1), self.local_weight(w2)
+        self.dist.exchange(self.feats)          # overlaps the map build
         self.dist.build_map()
-        self.dist.submconv(self.feats, w1, None, epi="silu", out=self.h)
-        self.dist.submconv(self.h, w2, None, out=self.out)
+        self.dist.submconv_grow(1, self.feats, w1l, None, epi="silu", out=self.h)
+        self.dist.submconv_grow(0, self.h, w2l, None, out=self.out)
 
     def capture(self, w1, w2, warmup: int = 3) -> None:
         """Record one step (map, both convs and their NCCL halo exchanges) into a CUDA graph.

@@ -30,10 +30,11 @@ _DT = {torch.float32: _lib.TB_F32, torch.float16: _lib.TB_F16, torch.bfloat16: _
 _EPI = {"none": _lib.TB_EPI_NONE, None: _lib.TB_EPI_NONE, "silu": _lib.TB_EPI_SILU}
 _ctxs: dict = {}
 
-# Kernels one tb_build_neighbor_map call launches: the block layout's insert, bucket clear,
-# voxel insert and lookup plus its table clear, and the voxel hash's clear, insert and lookup,
-# which return at once unless the block layout did not apply.
-NBR_MAP_LAUNCHES = 8
+# Kernels one tb_build_neighbor_map call launches: the sorted layout's check, column clear, fill
+# and lookup; the block layout's table clear, insert, bucket clear, voxel insert and lookup; and
+# the voxel hash's clear, insert and lookup. Each layout's kernels return at once when an earlier
+# layout applied.
+NBR_MAP_LAUNCHES = 12
 
 
 def _ptr(t) -> ctypes.c_void_p:
@@ -505,7 +506,7 @@ class Dist:
     exchanged and the caller fills the halo rows (one process driving several slabs). Calls
     enqueue on torch's current stream of ``device``."""
 
-    def __init__(self, device, rank: int, world: int, uid: bytes | None = None):
+    def __init__(self, device, rank: int, world: int, uid: bytes | None = None, halo_planes: int = 1):
         self.device = torch.device(device)
         self.rank, self.world = rank, world
         lib = _lib.load()
@@ -520,6 +521,8 @@ class Dist:
         ctx = context(self.device)
         check(lib.tb_dist_create(ctx, self.comm, rank, world, ctypes.byref(self.h)), "tb_dist_create", ctx)
         self.slab = None
+        self.halo_planes = halo_planes
+        self._check(lib.tb_dist_set_halo_planes(self.h, halo_planes), "tb_dist_set_halo_planes")
 
     def _check(self, st, call):
         if st != _lib.TB_OK:
@@ -573,6 +576,42 @@ class Dist:
         self._check(_lib.load().tb_dist_submconv(self.h, _ptr(feats), ci, _ptr(weight), _ptr(bias), co,
                                                  _DT[feats.dtype], _DT[od], _EPI[epi], _ptr(out)),
                     "tb_dist_submconv")
+        return out
+
+    def exchange(self, feats: torch.Tensor) -> None:
+        """Start the halo exchange of ``feats`` ([n_local, C]); the next conv waits for it."""
+        _need_cuda(feats)
+        if feats.shape[0] != self.slab.n_local or not feats.is_contiguous():
+            raise ValueError("feats must be a contiguous [n_local, C] tensor")
+        context(self.device)
+        self._check(_lib.load().tb_dist_exchange(self.h, _ptr(feats), feats[0].numel() * feats.element_size()),
+                    "tb_dist_exchange")
+
+    def local_weight(self, weight: torch.Tensor) -> torch.Tensor:
+        """The weight [Co,27,Ci] with its taps in the local map's order (for submconv_grow)."""
+        _need_cuda(weight)
+        co, _, ci = weight.shape
+        out = torch.empty_like(weight)
+        context(self.device)
+        self._check(_lib.load().tb_dist_local_weight(self.h, _ptr(weight), ci, co, _DT[weight.dtype], _ptr(out)),
+                    "tb_dist_local_weight")
+        return out
+
+    def submconv_grow(self, grow: int, feats: torch.Tensor, weight_local: torch.Tensor, bias=None,
+                      epi: str = "none", out_dtype=None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """A conv without exchange on the owned rows and the ``grow`` nearest halo planes per side."""
+        _need_cuda(feats, weight_local, bias)
+        n, ci = feats.shape
+        co = weight_local.shape[0]
+        if n != self.slab.n_local or weight_local.dtype != feats.dtype or weight_local.numel() != co * 27 * ci:
+            raise ValueError("feats must be [n_local, Ci] and weight_local [Co,27,Ci] of its dtype")
+        od = feats.dtype if out_dtype is None else out_dtype
+        if out is None:
+            out = torch.empty((n, co), dtype=od, device=feats.device)
+        context(self.device)
+        self._check(_lib.load().tb_dist_submconv_grow(self.h, grow, _ptr(feats), ci, _ptr(weight_local), _ptr(bias),
+                                                      co, _DT[feats.dtype], _DT[od], _EPI[epi], _ptr(out)),
+                    "tb_dist_submconv_grow")
         return out
 
     def count_valid_pairs(self) -> int:
