@@ -156,10 +156,10 @@ def test_builds_in_a_row_are_independent(tb):
         assert np.array_equal(_gpu_map(c), oracle.build_neighbor_table(c))
 
 
-# Rows in ascending (batch, x, y, z) order build the map from a table of (batch, x, y) columns
-# (the sorted layout); rows in any other order, coordinates outside [0, 2^20 - 2] or a bounding
-# box with more columns than the table holds go to the block layout. These cases sit on either
-# side of each condition and must all give the reference's map.
+# Rows in strictly ascending (batch, x, y, z) order build the map from a table of (batch, x, y)
+# columns (the sorted layout); rows in any other order, repeated coordinates, coordinates outside
+# [0, 2^20 - 2] or a bounding box with more columns than the table holds go to the block layout.
+# These cases sit on either side of each condition and must all give the reference's map.
 def _sorted(c):
     c = np.asarray(c, np.int64)
     k = (c[:, 0] << 60) | (c[:, 1] << 40) | (c[:, 2] << 20) | c[:, 3] if c.shape[1] == 4 else \
@@ -173,6 +173,7 @@ def _sorted_cases():
     dup_col[:1500] = [1, 4, 4, 5]                        # one voxel 1500 times: the binary-search path
     long_cols = np.concatenate([np.zeros((6000, 1), np.int64), rng.integers(0, 2, (6000, 2)),
                                 rng.integers(0, 4000, (6000, 1))], 1)       # 4 columns of ~1500 rows
+    long_cols = np.unique(long_cols, axis=0)                                  # distinct: the sorted layout
     top = (1 << 20) - 2
     edges = np.array([[0, 0, 0, 0], [0, 0, 0, 1], [0, 0, 1, 0], [0, 1, 0, 0], [0, top, top, top],
                       [0, top - 1, top, top], [0, top, top - 1, top], [0, top, top, top - 1],

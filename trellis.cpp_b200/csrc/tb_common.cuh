@@ -88,8 +88,6 @@ __device__ __forceinline__ float tb_silu(float v) { return __fdividef(v, 1.0f + 
 inline bool tb_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Launch helpers implemented in the individual .cu files (all enqueue on ctx->stream).
-tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride,
-                            int32_t* nbr, void* table, uint64_t cap, const int* gate);
 tb_status tb_nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws);
 size_t tb_nbr_workspace_bytes(int64_t n);
 // The seven neighbor offsets in {0,1}^3 other than (1,1,1), the corners of the dual-grid quads,

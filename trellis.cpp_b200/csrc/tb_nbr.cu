@@ -53,9 +53,9 @@ __device__ __forceinline__ uint64_t key_of(const int32_t* c, int stride, int dx,
     return tb_key3(c[0] + dx, c[1] + dy, c[2] + dz);
 }
 
-__global__ void k_hash_clear(Slot* __restrict__ t, uint64_t cap, int* __restrict__ special,
-                             const int* __restrict__ gate) {
-    if (gate && *gate == 0) return;
+// Grid-stride bodies of the voxel hash's three steps; kernels of their own for the
+// allocation-free entry point, and the fallback branch of the layout kernels below.
+__device__ __forceinline__ void hash_clear_body(Slot* __restrict__ t, uint64_t cap, int* __restrict__ special) {
     uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (; i < cap; i += stride) {
@@ -65,12 +65,13 @@ __global__ void k_hash_clear(Slot* __restrict__ t, uint64_t cap, int* __restrict
     if (blockIdx.x == 0 && threadIdx.x == 0) *special = -1;
 }
 
-// `gate` (may be null): when it points at 0 the block layout built the map and these kernels
-// return at once.
-__global__ void k_hash_insert(const int32_t* __restrict__ coords, int64_t n, int stride,
-                              Slot* __restrict__ t, uint64_t mask, int* __restrict__ special,
-                              int* __restrict__ err, const int* __restrict__ gate) {
-    if (gate && *gate == 0) return;
+__global__ void k_hash_clear(Slot* __restrict__ t, uint64_t cap, int* __restrict__ special) {
+    hash_clear_body(t, cap, special);
+}
+
+__device__ __forceinline__ void hash_insert_body(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                 Slot* __restrict__ t, uint64_t mask, int* __restrict__ special,
+                                                 int* __restrict__ err) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const uint64_t k = key_of(coords + i * stride, stride, 0, 0, 0);
         if (k == kEmpty) { atomicMax(special, (int)i); continue; }
@@ -83,6 +84,11 @@ __global__ void k_hash_insert(const int32_t* __restrict__ coords, int64_t n, int
         }
         if (!done && err) atomicCAS(err, 0, TB_DEVERR_HASH_PROBE);
     }
+}
+
+__global__ void k_hash_insert(const int32_t* __restrict__ coords, int64_t n, int stride, Slot* __restrict__ t,
+                              uint64_t mask, int* __restrict__ special, int* __restrict__ err) {
+    hash_insert_body(coords, n, stride, t, mask, special, err);
 }
 
 __device__ __forceinline__ int lookup(const Slot* __restrict__ t, uint64_t mask, int special,
@@ -110,11 +116,10 @@ __device__ __forceinline__ constexpr int tap_at(int j) {
 }
 
 template <int NT>
-__global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int stride,
-                             const Slot* __restrict__ t, uint64_t mask,
-                             const int* __restrict__ special_p, int32_t* __restrict__ nbr,
-                             int* __restrict__ err, const int* __restrict__ gate) {
-    if (gate && *gate == 0) return;
+__device__ __forceinline__ void nbr_lookup_body(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                const Slot* __restrict__ t, uint64_t mask,
+                                                const int* __restrict__ special_p, int32_t* __restrict__ nbr,
+                                                int* __restrict__ err) {
     const int special = *special_p;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         int32_t c[4];
@@ -127,6 +132,13 @@ __global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int 
             nbr[(int64_t)j * n + i] = lookup(t, mask, special, k, (int)n, err);
         }
     }
+}
+
+template <int NT>
+__global__ void k_nbr_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t,
+                             uint64_t mask, const int* __restrict__ special_p, int32_t* __restrict__ nbr,
+                             int* __restrict__ err) {
+    nbr_lookup_body<NT>(coords, n, stride, t, mask, special_p, nbr, err);
 }
 
 // ---- block layout ---------------------------------------------------------------------------
@@ -183,15 +195,27 @@ __device__ __forceinline__ void read_coords(const int32_t* c, int stride, int32_
 }
 
 constexpr int kInsPer = 4;      // voxels per thread in the insert kernels
+constexpr int kTpb = 256;       // threads per block of every map kernel
+
+// Coordinates of row i: one 16-byte load when the rows are [b, x, y, z] and 16-byte aligned.
+__device__ __forceinline__ void load_row(const int32_t* __restrict__ coords, int64_t i, int stride, bool vec,
+                                         int32_t& b, int32_t& x, int32_t& y, int32_t& z) {
+    if (vec) {
+        const int4 v = __ldg(reinterpret_cast<const int4*>(coords) + i);
+        b = v.x; x = v.y; y = v.z; z = v.w;
+    } else {
+        read_coords(coords + i * stride, stride, b, x, y, z);
+    }
+}
 
 // Claims each voxel's block and hands the block a bucket; flags coordinates outside the range
 // where block lookup equals the reference's key lookup, and bucket overflow. A warp takes
 // 32 * kInsPer consecutive voxels (group j = voxels j*32 .. j*32+31 of its range) and issues the
-// first claim attempt of every group before it waits on any: the kernel is bound by the latency
+// first claim attempt of every group before it waits on any: the work is bound by the latency
 // of these dependent round trips, not by bandwidth.
-__global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int stride, Slot* __restrict__ t,
-                             uint64_t mask, BlockCtl* __restrict__ ctl, unsigned int pool_blocks) {
-    if (ctl->sorted) return;
+__device__ __forceinline__ void blk_insert_body(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                Slot* __restrict__ t, uint64_t mask, BlockCtl* __restrict__ ctl,
+                                                unsigned int pool_blocks) {
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * kInsPer;
     uint64_t k[kInsPer], h[kInsPer];
@@ -261,113 +285,103 @@ __global__ void k_blk_insert(const int32_t* __restrict__ coords, int64_t n, int 
     }
 }
 
-__global__ void k_pool_clear(int32_t* __restrict__ pool, const BlockCtl* __restrict__ ctl) {
-    if (ctl->fallback || ctl->sorted) return;
-    const uint64_t total = (uint64_t)ctl->nblocks * 16;            // int4 words
-    uint64_t j = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (; j < total; j += stride) reinterpret_cast<int4*>(pool)[j] = make_int4(-1, -1, -1, -1);
-}
-
 // The largest row index of each coordinate wins, as the reference's later insert overwrites.
-// Four voxels per thread (blockDim apart, so each load of a warp is coalesced); their first
-// table probes are in flight together.
-__global__ void k_vox_insert(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t,
-                             uint64_t mask, const BlockCtl* __restrict__ ctl, int32_t* __restrict__ pool) {
-    if (ctl->fallback || ctl->sorted) return;
-    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x * kInsPer + threadIdx.x;
-    uint64_t k[kInsPer], h[kInsPer];
-    int loc[kInsPer];
-    ulonglong2 s[kInsPer];
+// Grid-stride over chunks of kTpb * kInsPer voxels: four voxels per thread (kTpb apart, so each
+// load of a warp is coalesced) whose first table probes are in flight together.
+__device__ __forceinline__ void vox_insert_body(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                const Slot* __restrict__ t, uint64_t mask, int32_t* __restrict__ pool) {
+    const int64_t nchunks = (n + (int64_t)kTpb * kInsPer - 1) / ((int64_t)kTpb * kInsPer);
+    for (int64_t ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
+        const int64_t i0 = ch * kTpb * kInsPer + threadIdx.x;
+        uint64_t k[kInsPer], h[kInsPer];
+        int loc[kInsPer];
+        ulonglong2 s[kInsPer];
 #pragma unroll
-    for (int j = 0; j < kInsPer; ++j) {
-        const int64_t i = i0 + (int64_t)j * blockDim.x;
-        if (i < n) {
-            int32_t b, x, y, z;
-            read_coords(coords + i * stride, stride, b, x, y, z);
-            k[j] = block_key(b, x >> 2, y >> 2, z >> 2);
-            h[j] = block_slot(b, x >> 2, y >> 2, z >> 2, mask);
-            loc[j] = ((x & 3) << 4) | ((y & 3) << 2) | (z & 3);
-            s[j] = slot_at(t, h[j]);
+        for (int j = 0; j < kInsPer; ++j) {
+            const int64_t i = i0 + (int64_t)j * kTpb;
+            if (i < n) {
+                int32_t b, x, y, z;
+                read_coords(coords + i * stride, stride, b, x, y, z);
+                k[j] = block_key(b, x >> 2, y >> 2, z >> 2);
+                h[j] = block_slot(b, x >> 2, y >> 2, z >> 2, mask);
+                loc[j] = ((x & 3) << 4) | ((y & 3) << 2) | (z & 3);
+                s[j] = slot_at(t, h[j]);
+            }
         }
-    }
 #pragma unroll
-    for (int j = 0; j < kInsPer; ++j) {
-        const int64_t i = i0 + (int64_t)j * blockDim.x;
-        if (i >= n) break;
-        const int bucket = block_resolve(t, mask, k[j], h[j], s[j]);
-        if (bucket < 0) continue;                                    // cannot happen after k_blk_insert
-        atomicMax(&pool[(int64_t)bucket * 64 + loc[j]], (int32_t)i);
+        for (int j = 0; j < kInsPer; ++j) {
+            const int64_t i = i0 + (int64_t)j * kTpb;
+            if (i >= n) break;
+            const int bucket = block_resolve(t, mask, k[j], h[j], s[j]);
+            if (bucket < 0) continue;                                    // cannot happen after the block claims
+            atomicMax(&pool[(int64_t)bucket * 64 + loc[j]], (int32_t)i);
+        }
     }
 }
 
-constexpr int kLookupThreads = 256;    // block size of k_blk_lookup (its shared-memory table)
-
-// 27 lookups per voxel. Per axis the taps reach at most one block besides the voxel's own (the
-// one below at position 0, above at position 3), so the up to 8 blocks are looked up once. Their
-// bucket bases go to shared memory (a column per thread, so reads never conflict), and each tap
-// reads the one its three "leaves the block" bits select instead of a select tree over eight
-// registers.
+// 27 lookups per voxel (grid-stride). Per axis the taps reach at most one block besides the
+// voxel's own (the one below at position 0, above at position 3), so the up to 8 blocks are
+// looked up once. Their bucket bases go to shared memory (a column per thread, so reads never
+// conflict), and each tap reads the one its three "leaves the block" bits select instead of a
+// select tree over eight registers.
 template <int NT>
-__global__ void __launch_bounds__(kLookupThreads)
-k_blk_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const Slot* __restrict__ t, uint64_t mask,
-             const BlockCtl* __restrict__ ctl, const int32_t* __restrict__ pool, int32_t* __restrict__ nbr) {
-    __shared__ int s_base[8][kLookupThreads];
-    if (ctl->fallback || ctl->sorted) return;
-    const int64_t i = blockIdx.x * (int64_t)kLookupThreads + threadIdx.x;
-    if (i >= n) return;
-    int32_t b, x, y, z;
-    read_coords(coords + i * stride, stride, b, x, y, z);
-    const int32_t bx = x >> 2, by = y >> 2, bz = z >> 2;
-    const int lx = x & 3, ly = y & 3, lz = z & 3;
-    const int ox = lx == 0 ? -1 : (lx == 3 ? 1 : 0);
-    const int oy = ly == 0 ? -1 : (ly == 3 ? 1 : 0);
-    const int oz = lz == 0 ? -1 : (lz == 3 ? 1 : 0);
-    // s_base[m] = bucket base (bucket * 64) of block own + (ax ? ox : 0, ay ? oy : 0, az ? oz : 0), or -1
+__device__ __forceinline__ void blk_lookup_body(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                const Slot* __restrict__ t, uint64_t mask,
+                                                const int32_t* __restrict__ pool, int32_t* __restrict__ nbr,
+                                                int (*s_base)[kTpb]) {
+    for (int64_t i = blockIdx.x * (int64_t)kTpb + threadIdx.x; i < n; i += (int64_t)gridDim.x * kTpb) {
+        int32_t b, x, y, z;
+        read_coords(coords + i * stride, stride, b, x, y, z);
+        const int32_t bx = x >> 2, by = y >> 2, bz = z >> 2;
+        const int lx = x & 3, ly = y & 3, lz = z & 3;
+        const int ox = lx == 0 ? -1 : (lx == 3 ? 1 : 0);
+        const int oy = ly == 0 ? -1 : (ly == 3 ? 1 : 0);
+        const int oz = lz == 0 ? -1 : (lz == 3 ? 1 : 0);
+        // s_base[m] = bucket base (bucket * 64) of block own + (ax ? ox : 0, ay ? oy : 0, az ? oz : 0), or -1
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
-        const int ax = (m >> 2) & 1, ay = (m >> 1) & 1, az = m & 1;
-        const bool need = (!ax || ox) && (!ay || oy) && (!az || oz);
-        const int32_t cx = bx + (ax ? ox : 0), cy = by + (ay ? oy : 0), cz = bz + (az ? oz : 0);
-        int bucket = -1;
-        if (need && cx >= 0 && cy >= 0 && cz >= 0) {
-            const uint64_t h = block_slot(b, cx, cy, cz, mask);
-            bucket = block_resolve(t, mask, block_key(b, cx, cy, cz), h, slot_at(t, h));
+        for (int m = 0; m < 8; ++m) {
+            const int ax = (m >> 2) & 1, ay = (m >> 1) & 1, az = m & 1;
+            const bool need = (!ax || ox) && (!ay || oy) && (!az || oz);
+            const int32_t cx = bx + (ax ? ox : 0), cy = by + (ay ? oy : 0), cz = bz + (az ? oz : 0);
+            int bucket = -1;
+            if (need && cx >= 0 && cy >= 0 && cz >= 0) {
+                const uint64_t h = block_slot(b, cx, cy, cz, mask);
+                bucket = block_resolve(t, mask, block_key(b, cx, cy, cz), h, slot_at(t, h));
+            }
+            s_base[m][threadIdx.x] = bucket >= 0 ? bucket * 64 : -1;
         }
-        s_base[m][threadIdx.x] = bucket >= 0 ? bucket * 64 : -1;
-    }
-    // per axis and offset d in {-1, 0, +1}: the block-select bit (x + d leaves the block) and the
-    // position in the block, pre-shifted into the bucket index
-    const int mx[3] = {lx == 0 ? 4 : 0, 0, lx == 3 ? 4 : 0};
-    const int my[3] = {ly == 0 ? 2 : 0, 0, ly == 3 ? 2 : 0};
-    const int mz[3] = {lz == 0 ? 1 : 0, 0, lz == 3 ? 1 : 0};
-    const int px[3] = {((lx - 1) & 3) << 4, lx << 4, ((lx + 1) & 3) << 4};
-    const int py[3] = {((ly - 1) & 3) << 2, ly << 2, ((ly + 1) & 3) << 2};
-    const int pz[3] = {(lz - 1) & 3, lz, (lz + 1) & 3};
+        // per axis and offset d in {-1, 0, +1}: the block-select bit (x + d leaves the block) and the
+        // position in the block, pre-shifted into the bucket index
+        const int mx[3] = {lx == 0 ? 4 : 0, 0, lx == 3 ? 4 : 0};
+        const int my[3] = {ly == 0 ? 2 : 0, 0, ly == 3 ? 2 : 0};
+        const int mz[3] = {lz == 0 ? 1 : 0, 0, lz == 3 ? 1 : 0};
+        const int px[3] = {((lx - 1) & 3) << 4, lx << 4, ((lx + 1) & 3) << 4};
+        const int py[3] = {((ly - 1) & 3) << 2, ly << 2, ((ly + 1) & 3) << 2};
+        const int pz[3] = {(lz - 1) & 3, lz, (lz + 1) & 3};
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-        const int tap = tap_at<NT>(j);
-        const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
-        const int bb = s_base[mx[kd] | my[kh] | mz[kw]][threadIdx.x];
-        int32_t r = -1;
-        if (bb >= 0) r = __ldg(pool + bb + (px[kd] | py[kh] | pz[kw]));
-        nbr[(int64_t)j * n + i] = r >= 0 ? r : (int32_t)n;
+        for (int j = 0; j < NT; ++j) {
+            const int tap = tap_at<NT>(j);
+            const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+            const int bb = s_base[mx[kd] | my[kh] | mz[kw]][threadIdx.x];
+            int32_t r = -1;
+            if (bb >= 0) r = __ldg(pool + bb + (px[kd] | py[kh] | pz[kw]));
+            nbr[(int64_t)j * n + i] = r >= 0 ? r : (int32_t)n;
+        }
     }
 }
 
 // ---- sorted layout ---------------------------------------------------------------------------
-// When the rows are in ascending (batch, x, y, z) order (equal coordinates adjacent), every
+// When the rows are in strictly ascending (batch, x, y, z) order (no repeated coordinate), every
 // (batch, x, y) column of voxels is a contiguous run of rows with z ascending. A dense table over
 // the columns of the bounding box holds each column's row range, built with plain stores from
 // the column boundaries of the row order (no hashing, no atomics), and a lookup finds z - 1, z
-// and z + 1 in the 9 columns (x + dx, y + dy) by a binary search and a short scan. It applies
-// when the block layout's coordinate range holds (so no two coordinates share a key and out-of-
-// grid neighbours are absent), the rows are in that order, and the box has at most col_cap
-// columns; the rows' z values are copied to a compact array so that a column's scan reads one
-// or two sectors. All three conditions are decided on the device; when one fails, the block
-// layout builds the map as before.
+// and z + 1 in the 9 columns (x + dx, y + dy). It applies when the block layout's coordinate
+// range holds (so no two coordinates share a key and out-of-grid neighbours are absent), the rows
+// are in that order, and the box has at most col_cap columns; the rows' z values are copied to a
+// compact array so that a column's rows sit in one or two sectors. All three conditions are
+// decided on the device; when one fails, the block layout builds the map.
 
-constexpr int kSrtScan = 8;   // rows a column scan walks before it resolves the rest by binary search
+constexpr int kSrtPer = 4;      // rows per thread per grid-stride step of the check
 
 __device__ __forceinline__ uint64_t srt_key(int32_t b, int32_t x, int32_t y, int32_t z) {
     return ((uint64_t)(uint32_t)b << 60) | ((uint64_t)(uint32_t)x << 40) | ((uint64_t)(uint32_t)y << 20) |
@@ -391,8 +405,9 @@ __device__ __forceinline__ SrtBox srt_box(const BlockCtl* ctl) {
     return bx;
 }
 
-__device__ __forceinline__ int64_t srt_col(const SrtBox& bx, int32_t b, int32_t x, int32_t y) {
-    return ((int64_t)(b - bx.b0) * bx.nx + (x - bx.x0)) * bx.ny + (y - bx.y0);
+// Column index of (b, x, y) inside the box; below col_cap < 2^31 wherever the layout applies.
+__device__ __forceinline__ int srt_col(const SrtBox& bx, int32_t b, int32_t x, int32_t y) {
+    return ((b - bx.b0) * (int)bx.nx + (x - bx.x0)) * (int)bx.ny + (y - bx.y0);
 }
 
 __device__ __forceinline__ int warp_min(int v) {
@@ -406,29 +421,45 @@ __device__ __forceinline__ int warp_max(int v) {
     return v;
 }
 
-// Range and order check, the (batch, x, y) bounding box and the compact z array. Grid-stride
-// with one set of atomics per block.
-__global__ void __launch_bounds__(256) k_srt_check(const int32_t* __restrict__ coords, int64_t n, int stride,
-                                                   BlockCtl* __restrict__ ctl, int32_t* __restrict__ zc) {
-    __shared__ int s_red[8][7];
+// First kernel of a build: range and order check, the (batch, x, y) bounding box and the compact
+// z array. Grid-stride over steps of kSrtPer rows per thread (kTpb apart, coalesced, loaded
+// together; row i - 1 from the neighbouring lane); a small grid, since each block ends with one
+// set of atomics on the same few words.
+__global__ void __launch_bounds__(kTpb) k_srt_check(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                    bool vec, BlockCtl* __restrict__ ctl, int32_t* __restrict__ zc) {
+    __shared__ int s_red[kTpb / 32][7];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int bad = 0;
     int lo[3] = {INT_MAX, INT_MAX, INT_MAX}, hi[3] = {INT_MIN, INT_MIN, INT_MIN};
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        int32_t b, x, y, z;
-        read_coords(coords + i * stride, stride, b, x, y, z);
-        if ((uint32_t)x > (uint32_t)kMaxCoord || (uint32_t)y > (uint32_t)kMaxCoord ||
-            (uint32_t)z > (uint32_t)kMaxCoord || (uint32_t)b > 15u)
-            bad = 1;
-        zc[i] = z;
-        if (i > 0) {
-            int32_t pb, px, py, pz;
-            read_coords(coords + (i - 1) * stride, stride, pb, px, py, pz);
-            if (srt_key(pb, px, py, pz) > srt_key(b, x, y, z)) bad = 1;
+    const int64_t step = (int64_t)gridDim.x * kTpb * kSrtPer;
+    for (int64_t base = (int64_t)blockIdx.x * kTpb * kSrtPer; base < n; base += step) {
+        int32_t b[kSrtPer], x[kSrtPer], y[kSrtPer], z[kSrtPer];
+#pragma unroll
+        for (int j = 0; j < kSrtPer; ++j) {
+            const int64_t i = base + (int64_t)j * kTpb + threadIdx.x;
+            b[j] = x[j] = y[j] = z[j] = 0;
+            if (i < n) load_row(coords, i, stride, vec, b[j], x[j], y[j], z[j]);
         }
-        lo[0] = min(lo[0], b); lo[1] = min(lo[1], x); lo[2] = min(lo[2], y);
-        hi[0] = max(hi[0], b); hi[1] = max(hi[1], x); hi[2] = max(hi[2], y);
+#pragma unroll
+        for (int j = 0; j < kSrtPer; ++j) {
+            const int64_t i = base + (int64_t)j * kTpb + threadIdx.x;
+            const uint64_t key = srt_key(b[j], x[j], y[j], z[j]);
+            uint64_t prev = __shfl_up_sync(0xffffffffu, key, 1);
+            if (i >= n) continue;
+            if ((uint32_t)x[j] > (uint32_t)kMaxCoord || (uint32_t)y[j] > (uint32_t)kMaxCoord ||
+                (uint32_t)z[j] > (uint32_t)kMaxCoord || (uint32_t)b[j] > 15u)
+                bad = 1;
+            zc[i] = z[j];
+            if (lane == 0 && i > 0) {
+                int32_t pb, px, py, pz;
+                load_row(coords, i - 1, stride, vec, pb, px, py, pz);
+                prev = srt_key(pb, px, py, pz);
+            }
+            if (i > 0 && prev >= key) bad = 1;       // out of order, or a repeated coordinate
+            lo[0] = min(lo[0], b[j]); lo[1] = min(lo[1], x[j]); lo[2] = min(lo[2], y[j]);
+            hi[0] = max(hi[0], b[j]); hi[1] = max(hi[1], x[j]); hi[2] = max(hi[2], y[j]);
+        }
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     bad = __any_sync(0xffffffffu, bad);
 #pragma unroll
     for (int k = 0; k < 3; ++k) { lo[k] = warp_min(lo[k]); hi[k] = warp_max(hi[k]); }
@@ -439,7 +470,7 @@ __global__ void __launch_bounds__(256) k_srt_check(const int32_t* __restrict__ c
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+        for (int w = 1; w < kTpb / 32; ++w) {
             bad |= s_red[w][0];
 #pragma unroll
             for (int k = 0; k < 3; ++k) { lo[k] = min(lo[k], s_red[w][1 + k]); hi[k] = max(hi[k], s_red[w][4 + k]); }
@@ -455,79 +486,27 @@ __global__ void __launch_bounds__(256) k_srt_check(const int32_t* __restrict__ c
     }
 }
 
-// Decides the layout, then clears the column table of the bounding box.
-__global__ void k_srt_clear(BlockCtl* __restrict__ ctl, int2* __restrict__ cols, uint64_t col_cap) {
-    const SrtBox bx = srt_box(ctl);
-    const int64_t nb = (int64_t)ctl->hi[0] - bx.b0 + 1;
-    const bool applies = !ctl->unsorted && nb > 0 && bx.nx > 0 && bx.ny > 0 &&
-                         (uint64_t)nb * (uint64_t)bx.nx * (uint64_t)bx.ny <= col_cap;
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        ctl->sorted = applies ? 1 : 0;
-        ctl->block_on = applies ? 0 : 1;
-    }
-    if (!applies) return;
-    const uint64_t cells = (uint64_t)nb * (uint64_t)bx.nx * (uint64_t)bx.ny;
-    for (uint64_t c = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; c < cells; c += (uint64_t)gridDim.x * blockDim.x)
-        cols[c] = make_int2(0, 0);
-}
-
-// cols[column] = {first row, last row + 1} from the column boundaries of the row order.
-__global__ void k_srt_fill(const int32_t* __restrict__ coords, int64_t n, int stride,
-                           const BlockCtl* __restrict__ ctl, int2* __restrict__ cols) {
-    if (!ctl->sorted) return;
+// cols[column] = {first row, last row + 1} from the column boundaries of the row order
+// (grid-stride, one row at a time, its neighbours' coordinates read again).
+__device__ __forceinline__ void srt_fill_body(const int32_t* __restrict__ coords, int64_t n, int stride, bool vec,
+                                              const BlockCtl* __restrict__ ctl, int2* __restrict__ cols) {
     const SrtBox bx = srt_box(ctl);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         int32_t b, x, y, z;
-        read_coords(coords + i * stride, stride, b, x, y, z);
-        const int64_t c = srt_col(bx, b, x, y);
+        load_row(coords, i, stride, vec, b, x, y, z);
+        const int c = srt_col(bx, b, x, y);
         bool first = i == 0, last = i == n - 1;
         if (!first) {
-            int32_t pb, px, py, pz;
-            read_coords(coords + (i - 1) * stride, stride, pb, px, py, pz);
-            first = srt_col(bx, pb, px, py) != c;
+            load_row(coords, i - 1, stride, vec, b, x, y, z);
+            first = srt_col(bx, b, x, y) != c;
         }
         if (!last) {
-            int32_t qb, qx, qy, qz;
-            read_coords(coords + (i + 1) * stride, stride, qb, qx, qy, qz);
-            last = srt_col(bx, qb, qx, qy) != c;
+            load_row(coords, i + 1, stride, vec, b, x, y, z);
+            last = srt_col(bx, b, x, y) != c;
         }
         if (first) cols[c].x = (int)i;
         if (last) cols[c].y = (int)(i + 1);
     }
-}
-
-// First k in [lo, hi) with zc[k] > v (hi when none).
-__device__ __forceinline__ int srt_upper(const int32_t* __restrict__ zc, int lo, int hi, int v) {
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (__ldg(zc + mid) <= v) lo = mid + 1; else hi = mid;
-    }
-    return lo;
-}
-
-// The last rows of z - 1, z and z + 1 (the reference's later duplicate wins) among the column
-// rows [s, e), whose z values ascend; -1 where absent.
-__device__ __forceinline__ void srt_col_find(const int32_t* __restrict__ zc, int s, int e, int z,
-                                             int& rm, int& r0, int& rp) {
-    rm = r0 = rp = -1;
-    int lo = s, hi = e;                       // first row with z' >= z - 1
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (__ldg(zc + mid) < z - 1) lo = mid + 1; else hi = mid;
-    }
-    int k = lo;
-    for (int step = 0; step < kSrtScan; ++step, ++k) {
-        if (k >= e) return;
-        const int d = __ldg(zc + k) - z;
-        if (d > 1) return;
-        if (d < 0) rm = k; else if (d == 0) r0 = k; else rp = k;
-    }
-    if (k >= e || __ldg(zc + k) > z + 1) return;
-    // more than kSrtScan rows hold z - 1 .. z + 1 (duplicates): the last of each by binary search
-    const int pm = srt_upper(zc, lo, e, z - 1), p0 = srt_upper(zc, pm, e, z), pp = srt_upper(zc, p0, e, z + 1);
-    rm = pm > lo && __ldg(zc + pm - 1) == z - 1 ? pm - 1 : -1;
-    r0 = p0 > pm && __ldg(zc + p0 - 1) == z ? p0 - 1 : -1;
-    rp = pp > p0 && __ldg(zc + pp - 1) == z + 1 ? pp - 1 : -1;
 }
 
 // Slot of a tap in the tap list (-1 when the list does not hold it).
@@ -538,34 +517,139 @@ __device__ __forceinline__ constexpr int slot_of_tap(int tap) {
     return -1;
 }
 
+// Column c = kd * 3 + kh (x + kd - 1, y + kh - 1) holds a tap of the list.
 template <int NT>
-__global__ void __launch_bounds__(256)
-k_srt_lookup(const int32_t* __restrict__ coords, int64_t n, int stride, const BlockCtl* __restrict__ ctl,
-             const int2* __restrict__ cols, const int32_t* __restrict__ zc, int32_t* __restrict__ nbr) {
-    if (!ctl->sorted) return;
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+__device__ __forceinline__ constexpr bool srt_col_needed(int c) {
+    return slot_of_tap<NT>(c * 3) >= 0 || slot_of_tap<NT>(c * 3 + 1) >= 0 || slot_of_tap<NT>(c * 3 + 2) >= 0;
+}
+
+// The rows of z - 1, z and z + 1 (-1 where absent) among the column rows [s, e), whose z values
+// strictly ascend: a binary search for the first row with z' >= z - 1, then at most three rows.
+__device__ __forceinline__ void srt_col_find(const int32_t* __restrict__ zc, int s, int e, int z, int& rm, int& r0,
+                                             int& rp) {
+    rm = r0 = rp = -1;
+    int lo = s, hi = e;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(zc + mid) < z - 1) lo = mid + 1; else hi = mid;
+    }
+    for (int k = lo; k < e && k < lo + 3; ++k) {
+        const int d = __ldg(zc + k) - z;
+        if (d > 1) return;
+        if (d < 0) rm = k; else if (d == 0) r0 = k; else rp = k;
+    }
+}
+
+// One row per thread: per neighbouring column (x + dx, y + dy) its row range from the table, then
+// srt_col_find; in the voxel's own column row i itself, and z -/+ 1 can only be rows i -/+ 1.
+template <int NT>
+__device__ __forceinline__ void srt_lookup_body(const int32_t* __restrict__ coords, int64_t n, int stride, bool vec,
+                                                const BlockCtl* __restrict__ ctl, const int2* __restrict__ cols,
+                                                const int32_t* __restrict__ zc, int32_t* __restrict__ nbr) {
+    const int64_t i = blockIdx.x * (int64_t)kTpb + threadIdx.x;
     if (i >= n) return;
     const SrtBox bx = srt_box(ctl);
     int32_t b, x, y, z;
-    read_coords(coords + i * stride, stride, b, x, y, z);
+    load_row(coords, i, stride, vec, b, x, y, z);
 #pragma unroll
-    for (int kd = 0; kd < 3; ++kd) {
-#pragma unroll
-        for (int kh = 0; kh < 3; ++kh) {
-            const int jm = slot_of_tap<NT>(kd * 9 + kh * 3), j0 = slot_of_tap<NT>(kd * 9 + kh * 3 + 1),
-                      jp = slot_of_tap<NT>(kd * 9 + kh * 3 + 2);
-            if (jm < 0 && j0 < 0 && jp < 0) continue;
-            const int32_t xx = x + kd - 1, yy = y + kh - 1;
-            int rm = -1, r0 = -1, rp = -1;
-            if (xx >= bx.x0 && xx <= bx.x1 && yy >= bx.y0 && yy <= bx.y1) {
-                const int2 se = __ldg(cols + srt_col(bx, b, xx, yy));
-                if (se.y > se.x) srt_col_find(zc, se.x, se.y, z, rm, r0, rp);
-            }
-            if (jm >= 0) nbr[(int64_t)jm * n + i] = rm >= 0 ? rm : (int32_t)n;
-            if (j0 >= 0) nbr[(int64_t)j0 * n + i] = r0 >= 0 ? r0 : (int32_t)n;
-            if (jp >= 0) nbr[(int64_t)jp * n + i] = rp >= 0 ? rp : (int32_t)n;
+    for (int c = 0; c < 9; ++c) {
+        if (!srt_col_needed<NT>(c)) continue;
+        const int32_t xx = x + c / 3 - 1, yy = y + c % 3 - 1;
+        int rm = -1, r0 = -1, rp = -1;
+        if (c == 4) {
+            const int2 se = __ldg(cols + srt_col(bx, b, x, y));
+            r0 = (int)i;
+            if (i > se.x && __ldg(zc + i - 1) == z - 1) rm = (int)i - 1;
+            if (i + 1 < se.y && __ldg(zc + i + 1) == z + 1) rp = (int)i + 1;
+        } else if (xx >= bx.x0 && xx <= bx.x1 && yy >= bx.y0 && yy <= bx.y1) {
+            const int2 se = __ldg(cols + srt_col(bx, b, xx, yy));
+            if (se.y > se.x) srt_col_find(zc, se.x, se.y, z, rm, r0, rp);
+        }
+        const int jm = slot_of_tap<NT>(c * 3), j0 = slot_of_tap<NT>(c * 3 + 1), jp = slot_of_tap<NT>(c * 3 + 2);
+        if (jm >= 0) nbr[(int64_t)jm * n + i] = rm >= 0 ? rm : (int32_t)n;
+        if (j0 >= 0) nbr[(int64_t)j0 * n + i] = r0 >= 0 ? r0 : (int32_t)n;
+        if (jp >= 0) nbr[(int64_t)jp * n + i] = rp >= 0 ? rp : (int32_t)n;
+    }
+}
+
+// ---- the build: six kernels, whichever layout applies ----------------------------------------
+// 1 k_srt_check (above). 2-6 below: each branches on the layout decided on the device, so the
+// layouts share launches and a build that takes the sorted layout ends with two that return at
+// once. The block and voxel-hash tables share memory (the block table is a prefix of the voxel
+// hash's), the sorted layout's column table takes the bucket pool's memory and its z array the
+// table's: only one layout writes them in a build.
+
+// 2: the layout, then the sorted layout's column table or the block layout's table cleared.
+__global__ void __launch_bounds__(kTpb) k_map_decide_clear(BlockCtl* __restrict__ ctl, int2* __restrict__ cols,
+                                                           uint64_t col_cap, Slot* __restrict__ t, uint64_t cap_b) {
+    const SrtBox bx = srt_box(ctl);
+    const int64_t nb = (int64_t)ctl->hi[0] - bx.b0 + 1;
+    const bool applies = !ctl->unsorted && nb > 0 && bx.nx > 0 && bx.ny > 0 &&
+                         (uint64_t)nb * (uint64_t)bx.nx * (uint64_t)bx.ny <= col_cap;
+    if (blockIdx.x == 0 && threadIdx.x == 0) ctl->sorted = applies ? 1 : 0;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    uint64_t c = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+    if (applies) {
+        const uint64_t cells = (uint64_t)nb * (uint64_t)bx.nx * (uint64_t)bx.ny;
+        for (; c < cells; c += stride) cols[c] = make_int2(0, 0);
+    } else {
+        for (; c < cap_b; c += stride) {
+            ulonglong2 v; v.x = kEmpty; v.y = 0xFFFFFFFFull;   // row = -1
+            reinterpret_cast<ulonglong2*>(t)[c] = v;
         }
     }
+}
+
+// 3: the sorted layout's column table, or the block layout's block claims.
+__global__ void k_map_fill_claim(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                         bool vec, BlockCtl* __restrict__ ctl, int2* __restrict__ cols,
+                                                         Slot* __restrict__ t, uint64_t mask_b,
+                                                         unsigned int pool_blocks) {
+    if (ctl->sorted) srt_fill_body(coords, n, stride, vec, ctl, cols);
+    else blk_insert_body(coords, n, stride, t, mask_b, ctl, pool_blocks);
+}
+
+// 4: the sorted layout's lookups; otherwise the block layout's bucket pool cleared, or the voxel
+// hash's table when the block layout did not apply either.
+template <int NT>
+__global__ void __launch_bounds__(kTpb) k_map_lookup_clear(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                           bool vec, const BlockCtl* __restrict__ ctl,
+                                                           const int2* __restrict__ cols, const int32_t* __restrict__ zc,
+                                                           int32_t* __restrict__ nbr, int32_t* __restrict__ pool,
+                                                           Slot* __restrict__ t, uint64_t cap, int* __restrict__ special) {
+    if (ctl->sorted) {
+        srt_lookup_body<NT>(coords, n, stride, vec, ctl, cols, zc, nbr);
+    } else if (ctl->fallback) {
+        hash_clear_body(t, cap, special);
+    } else {
+        const uint64_t total = (uint64_t)ctl->nblocks * 16;            // int4 words
+        const uint64_t stride_w = (uint64_t)gridDim.x * blockDim.x;
+        for (uint64_t j = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; j < total; j += stride_w)
+            reinterpret_cast<int4*>(pool)[j] = make_int4(-1, -1, -1, -1);
+    }
+}
+
+// 5: the block layout's voxel inserts, or the voxel hash's inserts (nothing for the sorted layout).
+__global__ void __launch_bounds__(kTpb) k_map_insert(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                     const BlockCtl* __restrict__ ctl, Slot* __restrict__ t,
+                                                     uint64_t mask_b, int32_t* __restrict__ pool, uint64_t cap,
+                                                     int* __restrict__ special, int* __restrict__ err) {
+    if (ctl->sorted) return;
+    if (ctl->fallback) hash_insert_body(coords, n, stride, t, cap - 1, special, err);
+    else vox_insert_body(coords, n, stride, t, mask_b, pool);
+}
+
+// 6: the block layout's lookups, or the voxel hash's (nothing for the sorted layout).
+template <int NT>
+__global__ void __launch_bounds__(kTpb) k_map_lookup(const int32_t* __restrict__ coords, int64_t n, int stride,
+                                                     const BlockCtl* __restrict__ ctl, const Slot* __restrict__ t,
+                                                     uint64_t mask_b, const int32_t* __restrict__ pool, uint64_t cap,
+                                                     const int* __restrict__ special, int32_t* __restrict__ nbr,
+                                                     int* __restrict__ err) {
+    __shared__ int s_base[8][kTpb];
+    if (ctl->sorted) return;
+    if (ctl->fallback) nbr_lookup_body<NT>(coords, n, stride, t, cap - 1, special, nbr, err);
+    else blk_lookup_body<NT>(coords, n, stride, t, mask_b, pool, nbr, s_base);
 }
 
 __global__ void k_count_valid(const int32_t* __restrict__ nbr, int64_t total, int32_t n,
@@ -632,43 +716,14 @@ uint64_t tb_hash_capacity(int64_t n) {
     return cap;
 }
 
-// `table` holds cap Slots followed by one int (the all-ones key cell); 16*cap + 16 bytes.
-// `gate` (may be null) skips the build when it points at 0.
-namespace {
-
-template <int NT>
-tb_status nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* table,
-                         uint64_t cap, const int* gate) {
-    Slot* t = reinterpret_cast<Slot*>(table);
-    int* special = reinterpret_cast<int*>(t + cap);
-    const uint64_t mask = cap - 1;
-    const int tpb = 256;
-    const int clear_blocks = (int)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
-    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap, special, gate);
-    TB_LAUNCH_CHECK(ctx, "k_hash_clear");
-    // grid-stride kernels: a gated launch that returns at once costs a small grid only
-    const int64_t blocks = std::min<int64_t>((n + tpb - 1) / tpb, (int64_t)ctx->num_sms * 16);
-    k_hash_insert<<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, ctx->d_err, gate);
-    TB_LAUNCH_CHECK(ctx, "k_hash_insert");
-    k_nbr_lookup<NT><<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, special, nbr, ctx->d_err,
-                                                                 gate);
-    TB_LAUNCH_CHECK(ctx, "k_nbr_lookup");
-    return TB_OK;
-}
-
-}  // namespace
-
-tb_status tb_nbr_build_impl(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride,
-                            int32_t* nbr, void* table, uint64_t cap, const int* gate) {
-    return nbr_build_impl<27>(ctx, coords, n, stride, nbr, table, cap, gate);
-}
-
 // Buckets for at most N/4 + 64 blocks, and fewer than 2^25 so a bucket's first entry index
 // (bucket * 64) fits an int; more blocks than that send the build to the voxel hash.
 static uint64_t tb_nbr_pool_blocks(int64_t n) {
     return std::min<uint64_t>((uint64_t)n / 4 + 64, (1ull << 25) - 64);
 }
 
+// The voxel-hash table (cap Slots, then one int: the all-ones key cell, padded to 16 bytes),
+// BlockCtl, and the block layout's bucket pool.
 size_t tb_nbr_workspace_bytes(int64_t n) {
     const uint64_t cap = tb_hash_capacity(n);
     return cap * sizeof(Slot) + 16 + sizeof(BlockCtl) + tb_nbr_pool_blocks(n) * 64 * sizeof(int32_t);
@@ -676,53 +731,44 @@ size_t tb_nbr_workspace_bytes(int64_t n) {
 
 namespace {
 
-// Sorted layout first, then the block layout, then the voxel hash: each later layout's kernels
-// return at once unless the earlier ones did not apply (BlockCtl::sorted, BlockCtl::fallback),
-// so exactly one writes the map.
 template <int NT>
 tb_status nbr_build_blocks(tb_ctx* ctx, const int32_t* coords, int64_t n, int stride, int32_t* nbr, void* ws) {
-    const uint64_t cap = tb_hash_capacity(n);                   // voxel-hash table (fallback)
+    const uint64_t cap = tb_hash_capacity(n);                   // voxel-hash table
     const uint64_t pool_blocks = tb_nbr_pool_blocks(n);
     const uint64_t cap_b = tb_hash_capacity((int64_t)pool_blocks);   // block table, a prefix of it
-    const uint64_t mask = cap_b - 1;
+    const uint64_t mask_b = cap_b - 1;
     Slot* t = reinterpret_cast<Slot*>(ws);
+    int* special = reinterpret_cast<int*>(t + cap);
     unsigned char* after = reinterpret_cast<unsigned char*>(t + cap) + 16;
     BlockCtl* ctl = reinterpret_cast<BlockCtl*>(after);
     int32_t* pool = reinterpret_cast<int32_t*>(after + sizeof(BlockCtl));
-    const int tpb = 256;
-    TB_CUDA_TRY(ctx, cudaMemsetAsync(ctl, 0, sizeof(BlockCtl), ctx->stream));
-    const int64_t blocks = (n + tpb - 1) / tpb;
-    // sorted layout: its column table takes the bucket pool's memory and the compact z array the
-    // voxel-hash table's; the block and voxel-hash layouts run only when it does not apply and
-    // then overwrite both
-    const int grid_stride_blocks = (int)std::min<int64_t>(blocks, (int64_t)ctx->num_sms * 8);
-    int2* cols = reinterpret_cast<int2*>(pool);
-    int32_t* zc = reinterpret_cast<int32_t*>(t);
+    int2* cols = reinterpret_cast<int2*>(pool);                 // sorted layout: column table
+    int32_t* zc = reinterpret_cast<int32_t*>(t);                // sorted layout: z of every row
     const uint64_t col_cap = pool_blocks * 64 * sizeof(int32_t) / sizeof(int2);
-    k_srt_check<<<grid_stride_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, ctl, zc);
+    const bool vec = stride == 4 && (reinterpret_cast<uintptr_t>(coords) & 15) == 0;
+    const int64_t sms = ctx->num_sms;
+    const int64_t blocks = (n + kTpb - 1) / kTpb;
+    const int64_t ins_blocks = (n + (int64_t)kTpb * kInsPer - 1) / ((int64_t)kTpb * kInsPer);
+    TB_CUDA_TRY(ctx, cudaMemsetAsync(ctl, 0, sizeof(BlockCtl), ctx->stream));
+    k_srt_check<<<(unsigned)std::min<int64_t>((n + kTpb * kSrtPer - 1) / (kTpb * kSrtPer), sms * 4), kTpb, 0,
+                  ctx->stream>>>(coords, n, stride, vec, ctl, zc);
     TB_LAUNCH_CHECK(ctx, "k_srt_check");
-    k_srt_clear<<<ctx->num_sms * 8, tpb, 0, ctx->stream>>>(ctl, cols, col_cap);
-    TB_LAUNCH_CHECK(ctx, "k_srt_clear");
-    k_srt_fill<<<grid_stride_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, ctl, cols);
-    TB_LAUNCH_CHECK(ctx, "k_srt_fill");
-    k_srt_lookup<NT><<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, ctl, cols, zc, nbr);
-    TB_LAUNCH_CHECK(ctx, "k_srt_lookup");
-    // block layout
-    const int clear_blocks = (int)std::min<uint64_t>((cap_b + tpb - 1) / tpb, (uint64_t)ctx->num_sms * 16);
-    k_hash_clear<<<clear_blocks, tpb, 0, ctx->stream>>>(t, cap_b, reinterpret_cast<int*>(t + cap), &ctl->block_on);
-    TB_LAUNCH_CHECK(ctx, "k_hash_clear");
-    const int64_t ins_blocks = (n + (int64_t)tpb * kInsPer - 1) / ((int64_t)tpb * kInsPer);
-    k_blk_insert<<<(unsigned)ins_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, (unsigned)pool_blocks);
-    TB_LAUNCH_CHECK(ctx, "k_blk_insert");
-    k_pool_clear<<<ctx->num_sms * 8, tpb, 0, ctx->stream>>>(pool, ctl);
-    TB_LAUNCH_CHECK(ctx, "k_pool_clear");
-    k_vox_insert<<<(unsigned)ins_blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool);
-    TB_LAUNCH_CHECK(ctx, "k_vox_insert");
-    static_assert(kLookupThreads == 256, "k_blk_lookup runs with the builder's block size");
-    k_blk_lookup<NT><<<(unsigned)blocks, tpb, 0, ctx->stream>>>(coords, n, stride, t, mask, ctl, pool, nbr);
-    TB_LAUNCH_CHECK(ctx, "k_blk_lookup");
-    // voxel hash, run only when the block layout did not apply
-    return nbr_build_impl<NT>(ctx, coords, n, stride, nbr, ws, cap, &ctl->fallback);
+    k_map_decide_clear<<<(unsigned)(sms * 8), kTpb, 0, ctx->stream>>>(ctl, cols, col_cap, t, cap_b);
+    TB_LAUNCH_CHECK(ctx, "k_map_decide_clear");
+    k_map_fill_claim<<<(unsigned)ins_blocks, kTpb, 0, ctx->stream>>>(coords, n, stride, vec, ctl, cols, t, mask_b,
+                                                                     (unsigned)pool_blocks);
+    TB_LAUNCH_CHECK(ctx, "k_map_fill_claim");
+    k_map_lookup_clear<NT><<<(unsigned)blocks, kTpb, 0, ctx->stream>>>(coords, n, stride, vec, ctl, cols, zc, nbr, pool,
+                                                                       t, cap, special);
+    TB_LAUNCH_CHECK(ctx, "k_map_lookup_clear");
+    // grid-stride kernels: when the sorted layout applied they return at once, so a small grid
+    k_map_insert<<<(unsigned)std::min<int64_t>(ins_blocks, sms * 8), kTpb, 0, ctx->stream>>>(
+        coords, n, stride, ctl, t, mask_b, pool, cap, special, ctx->d_err);
+    TB_LAUNCH_CHECK(ctx, "k_map_insert");
+    k_map_lookup<NT><<<(unsigned)std::min<int64_t>(blocks, sms * 8), kTpb, 0, ctx->stream>>>(
+        coords, n, stride, ctl, t, mask_b, pool, cap, special, nbr, ctx->d_err);
+    TB_LAUNCH_CHECK(ctx, "k_map_lookup");
+    return TB_OK;
 }
 
 }  // namespace
@@ -884,7 +930,6 @@ extern "C" tb_status tb_build_neighbor_map_noalloc(void* stream, const int32_t* 
     // scan the whole table, so an insert always finds a free or matching slot and a lookup always
     // reaches one; the probe bound of the hash kernels can never be hit here.
     int* const no_err = nullptr;
-    const int* const no_gate = nullptr;
     const int tpb = 256;
     const int64_t blocks = (n + tpb - 1) / tpb;
     // every call rebuilds the table from scratch: the previous call's contents are cleared here.
@@ -894,13 +939,12 @@ extern "C" tb_status tb_build_neighbor_map_noalloc(void* stream, const int32_t* 
     cfg.blockDim = dim3(tpb);
     cfg.stream = st;
     cfg.gridDim = dim3((unsigned)std::min<uint64_t>((cap + tpb - 1) / tpb, (uint64_t)g_noalloc_sms[dev] * 16));
-    if (cudaLaunchKernelEx(&cfg, k_hash_clear, t, cap, special, no_gate) != cudaSuccess) return TB_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, k_hash_clear, t, cap, special) != cudaSuccess) return TB_ERR_CUDA;
     cfg.gridDim = dim3((unsigned)blocks);
-    if (cudaLaunchKernelEx(&cfg, k_hash_insert, coords, n, coord_stride, t, cap - 1, special, no_err, no_gate) !=
-        cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, k_hash_insert, coords, n, coord_stride, t, cap - 1, special, no_err) != cudaSuccess)
         return TB_ERR_CUDA;
     if (cudaLaunchKernelEx(&cfg, k_nbr_lookup<27>, coords, n, coord_stride, (const Slot*)t, cap - 1,
-                           (const int*)special, nbr_out, no_err, no_gate) != cudaSuccess)
+                           (const int*)special, nbr_out, no_err) != cudaSuccess)
         return TB_ERR_CUDA;
     return TB_OK;
 }

@@ -30,11 +30,10 @@ _DT = {torch.float32: _lib.TB_F32, torch.float16: _lib.TB_F16, torch.bfloat16: _
 _EPI = {"none": _lib.TB_EPI_NONE, None: _lib.TB_EPI_NONE, "silu": _lib.TB_EPI_SILU}
 _ctxs: dict = {}
 
-# Kernels one tb_build_neighbor_map call launches: the sorted layout's check, column clear, fill
-# and lookup; the block layout's table clear, insert, bucket clear, voxel insert and lookup; and
-# the voxel hash's clear, insert and lookup. Each layout's kernels return at once when an earlier
-# layout applied.
-NBR_MAP_LAUNCHES = 12
+# Kernels one tb_build_neighbor_map call launches: the order and range check, then five that
+# branch on the layout decided on the device (sorted, block or voxel hash); with the sorted
+# layout the last two return at once.
+NBR_MAP_LAUNCHES = 6
 
 
 def _ptr(t) -> ctypes.c_void_p:
