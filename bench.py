@@ -1179,7 +1179,7 @@ def measure_conv_config(name, dev, steps, warmup, cpu=True, coords_np=None, orde
                 "frac": achieved / peak_tf, "peak_source": f"{peak_kind} bf16_tflops (burst)",
                 "flops_per_launch": flops}
     path = "k_conv_f32 (FFMA)" if dts == "f32" else (
-        "k_submconv_pair" if ci == 64 and co in (32, 64) else
+        "k_submconv_pair" if ci in (32, 64) and co in (32, 64) else
         ("k_submconv_brick" if ci % 64 == 0 else "k_submconv_tc (gather4)"))
     roof["kernel"] = path
     # parity of sampled rows against a plain torch fp32 gather + matmul of the same operands
