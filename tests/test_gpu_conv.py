@@ -106,6 +106,18 @@ def test_sizes_and_partial_tiles(tb, n, path, ci):
     assert max_rel(out, ref) < 1e-4
 
 
+# Output column blocks of 128 or more run the brick kernel on CTA pairs (two tiles per cluster,
+# each CTA streaming half of every weight slice): odd and even tile counts, partial tiles, and
+# Co above 256 (several column blocks).
+@pytest.mark.parametrize("ci,co", [(64, 128), (128, 256), (256, 512)])
+@pytest.mark.parametrize("n", [1, 127, 128, 129, 255, 256, 257, 383, 385, 1000])
+def test_brick_pair_sizes_and_partial_tiles(tb, n, ci, co):
+    coords, feats, w, b = _problem(n, ci, co, 16, n + co, "bf16")
+    out, nbr = _run(coords, feats, w, b, "bf16", out_dtype="f32", path="brick")
+    ref = oracle.submconv(nbr.cpu().numpy(), feats, w, b)
+    assert max_rel(out, ref) < 1e-4
+
+
 @pytest.mark.parametrize("ci", [64, 32])
 @pytest.mark.parametrize("misaligned", [False, True])
 @pytest.mark.parametrize("n", [1003, 2050, 4097, 6144])

@@ -27,6 +27,7 @@ def _conv_inputs(n, ci, co, dtype, seed, box):
 
 
 @pytest.mark.parametrize("ci,co,dtype,path", [(64, 64, torch.bfloat16, "pair"), (128, 64, torch.bfloat16, "brick"),
+                                              (64, 256, torch.bfloat16, "brick"),
                                               (32, 32, torch.float16, "gather"), (24, 40, torch.float32, "auto")])
 def test_range_chunks_equal_whole_conv(tb, ci, co, dtype, path):
     from trellis_cpp_b200 import ops
@@ -63,6 +64,7 @@ def test_range_writes_only_its_rows(tb):
 
 
 @pytest.mark.parametrize("ci,co,dtype,path", [(64, 64, torch.bfloat16, "pair"), (128, 64, torch.bfloat16, "brick"),
+                                              (128, 128, torch.bfloat16, "brick"),
                                               (32, 32, torch.float16, "gather"), (24, 40, torch.float32, "auto")])
 def test_range_any_start_row(tb, ci, co, dtype, path):
     """Ranges may start and end anywhere: the kernels run the whole tiles that hold the range and

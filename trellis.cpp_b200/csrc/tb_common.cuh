@@ -35,6 +35,7 @@ struct tb_ctx {
     // graph) make no function-attribute call
     size_t pair_smem_set[2] = {0, 0};   // the pair kernel's Ci = 64 and Ci = 32 instances
     size_t brick_smem_set = 0;
+    size_t brick_pair_smem_set = 0;
     void* block_h = nullptr;       // fp32 conv output of tb_sparse_convnext
     size_t block_h_bytes = 0;
     void* c2s_ws1 = nullptr;       // tb_sparse_c2s: parent map, mask, norm1 output, conv1 output, gidx

@@ -459,6 +459,357 @@ k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant
     }
 }
 
+// ---- CTA-pair form ---------------------------------------------------------------------------
+// The same pipeline on two CTAs of a cluster (neighbouring SMs) sharing each MMA, for output
+// column blocks of 128 or more: each CTA loads its own tile's indices and brick and builds its
+// own 128 rows of A in its TMEM, but streams only half of every weight slice (nb / 2 output
+// columns); the even CTA issues tcgen05.mma.cta_group::2 with M = 256, whose B operand is the two
+// halves and whose D rows land in each CTA's TMEM. Per output row that halves the weight bytes
+// streamed from L2 and doubles the work each stage hand-off covers.
+// Cross-CTA hand-offs: one barrier of the even CTA per stage collects both CTAs' builder warps,
+// the even CTA's weight TMA and the odd CTA's weight half, which the odd CTA's first MMA warp
+// passes on once its TMA has landed, so the issuer waits once per stage; epilogue warps arrive on
+// the even CTA's barriers; MMA commits multicast to both CTAs. The cross-CTA arrives and waits
+// are relaxed at cluster scope: with release / acquire the hand-offs took more than twice as long
+// (C2: 1.17 ms against 0.75 ms per conv). Every wait is bounded and aborts the CTA cleanly.
+constexpr int kNumBarsPair = kNumBars;
+constexpr int kPairMinNb = 128;                 // output column blocks at least this wide use the pair
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+k_submconv_brick_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap fmap,
+                      const BrickParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const size_t brick_bytes = (size_t)p.brick_cap * 128;
+    uint8_t* brick_base = smem;                                        // [2][brick_cap][128]
+    uint8_t* wst_base = smem + 2 * brick_bytes;                        // [nbst][b_alloc]
+    int32_t* s_nbr = reinterpret_cast<int32_t*>(wst_base + (size_t)p.nbst * p.b_alloc);   // [2][27*128]
+    BrickMeta* s_meta = reinterpret_cast<BrickMeta*>(s_nbr + 2 * kNbrInts);               // [2]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s_meta + 2);
+    uint32_t* s_misc = reinterpret_cast<uint32_t*>(bars + kNumBarsPair);   // [0] tmem base, [1] abort
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_misc + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const uint32_t bar0 = smem_u32(bars);
+    const uint32_t nbrf = bar0, nbre = bar0 + 16, brkf = bar0 + 32, brke = bar0 + 48;
+    const uint32_t af = bar0 + 64, ae = af + 8 * kNA;
+    const uint32_t bf = ae + 8 * kNA, be = bf + 8 * kMaxB;
+    const uint32_t df = be + 8 * kMaxB, de = df + 32, drain = de + 32;   // df/de: [issuer][buffer]
+
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(nbrf + 8 * b, 1);
+            mbar_init(nbre + 8 * b, 8);
+            mbar_init(brkf + 8 * b, 1);
+            mbar_init(brke + 8 * b, 8);
+        }
+        for (int k = 0; k < 4; ++k) {
+            mbar_init(df + 8 * k, 1);
+            mbar_init(de + 8 * k, 8);        // four epilogue warps in each CTA (even CTA's copy used)
+        }
+        for (int a = 0; a < kNA; ++a) {
+            // stage seq is ready when af[seq % kNA] of the even CTA has: four builder warps of each
+            // CTA, the odd CTA's weight half (forwarded) and the even CTA's own weight TMA
+            mbar_init(af + 8 * a, 10);
+            mbar_init(ae + 8 * a, 1);
+        }
+        for (int s = 0; s < kMaxB; ++s) {
+            mbar_init(bf + 8 * s, 1);
+            mbar_init(be + 8 * s, 1);
+        }
+        mbar_init(drain, (uint32_t)p.niss);
+        s_misc[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&fmap)) : "memory");
+    }
+    if (warp == kWarpMma0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(s_misc)), "r"(p.tmem_cols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    cluster_sync_all();                       // both CTAs' barriers and TMEM exist before any cross-CTA use
+    tc_fence_after();
+    const uint32_t tmem_base = s_misc[0];
+    const int npairs = (p.ntiles + 1) / 2;
+    const int nunits = npairs * p.ncb;
+    const int cid = (int)cluster_id_x(), ncl = (int)nclusters_x();
+    const int32_t sentinel = (int32_t)p.n;
+
+    if (warp == kWarpLoader) {
+        // ------------------------------------------------------------------ loader (per CTA)
+        int it = 0, bseq = 0;
+        bool ok = true;
+        for (int u = cid; u < nunits && ok; u += ncl, ++it) {
+            const int tile = p.tile0 + 2 * (u / p.ncb) + (int)rank;
+            const int buf = it & 1;
+            if (!mbar_wait(nbre + 8 * buf, ((it >> 1) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
+            const int64_t r0 = (int64_t)tile * kTileM;
+            int32_t* dst = s_nbr + buf * kNbrInts;
+            for (int t = 0; t < 27; ++t) {
+                const int32_t* src = p.nbr + (int64_t)t * p.n + r0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int r = lane + 32 * q;
+                    if (r0 + r < p.n) cp_async_4(smem_u32(dst + t * kTileM + r), src + r);
+                    else dst[t * kTileM + r] = sentinel;
+                }
+            }
+            cp_async_wait_all();
+            __syncwarp();
+            int lo[3] = {INT_MAX, INT_MAX, INT_MAX}, hi[3] = {-1, -1, -1};
+#pragma unroll
+            for (int g = 0; g < 3; ++g) {
+                for (int tt = 0; tt < 9; ++tt) {
+                    const int t = 9 * g + tt;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int32_t v = dst[t * kTileM + lane + 32 * q];
+                        if (v != sentinel) { lo[g] = min(lo[g], v); hi[g] = max(hi[g], v); }
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < 3; ++g) {
+                lo[g] = __reduce_min_sync(0xffffffffu, lo[g]);
+                hi[g] = __reduce_max_sync(0xffffffffu, hi[g]);
+            }
+            int off = 0, nbox = 0;
+            int glo[3], glen[3], goff[3], gbox[3];
+#pragma unroll
+            for (int g = 0; g < 3; ++g) {
+                const int len = hi[g] >= 0 ? hi[g] - lo[g] + 1 : 0;
+                const int room = p.brick_cap - off;
+                const int held = len < room ? len : room;
+                glo[g] = hi[g] >= 0 ? lo[g] : 0;
+                glen[g] = held;
+                goff[g] = off;
+                gbox[g] = (held + kBox - 1) / kBox;
+                off += gbox[g] * kBox;
+                nbox += gbox[g];
+            }
+            if (lane == 0) {
+                BrickMeta& m = s_meta[buf];
+#pragma unroll
+                for (int g = 0; g < 3; ++g) { m.lo[g] = glo[g]; m.len[g] = glen[g]; m.off[g] = goff[g]; }
+                m.nbox = nbox;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(nbrf + 8 * buf);
+            for (int kc = 0; kc < p.nkc; ++kc, ++bseq) {
+                const int slot = bseq & 1;
+                if (!mbar_wait(brke + 8 * slot, ((bseq >> 1) & 1) ^ 1, s_abort, p.err)) { ok = false; break; }
+                const uint32_t bdst = smem_u32(brick_base + (size_t)slot * brick_bytes);
+                if (lane == 0) mbar_arrive_expect_tx(brkf + 8 * slot, (uint32_t)nbox * kBox * 128);
+                __syncwarp();
+                for (int j = lane; j < nbox; j += 32) {
+                    int g = 0, k = j;
+                    if (k >= gbox[0]) { k -= gbox[0]; g = 1; if (k >= gbox[1]) { k -= gbox[1]; g = 2; } }
+                    const int go = g == 0 ? goff[0] : (g == 1 ? goff[1] : goff[2]);
+                    const int gl = g == 0 ? glo[0] : (g == 1 ? glo[1] : glo[2]);
+                    tma_load_2d(bdst + (uint32_t)(go + k * kBox) * 128, &fmap, kc * 64, gl + k * kBox, brkf + 8 * slot);
+                }
+            }
+        }
+        if (!ok && lane == 0) {
+            const long long t0 = clock64();
+            while (clock64() - t0 < 4000000ll) __nanosleep(256);
+        }
+    } else if (warp >= kWarpBuild0 && warp < kWarpBuild0 + 8) {
+        // ------------------------------------------------------------------ A builders (per CTA)
+        const int q = warp & 3;
+        const int half = (warp - kWarpBuild0) >> 2;
+        const int i = q * 32 + lane;
+        const uint32_t a_lane = tmem_base + ((uint32_t)(q * 32) << 16) + p.a_col0;
+        int it = 0, bseq = 0, seq0 = 0;
+        bool ok = true;
+        for (int u = cid; u < nunits && ok; u += ncl, ++it) {
+            const int buf = it & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(nbrf + 8 * buf, (it >> 1) & 1, s_abort, p.err))) { ok = false; break; }
+            const BrickMeta m = s_meta[buf];
+            const int32_t* rows = s_nbr + buf * kNbrInts;
+            const int rot = u % 27;
+            for (int kc = 0; kc < p.nkc && ok; ++kc, ++bseq, seq0 += 27) {
+                const int slot = bseq & 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(brkf + 8 * slot, (bseq >> 1) & 1, s_abort, p.err))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* brick = brick_base + (size_t)slot * brick_bytes;
+                for (int j = (half ^ seq0) & 1; j < 27 && ok; j += 4) {
+                    const int j2 = j + 2;
+                    const bool has2 = j2 < 27;
+                    const int t = rot_tap(rot, j), t2 = rot_tap(rot, j2);
+                    uint32_t r0[32], r1[32];
+                    load_nbr_row(p, m, brick, rows[t * kTileM + i], t, kc, r0);
+                    if (has2) load_nbr_row(p, m, brick, rows[t2 * kTileM + i], t2, kc, r1);
+                    const int s1 = seq0 + j, s2 = seq0 + j2;
+                    const int a1 = s1 & (kNA - 1), a2 = s2 & (kNA - 1);
+                    // the slots' previous stages have been multiplied (commits reach both CTAs)
+                    if (!__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(ae + 8 * a1, ((s1 >> 3) & 1) ^ 1, s_abort,
+                                                                           p.err))) { ok = false; break; }
+                    if (has2 && !__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(ae + 8 * a2, ((s2 >> 3) & 1) ^ 1,
+                                                                                   s_abort, p.err))) { ok = false; break; }
+                    tc_fence_after();
+                    tmem_st_x32(a_lane + 32u * a1, r0);
+                    if (has2) tmem_st_x32(a_lane + 32u * a2, r1);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive_cluster_relaxed(af + 8 * a1, 0);
+                        if (has2) mbar_arrive_cluster_relaxed(af + 8 * a2, 0);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(brke + 8 * slot);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(nbre + 8 * buf);
+        }
+    } else if (warp >= kWarpWeight0 && warp < kWarpWeight0 + kWeightWarps) {
+        // ------------------------------------------------------------------ weight producers (per CTA)
+        // this CTA's half of each [nb x 64] slice: output columns cb*nb + rank*nb/2 .. + nb/2
+        const int wk = warp - kWarpWeight0;
+        const int nw = p.nbst < kWeightWarps ? p.nbst : kWeightWarps;
+        if (lane == 0 && wk < nw) {
+            int seq = wk;
+            bool ok = true;
+            const int stages_per_unit = 27 * p.nkc;
+            int it = 0;
+            for (int u = cid; u < nunits && ok; u += ncl, ++it) {
+                const int cb = u % p.ncb;
+                const int unit_end = (it + 1) * stages_per_unit;
+                for (; seq < unit_end; seq += nw) {
+                    const int local = seq - it * stages_per_unit;
+                    const int kc = local / 27, t = rot_tap(u % 27, local - kc * 27);
+                    const int st = seq & (p.nbst - 1);
+                    // the stage's previous slice has been multiplied (the commit reaches both CTAs)
+                    if (!mbar_wait_cluster_relaxed(be + 8 * st, ((seq >> p.nbst_log2) & 1) ^ 1, s_abort, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    // the even CTA's half completes on the stage's ready barrier directly; the odd
+                    // CTA's on its own barrier, which the forwarder passes on
+                    const uint32_t done = leader ? af + 8 * (seq & (kNA - 1)) : bf + 8 * st;
+                    mbar_arrive_expect_tx(done, p.b_bytes);
+                    tma_load_2d(smem_u32(wst_base + (size_t)st * p.b_alloc), &wmap, t * p.ci + kc * 64,
+                                cb * p.nb + (int)rank * (p.nb / 2), done);
+                }
+            }
+            if (!ok) {
+                const long long t0 = clock64();
+                while (clock64() - t0 < 4000000ll) __nanosleep(256);
+            }
+        }
+    } else if (warp == kWarpMma0 && !leader) {
+        // ------------------------------------------------------------------ odd CTA: stage forwarder
+        // each of this CTA's weight stages, once its TMA has landed, is passed on to the even CTA
+        if (lane == 0) {
+            const int total = ((nunits - cid + ncl - 1) / ncl) * 27 * p.nkc;   // stages of this cluster's units
+            for (int seq = 0; seq < total; ++seq) {
+                const int st = seq & (p.nbst - 1);
+                if (!mbar_wait(bf + 8 * st, (seq >> p.nbst_log2) & 1, s_abort, p.err)) break;
+                mbar_arrive_cluster_relaxed(af + 8 * (seq & (kNA - 1)), 0);
+            }
+        }
+    } else if (warp >= kWarpMma0 && warp < kWarpMma0 + 2) {
+        // ------------------------------------------------------------------ MMA issuers (even CTA)
+        const int mi = warp - kWarpMma0;
+        if (leader && lane == 0 && mi < p.niss) {
+            const uint64_t bdesc0 = smem_desc<128>(smem_u32(wst_base));
+            const uint32_t bstep = p.b_alloc >> 4;
+            const uint32_t a0 = tmem_base + p.a_col0;
+            const int stages_per_unit = 27 * p.nkc;
+            int seq = mi, it = 0;
+            bool ok = true;
+            for (int u = cid; u < nunits && ok; u += ncl, ++it) {
+                const int d = p.nd == 2 ? (it & 1) : 0;
+                const uint32_t dph = p.nd == 2 ? ((it >> 1) & 1) : (it & 1);
+                const int dk = mi * 2 + d;
+                // both CTAs' epilogues have read this accumulator
+                if (!mbar_wait_cluster_relaxed(de + 8 * dk, dph ^ 1, s_abort, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t dt = tmem_base + (uint32_t)((mi * p.nd + d) * p.nb);
+                const int unit_end = (it + 1) * stages_per_unit;
+                uint32_t acc = 0;
+                for (; seq < unit_end; seq += p.niss) {
+                    const int a = seq & (kNA - 1);
+                    const int st = seq & (p.nbst - 1);
+                    // both CTAs' A rows and weight halves of the stage (one barrier)
+                    if (!mbar_wait_cluster_relaxed(af + 8 * a, (seq >> 3) & 1, s_abort, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t at = a0 + 32u * (uint32_t)a;
+                    const uint64_t bd = bdesc0 + (uint64_t)(bstep * (uint32_t)st);
+                    tc_mma_ts_pair(dt, at, bd, p.idesc, acc);
+                    tc_mma_ts_pair(dt, at + 8, bd + 2, p.idesc, 1u);
+                    tc_mma_ts_pair(dt, at + 16, bd + 4, p.idesc, 1u);
+                    tc_mma_ts_pair(dt, at + 24, bd + 6, p.idesc, 1u);
+                    acc = 1u;
+                    tc_commit_pair(ae + 8 * a, 0x3);
+                    tc_commit_pair(be + 8 * st, 0x3);
+                }
+                if (!ok) break;
+                tc_commit_pair(df + 8 * dk, 0x3);
+            }
+            tc_commit_pair(drain, 0x1);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) __nanosleep(64);
+        }
+    } else if (warp < 4) {
+        // ------------------------------------------------------------------ epilogue (per CTA)
+        const int q = warp;
+        int it = 0;
+        const size_t esize = p.out_kind == 0 ? 4 : 2;
+        for (int u = cid; u < nunits; u += ncl, ++it) {
+            const int tile = p.tile0 + 2 * (u / p.ncb) + (int)rank, cb = u % p.ncb;
+            const int d = p.nd == 2 ? (it & 1) : 0;
+            const uint32_t dph = p.nd == 2 ? ((it >> 1) & 1) : (it & 1);
+            bool ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(df + 8 * d, dph, s_abort, p.err));
+            if (ok && p.niss == 2) ok = __all_sync(0xffffffffu, mbar_wait_cluster_relaxed(df + 8 * (2 + d), dph, s_abort, p.err));
+            if (!ok) break;
+            tc_fence_after();
+            const int64_t row = (int64_t)tile * kTileM + q * 32 + lane;
+            const bool valid = row >= p.row_begin && row < p.row_end;
+            uint8_t* orow = p.out + ((size_t)row * p.co + (size_t)cb * p.nb) * esize;
+            const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+            const uint32_t d0 = lane_base + (uint32_t)(d * p.nb);
+            const uint32_t d1 = lane_base + (uint32_t)((p.nd + d) * p.nb);
+            for (int c0 = 0; c0 < p.nb; c0 += 16) {
+                uint32_t v[16], w[16];
+                TMEM_LD_X16(d0 + c0, v);
+                if (p.niss == 2) {
+                    TMEM_LD_X16(d1 + c0, w);
+                }
+                tmem_wait_ld();
+                float a[16], f[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) a[j] = __uint_as_float(v[j]) + (p.niss == 2 ? __uint_as_float(w[j]) : 0.0f);
+                epi16(a, p.bias ? p.bias + cb * p.nb + c0 : nullptr, p.epi, f);
+                if (valid) store16(orow + (size_t)c0 * esize, f, p.out_kind);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_cluster_relaxed(de + 8 * d, 0);
+                if (p.niss == 2) mbar_arrive_cluster_relaxed(de + 8 * (2 + d), 0);
+            }
+        }
+    }
+
+    __syncthreads();
+    cluster_sync_all();                       // the peer's MMAs and reads are finished
+    if (warp == kWarpMma0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(tmem_base), "r"(p.tmem_cols) : "memory");
+    }
+}
+
 }  // namespace
 
 #ifdef TB_TRACE
@@ -483,6 +834,8 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64
         ctx->encode_tiled = fn;
     }
     const int nb = co <= 256 ? co : 256;
+    // output column blocks of kPairMinNb or more run on CTA pairs (each CTA streams half the weights)
+    const bool pair = nb >= kPairMinNb;
     BrickParams p{};
     p.trace = nullptr;
 #ifdef TB_TRACE
@@ -505,10 +858,11 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64
     p.ncb = co / nb;
     p.nkc = ci / 64;
     p.nb = nb;
-    p.b_bytes = (uint32_t)nb * 128;
+    const int nb_cta = pair ? nb / 2 : nb;      // weight rows each CTA streams per stage
+    p.b_bytes = (uint32_t)nb_cta * 128;
     p.b_alloc = (p.b_bytes + 1023u) & ~1023u;
     // 64 KB of weight stages; each stage is owned by weight warp (seq % 4)
-    p.nbst = nb <= 64 ? kMaxB : (nb <= 128 ? 4 : 2);
+    p.nbst = nb_cta <= 64 ? kMaxB : (nb_cta <= 128 ? 4 : 2);
     p.nbst_log2 = p.nbst == 8 ? 3 : (p.nbst == 4 ? 2 : 1);
     p.niss = nb <= 64 ? 2 : 1;
     p.nd = (p.niss * 2 * nb + 32 * kNA <= 512) ? 2 : 1;
@@ -517,9 +871,12 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64
     while (cols < p.a_col0 + 32u * kNA) cols <<= 1;
     p.tmem_cols = cols;
     const uint32_t fmt = dtype == TB_BF16 ? 1u : 0u;
-    p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(nb >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+    // D f32, A/B format, K-major, N = nb, M = 128 (one CTA) or 256 (the pair)
+    p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(nb >> 3) << 17) |
+              ((uint32_t)((pair ? 2 : 1) * kTileM >> 4) << 24);
 
-    const size_t fixed = 2 * (size_t)kNbrInts * 4 + 2 * sizeof(BrickMeta) + 8 * kNumBars + 16 + 1024;
+    const size_t fixed = 2 * (size_t)kNbrInts * 4 + 2 * sizeof(BrickMeta) + 8 * (pair ? kNumBarsPair : kNumBars) + 16 +
+                         1024;
     const size_t budget = (size_t)ctx->max_smem_optin;
     const size_t wbytes = (size_t)p.nbst * p.b_alloc;
     if (budget < fixed + wbytes + 2 * 128 * 128)
@@ -536,7 +893,7 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64
     {
         const cuuint64_t gdim[2] = {(cuuint64_t)27 * ci, (cuuint64_t)co};
         const cuuint64_t gstride[1] = {(cuuint64_t)27 * ci * 2};
-        const cuuint32_t box[2] = {64, (cuuint32_t)nb};
+        const cuuint32_t box[2] = {64, (cuuint32_t)nb_cta};
         CUresult cr = reinterpret_cast<EncodeTiledFn>(ctx->encode_tiled)(
             &wmap, dt, 2, const_cast<void*>(weight), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -551,9 +908,21 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the feature view");
     }
+    cudaError_t e = cudaSuccess;
+    if (pair) {
+        const int units = (p.ntiles + 1) / 2 * p.ncb;
+        const int nclusters = std::max(1, std::min(units, ctx->num_sms / 2));
+        if (smem > ctx->brick_pair_smem_set) {
+            e = cudaFuncSetAttribute(k_submconv_brick_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_submconv_brick_pair)");
+            ctx->brick_pair_smem_set = smem;
+        }
+        k_submconv_brick_pair<<<2 * nclusters, kThreads, smem, ctx->stream>>>(wmap, fmap, p);
+        TB_LAUNCH_CHECK(ctx, "k_submconv_brick_pair");
+        return TB_OK;
+    }
     const int units = p.ntiles * p.ncb;
     const int grid = std::min(units, ctx->num_sms);
-    cudaError_t e = cudaSuccess;
     if (smem > ctx->brick_smem_set) {
         e = cudaFuncSetAttribute(k_submconv_brick, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_submconv_brick)");
