@@ -720,8 +720,11 @@ k_submconv_brick_pair(const __grid_constant__ CUtensorMap wmap, const __grid_con
         }
     } else if (warp >= kWarpMma0 && warp < kWarpMma0 + 2) {
         // ------------------------------------------------------------------ MMA issuers (even CTA)
+        // The whole warp runs the loop and waits (warp-uniform results); one elected lane issues.
+        // From a converged warp an MMA issues in about 40 cycles with the commits hidden, against
+        // about 55 plus about 80 per commit from a lone active lane.
         const int mi = warp - kWarpMma0;
-        if (leader && lane == 0 && mi < p.niss) {
+        if (leader && mi < p.niss) {
             const uint64_t bdesc0 = smem_desc<128>(smem_u32(wst_base));
             const uint32_t bstep = p.b_alloc >> 4;
             const uint32_t a0 = tmem_base + p.a_col0;
@@ -733,7 +736,10 @@ k_submconv_brick_pair(const __grid_constant__ CUtensorMap wmap, const __grid_con
                 const uint32_t dph = p.nd == 2 ? ((it >> 1) & 1) : (it & 1);
                 const int dk = mi * 2 + d;
                 // both CTAs' epilogues have read this accumulator
-                if (!mbar_wait_cluster_relaxed(de + 8 * dk, dph ^ 1, s_abort, p.err)) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(de + 8 * dk, dph ^ 1, s_abort, p.err))) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t dt = tmem_base + (uint32_t)((mi * p.nd + d) * p.nb);
                 const int unit_end = (it + 1) * stages_per_unit;
@@ -742,24 +748,35 @@ k_submconv_brick_pair(const __grid_constant__ CUtensorMap wmap, const __grid_con
                     const int a = seq & (kNA - 1);
                     const int st = seq & (p.nbst - 1);
                     // both CTAs' A rows and weight halves of the stage (one barrier)
-                    if (!mbar_wait_cluster_relaxed(af + 8 * a, (seq >> 3) & 1, s_abort, p.err)) { ok = false; break; }
+                    if (!__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(af + 8 * a, (seq >> 3) & 1, s_abort, p.err))) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
-                    const uint32_t at = a0 + 32u * (uint32_t)a;
-                    const uint64_t bd = bdesc0 + (uint64_t)(bstep * (uint32_t)st);
-                    tc_mma_ts_pair(dt, at, bd, p.idesc, acc);
-                    tc_mma_ts_pair(dt, at + 8, bd + 2, p.idesc, 1u);
-                    tc_mma_ts_pair(dt, at + 16, bd + 4, p.idesc, 1u);
-                    tc_mma_ts_pair(dt, at + 24, bd + 6, p.idesc, 1u);
+                    if (elect_one()) {
+                        const uint32_t at = a0 + 32u * (uint32_t)a;
+                        const uint64_t bd = bdesc0 + (uint64_t)(bstep * (uint32_t)st);
+                        tc_mma_ts_pair(dt, at, bd, p.idesc, acc);
+                        tc_mma_ts_pair(dt, at + 8, bd + 2, p.idesc, 1u);
+                        tc_mma_ts_pair(dt, at + 16, bd + 4, p.idesc, 1u);
+                        tc_mma_ts_pair(dt, at + 24, bd + 6, p.idesc, 1u);
+                        tc_commit_pair(ae + 8 * a, 0x3);
+                        tc_commit_pair(be + 8 * st, 0x3);
+                    }
+                    __syncwarp();
                     acc = 1u;
-                    tc_commit_pair(ae + 8 * a, 0x3);
-                    tc_commit_pair(be + 8 * st, 0x3);
                 }
                 if (!ok) break;
-                tc_commit_pair(df + 8 * dk, 0x3);
+                if (elect_one()) tc_commit_pair(df + 8 * dk, 0x3);
+                __syncwarp();
             }
-            tc_commit_pair(drain, 0x1);
-            const long long t0 = clock64();
-            while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) __nanosleep(64);
+            if (elect_one()) tc_commit_pair(drain, 0x1);
+            __syncwarp();
+            if (lane == 0) {
+                const long long t0 = clock64();
+                while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) __nanosleep(64);
+            }
+            __syncwarp();
         }
     } else if (warp < 4) {
         // ------------------------------------------------------------------ epilogue (per CTA)
@@ -864,7 +881,9 @@ tb_status tb_conv_brick_launch(tb_ctx* ctx, const int32_t* nbr, int64_t n, int64
     // 64 KB of weight stages; each stage is owned by weight warp (seq % 4)
     p.nbst = nb_cta <= 64 ? kMaxB : (nb_cta <= 128 ? 4 : 2);
     p.nbst_log2 = p.nbst == 8 ? 3 : (p.nbst == 4 ? 2 : 1);
-    p.niss = nb <= 64 ? 2 : 1;
+    // two issuers alternate stages into two accumulators where one stage's MMAs are shorter than
+    // the hand-offs around them: 64-column blocks, and 128-column blocks on CTA pairs
+    p.niss = (nb <= 64 || (pair && nb <= 128)) ? 2 : 1;
     p.nd = (p.niss * 2 * nb + 32 * kNA <= 512) ? 2 : 1;
     p.a_col0 = (uint32_t)(p.niss * p.nd * nb);
     uint32_t cols = 32;
