@@ -31,6 +31,25 @@ def test_linear_shapes(tb, m, k, n, dtype):
     assert max_rel(out.cpu().numpy(), ref) < 1e-4
 
 
+# K a multiple of 64 with 256-column tiles and more than one row block runs on CTA pairs (two row
+# blocks per cluster, each CTA loading half of the tile's weight rows): odd and even row-block
+# counts, a partial last N tile, the decoder's MLP shapes.
+@pytest.mark.parametrize("m,k,n", [(129, 64, 256), (255, 128, 512), (256, 64, 272), (383, 512, 2048), (384, 256, 260),
+                                   (14211, 512, 2048), (3968, 4096, 1024)])
+def test_linear_pair_shapes(tb, m, k, n):
+    from trellis_cpp_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(m * 3 + k + n)
+    a = torch.randn((m, k), device="cuda", generator=g).bfloat16()
+    w = (torch.randn((n, k), device="cuda", generator=g) / np.sqrt(k)).bfloat16()
+    b = 0.1 * torch.randn(n, device="cuda", generator=g)
+    r = torch.randn((m, n), device="cuda", generator=g)
+    out = ops.linear(a, w, b, act="silu", residual=r, out_dtype=torch.float32)
+    ops.check_device()
+    ref = _silu(a.double().cpu().numpy() @ w.double().cpu().numpy().T + b.double().cpu().numpy()) \
+        + r.double().cpu().numpy()
+    assert max_rel(out.cpu().numpy(), ref) < 1e-4
+
+
 @pytest.mark.parametrize("res_dtype", [torch.float32, torch.bfloat16])
 def test_linear_silu_residual_16bit_out(tb, res_dtype):
     from trellis_cpp_b200 import ops

@@ -37,6 +37,7 @@ struct LinParams {
     uint8_t* out;
     int out_kind;
     int act;               // 0 none, 1 SiLU
+    int vec_ok;            // bias and residual rows 16-byte aligned: the epilogue reads them by 16 bytes
     uint32_t idesc, tmem_cols, a_bytes, b_bytes;   // b_bytes: the W block's slot, rounded to 1024
     uint32_t tx_bytes;                             // bytes one stage's two TMA boxes deliver
     int* err;
@@ -47,6 +48,37 @@ __device__ __forceinline__ float ld_kind(const uint8_t* p, int64_t i, int kind) 
     const uint16_t u = reinterpret_cast<const uint16_t*>(p)[i];
     if (kind == 2) return __uint_as_float((uint32_t)u << 16);
     return __half2float(__ushort_as_half(u));
+}
+
+// 16 consecutive elements from element index i of a 16-byte aligned row (i a multiple of 8, of 4
+// for fp32): one thread's columns of an output row in the epilogue, read with 16-byte loads.
+__device__ __forceinline__ void ld16_kind(const uint8_t* p, int64_t i, int kind, float* v) {
+    if (kind == 0) {
+        const float4* s = reinterpret_cast<const float4*>(p) + i / 4;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 x = s[q];
+            v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+        }
+        return;
+    }
+    const uint4* s = reinterpret_cast<const uint4*>(p) + i / 8;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const uint4 x = s[q];            // plain loads: the residual may be the output buffer itself
+        const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = w[j] & 0xFFFFu, hi = w[j] >> 16;
+            if (kind == 2) {
+                v[8 * q + 2 * j] = __uint_as_float(lo << 16);
+                v[8 * q + 2 * j + 1] = __uint_as_float(hi << 16);
+            } else {
+                v[8 * q + 2 * j] = __half2float(__ushort_as_half((unsigned short)lo));
+                v[8 * q + 2 * j + 1] = __half2float(__ushort_as_half((unsigned short)hi));
+            }
+        }
+    }
 }
 
 __device__ __forceinline__ void st_kind(uint8_t* p, int64_t i, float v, int kind) {
@@ -179,16 +211,31 @@ k_linear(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUten
                 const int col0 = tn * p.bn + c0;
                 if (!rvalid || col0 >= p.n) continue;
                 float f[16];
+                if (col0 + 16 <= p.n && p.vec_ok) {
+                    // whole chunk, 16-byte aligned bias and residual rows: vector loads
+                    float bb[16], rr[16];
+                    if (p.bias) ld16_kind(reinterpret_cast<const uint8_t*>(p.bias), col0, 0, bb);
+                    if (p.res) ld16_kind(p.res, row * p.n + col0, p.res_kind, rr);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int col = col0 + j;
-                    float x = __uint_as_float(v[j]);
-                    if (col < p.n) {
-                        if (p.bias) x += __ldg(p.bias + col);
+                    for (int j = 0; j < 16; ++j) {
+                        float x = __uint_as_float(v[j]);
+                        if (p.bias) x += bb[j];
                         if (p.act) x = tb_silu(x);
-                        if (p.res) x += ld_kind(p.res, row * p.n + col, p.res_kind);
+                        if (p.res) x += rr[j];
+                        f[j] = x;
                     }
-                    f[j] = x;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int col = col0 + j;
+                        float x = __uint_as_float(v[j]);
+                        if (col < p.n) {
+                            if (p.bias) x += __ldg(p.bias + col);
+                            if (p.act) x = tb_silu(x);
+                            if (p.res) x += ld_kind(p.res, row * p.n + col, p.res_kind);
+                        }
+                        f[j] = x;
+                    }
                 }
                 uint8_t* orow = p.out + (size_t)row * p.n * osz;
                 if (col0 + 16 <= p.n && (p.n % (osz == 4 ? 4 : 8)) == 0) {
@@ -213,6 +260,216 @@ k_linear(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUten
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(p.tmem_cols) : "memory");
+    }
+}
+
+// ---- CTA-pair form (K a multiple of 64, 256-column tiles, at least two row blocks) -----------
+// Two CTAs of a cluster (neighbouring SMs) share each MMA: each loads its own 128-row block of A
+// and half of the tile's 256 weight rows, and the even CTA issues tcgen05.mma.cta_group::2
+// (M = 256) over both. Per output row that halves the weight bytes streamed from L2. The even
+// CTA's stage barrier also waits for the odd CTA's stage, which the odd CTA's MMA warp passes on
+// once its TMA has landed; MMA commits multicast to both CTAs; the epilogue warps of both arrive
+// on the even CTA's accumulator-free barrier. Cross-CTA hand-offs are relaxed at cluster scope.
+constexpr int kLinPairStages = 6;
+constexpr int kLinPairBars = 2 * kLinPairStages + 2 * 2 + 1;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
+k_linear_pair(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap, const LinParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t stage_bytes = p.a_bytes + p.b_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kLinPairStages * stage_bytes);
+    uint32_t* s_misc = reinterpret_cast<uint32_t*>(bars + kLinPairBars);   // [0] tmem, [1] abort, [2] consumed
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_misc + 1);
+    const uint32_t b0 = smem_u32(bars);
+    auto full = [&](int s) { return b0 + 8u * s; };
+    auto empty = [&](int s) { return b0 + 8u * (kLinPairStages + s); };
+    auto accf = [&](int s) { return b0 + 8u * (2 * kLinPairStages + s); };
+    auto acce = [&](int s) { return b0 + 8u * (2 * kLinPairStages + 2 + s); };
+    const uint32_t drain = b0 + 8u * (2 * kLinPairStages + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kLinPairStages; ++s) {
+            mbar_init(full(s), leader ? 2 : 1);     // even CTA: its own TMA and the odd CTA's, passed on
+            mbar_init(empty(s), 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(accf(s), 1);
+            mbar_init(acce(s), 8);                  // four epilogue warps in each CTA (even CTA's copy used)
+        }
+        mbar_init(drain, 1);
+        s_misc[1] = 0;
+        s_misc[2] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(s_misc)), "r"(p.tmem_cols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = s_misc[0];
+    const int cid = (int)cluster_id_x(), ncl = (int)nclusters_x();
+    int issued = 0;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer (per CTA)
+        int it = 0;
+        bool ok = true;
+        for (int64_t t = cid; t < p.ntiles && ok; t += ncl) {
+            const int tm = 2 * (int)(t / p.ntn) + (int)rank, tn = (int)(t % p.ntn);
+            for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+                const int s = it % kLinPairStages;
+                if (it >= kLinPairStages &&
+                    !__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(empty(s), (uint32_t)(((it / kLinPairStages) - 1) & 1),
+                                                                      s_abort, p.err))) {
+                    ok = false;
+                    break;
+                }
+                if (elect_one()) {
+                    const uint32_t dst = smem_u32(smem + s * stage_bytes);
+                    mbar_arrive_expect_tx(full(s), p.tx_bytes);
+                    tma_load_2d(dst, &amap, kb * p.kb, tm * 128, full(s));
+                    tma_load_2d(dst + p.a_bytes, &wmap, kb * p.kb, tn * p.bn + (int)rank * (p.bn / 2), full(s));
+                }
+                __syncwarp();
+                issued = it + 1;
+            }
+        }
+    } else if (warp == 1 && !leader) {
+        // ------------------------------------------------------------------ odd CTA: stage forwarder
+        if (lane == 0) {
+            const int64_t ntl = (p.ntiles - cid + ncl - 1) / ncl;       // this cluster's tiles
+            const int64_t total = ntl * p.nkb;
+            for (int64_t it = 0; it < total; ++it) {
+                const int s = (int)(it % kLinPairStages);
+                if (!mbar_wait(full(s), (uint32_t)((it / kLinPairStages) & 1), s_abort, p.err)) break;
+                mbar_arrive_cluster_relaxed(full(s), 0);
+                s_misc[2] = (uint32_t)(it + 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer (even CTA)
+        int it = 0, i = 0;
+        bool ok = true;
+        for (int64_t t = cid; t < p.ntiles && ok; t += ncl, ++i) {
+            const int acc = i & 1;
+            if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(acce(acc), (uint32_t)(((i >> 1) - 1) & 1),
+                                                                            s_abort, p.err))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+                const int s = it % kLinPairStages;
+                if (!__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(full(s), (uint32_t)((it / kLinPairStages) & 1),
+                                                                      s_abort, p.err))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (elect_one()) {
+                    const uint32_t a_addr = smem_u32(smem + s * stage_bytes), b_addr = a_addr + p.a_bytes;
+                    for (int k = 0; k < p.kb / 16; ++k)
+                        tc_mma_ss_pair(tmem + (uint32_t)(acc * p.bn), smem_desc<128>(a_addr + 32 * k),
+                                       smem_desc<128>(b_addr + 32 * k), p.idesc, (kb | k) ? 1u : 0u);
+                    tc_commit_pair(empty(s), 0x3);
+                    if (kb == p.nkb - 1) tc_commit_pair(accf(acc), 0x3);
+                }
+                __syncwarp();
+                if (lane == 0) s_misc[2] = (uint32_t)(it + 1);
+            }
+        }
+        if (elect_one()) tc_commit_pair(drain, 0x1);
+        __syncwarp();
+        const long long t0 = clock64();
+        while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) { }
+    } else if (warp >= 2) {
+        // ------------------------------------------------------------------ epilogue warps (per CTA)
+        const int q = warp & 3;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        const int osz = p.out_kind == 0 ? 4 : 2;
+        int i = 0;
+        for (int64_t t = cid; t < p.ntiles; t += ncl, ++i) {
+            const int acc = i & 1;
+            const int tm = 2 * (int)(t / p.ntn) + (int)rank, tn = (int)(t % p.ntn);
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster_relaxed(accf(acc), (uint32_t)((i >> 1) & 1), s_abort, p.err)))
+                break;
+            tc_fence_after();
+            const int64_t row = (int64_t)tm * 128 + q * 32 + lane;
+            const bool rvalid = row < p.m;
+            for (int c0 = 0; c0 < p.bn; c0 += 16) {
+                uint32_t v[16];
+                __syncwarp();
+                TMEM_LD_X16(lane_base + (uint32_t)(acc * p.bn + c0), v);
+                tmem_wait_ld();
+                if (c0 + 16 >= p.bn) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster_relaxed(acce(acc), 0);
+                }
+                const int col0 = tn * p.bn + c0;
+                if (!rvalid || col0 >= p.n) continue;
+                float f[16];
+                if (col0 + 16 <= p.n && p.vec_ok) {
+                    // whole chunk, 16-byte aligned bias and residual rows: vector loads
+                    float bb[16], rr[16];
+                    if (p.bias) ld16_kind(reinterpret_cast<const uint8_t*>(p.bias), col0, 0, bb);
+                    if (p.res) ld16_kind(p.res, row * p.n + col0, p.res_kind, rr);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        float x = __uint_as_float(v[j]);
+                        if (p.bias) x += bb[j];
+                        if (p.act) x = tb_silu(x);
+                        if (p.res) x += rr[j];
+                        f[j] = x;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int col = col0 + j;
+                        float x = __uint_as_float(v[j]);
+                        if (col < p.n) {
+                            if (p.bias) x += __ldg(p.bias + col);
+                            if (p.act) x = tb_silu(x);
+                            if (p.res) x += ld_kind(p.res, row * p.n + col, p.res_kind);
+                        }
+                        f[j] = x;
+                    }
+                }
+                uint8_t* orow = p.out + (size_t)row * p.n * osz;
+                if (col0 + 16 <= p.n && (p.n % (osz == 4 ? 4 : 8)) == 0) {
+                    store16(orow + (size_t)col0 * osz, f, p.out_kind);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (col0 + j < p.n) st_kind(orow, col0 + j, f[j], p.out_kind);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 0 && lane == 0) {
+        // TMA loads still in flight after an abort land before the CTA exits (the odd CTA's own
+        // barrier completes with its TMA alone; the even CTA's also needs the passed-on stage)
+        for (int it = (int)s_misc[2]; it < issued; ++it) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(full(it % kLinPairStages), (uint32_t)((it / kLinPairStages) & 1)) &&
+                   clock64() - t0 < kWaitCycles) { }
+        }
+    }
+    __syncthreads();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(p.tmem_cols) : "memory");
     }
 }
 
@@ -265,6 +522,51 @@ tb_status launch_linear(tb_ctx* ctx, const LinParams& p0, const void* a, const v
     return TB_OK;
 }
 
+tb_status launch_linear_pair(tb_ctx* ctx, const LinParams& p0, const void* a, const void* w, tb_dtype dtype) {
+    LinParams p = p0;
+    if (!ctx->encode_tiled) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        TB_CUDA_TRY(ctx, cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (!fn || q != cudaDriverEntryPointSuccess)
+            return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+        ctx->encode_tiled = fn;
+    }
+    const CUtensorMapDataType dt = dtype == TB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap amap, wmap;
+    {
+        const cuuint64_t gdim[2] = {(cuuint64_t)p.k, (cuuint64_t)p.m};
+        const cuuint64_t gstride[1] = {(cuuint64_t)p.k * 2};
+        const cuuint32_t box[2] = {64, 128};
+        CUresult cr = reinterpret_cast<EncodeTiledFn>(ctx->encode_tiled)(
+            &amap, dt, 2, const_cast<void*>(a), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the linear input");
+    }
+    {
+        const cuuint64_t gdim[2] = {(cuuint64_t)p.k, (cuuint64_t)p.n};
+        const cuuint64_t gstride[1] = {(cuuint64_t)p.k * 2};
+        const cuuint32_t box[2] = {64, (cuuint32_t)(p.bn / 2)};
+        CUresult cr = reinterpret_cast<EncodeTiledFn>(ctx->encode_tiled)(
+            &wmap, dt, 2, const_cast<void*>(w), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) return tb_fail(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the linear weight");
+    }
+    const size_t smem = (size_t)kLinPairStages * (p.a_bytes + p.b_bytes) + 8 * kLinPairBars + 16 + 1024;
+    if (smem > (size_t)ctx->max_smem_optin) return tb_fail(ctx, TB_ERR_UNSUPPORTED, "linear: shared memory too small");
+    static size_t smem_set = 0;
+    if (smem > smem_set) {
+        cudaError_t e = cudaFuncSetAttribute(k_linear_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return tb_cuda_fail(ctx, e, "cudaFuncSetAttribute(k_linear_pair)");
+        smem_set = smem;
+    }
+    const int nclusters = (int)std::max<int64_t>(1, std::min<int64_t>(p.ntiles, ctx->num_sms / 2));
+    k_linear_pair<<<2 * nclusters, kLinThreads, smem, ctx->stream>>>(amap, wmap, p);
+    TB_LAUNCH_CHECK(ctx, "k_linear_pair");
+    return TB_OK;
+}
+
 }  // namespace
 
 tb_status tb_linear_launch(tb_ctx* ctx, int64_t m, int k, int n, const void* a, const void* w, const float* bias,
@@ -288,6 +590,13 @@ tb_status tb_linear_launch(tb_ctx* ctx, int64_t m, int k, int n, const void* a, 
     p.out_kind = kind(out_dtype);
     p.act = act;
     p.err = ctx->d_err;
+    {
+        // a residual row starts 16-byte aligned when the base is and n elements fill whole 16 bytes
+        const int rsz = res ? (p.res_kind == 0 ? 4 : 2) : 4;
+        const bool bias_ok = !bias || (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+        const bool res_ok = !res || ((reinterpret_cast<uintptr_t>(res) & 15) == 0 && ((int64_t)n * rsz) % 16 == 0);
+        p.vec_ok = bias_ok && res_ok ? 1 : 0;
+    }
     const uint32_t fmt = dtype == TB_BF16 ? 1u : 0u;
     p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     uint32_t cols = 32;
@@ -296,6 +605,14 @@ tb_status tb_linear_launch(tb_ctx* ctx, int64_t m, int k, int n, const void* a, 
     p.a_bytes = 128u * (uint32_t)p.kb * 2u;
     p.b_bytes = ((uint32_t)p.bn * (uint32_t)p.kb * 2u + 1023u) & ~1023u;
     p.tx_bytes = p.a_bytes + (uint32_t)p.bn * (uint32_t)p.kb * 2u;
+    if (p.kb == 64 && p.bn == 256 && m > 128) {
+        // CTA pairs over two row blocks: each CTA loads half of the 256 weight rows of a tile
+        p.ntiles = ((m + 255) / 256) * p.ntn;
+        p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+        p.b_bytes = 128u * 64u * 2u;
+        p.tx_bytes = p.a_bytes + p.b_bytes;
+        return launch_linear_pair(ctx, p, a, w, dtype);
+    }
     if (p.kb == 64) return launch_linear<128>(ctx, p, a, w, dtype);
     if (p.kb == 32) return launch_linear<64>(ctx, p, a, w, dtype);
     return launch_linear<32>(ctx, p, a, w, dtype);
