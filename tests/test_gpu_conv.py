@@ -118,6 +118,16 @@ def test_brick_pair_sizes_and_partial_tiles(tb, n, ci, co):
     assert max_rel(out, ref) < 1e-4
 
 
+@pytest.mark.parametrize("ci,co", [(128, 128), (256, 256), (64, 512)])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_brick_pair_silu_16bit_output(tb, ci, co, dtype):
+    """The pair brick's epilogue: bias, SiLU and a 16-bit output of the operand type."""
+    coords, feats, w, b = _problem(2100, ci, co, 18, ci + co + 1, dtype)
+    out, nbr = _run(coords, feats, w, b, dtype, epi="silu", path="brick")
+    ref = oracle.submconv(nbr.cpu().numpy(), feats, w, b, silu=True)
+    assert max_rel(out, ref) < TOL[dtype]
+
+
 @pytest.mark.parametrize("ci", [64, 32])
 @pytest.mark.parametrize("misaligned", [False, True])
 @pytest.mark.parametrize("n", [1003, 2050, 4097, 6144])
