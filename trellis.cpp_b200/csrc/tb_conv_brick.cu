@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 k_submconv_brick(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap fmap,
                  const BrickParams p) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     const size_t brick_bytes = (size_t)p.brick_cap * 128;
     uint8_t* brick_base = smem;                                        // [2][brick_cap][128]
     uint8_t* wst_base = smem + 2 * brick_bytes;                        // [nbst][b_alloc]
@@ -479,7 +479,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 k_submconv_brick_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap fmap,
                       const BrickParams p) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     const size_t brick_bytes = (size_t)p.brick_cap * 128;
     uint8_t* brick_base = smem;                                        // [2][brick_cap][128]
     uint8_t* wst_base = smem + 2 * brick_bytes;                        // [nbst][b_alloc]

@@ -138,7 +138,7 @@ k_submconv_pair(const __grid_constant__ CUtensorMap wmap, const __grid_constant_
     using G = PairGeom<CI, TPU>;
     constexpr int kNU = G::kNU;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* w_base = smem;                                                   // [27][w_tap_bytes]
     uint8_t* ring = w_base + 27 * (size_t)p.w_tap_bytes;                      // [ring_rows][128]
     int32_t* s_nbr = reinterpret_cast<int32_t*>(ring + (size_t)p.ring_rows * G::kRB);   // [kNB][27][kNbrRow]

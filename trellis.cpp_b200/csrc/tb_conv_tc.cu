@@ -87,7 +87,7 @@ k_submconv_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ 
               const ConvParams p) {
     constexpr int KSTEPS = RB / 32;      // K=16 MMAs per chunk
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
 
     uint8_t* stage_base = smem;
     int32_t* s_nbr = reinterpret_cast<int32_t*>(smem + (size_t)p.stages * p.stage_bytes);   // [2][27*128]

@@ -567,7 +567,7 @@ k_convnext_tail(const __grid_constant__ CUtensorMap w1map, const __grid_constant
     using K = typename L::K;
     constexpr int HC = L::HC, NCH = L::NCH, KB1 = L::KB1, KB2 = L::KB2;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* a1 = smem;
     uint8_t* a2 = smem + L::off_a2;
     uint8_t* w1s = smem + L::off_w1;

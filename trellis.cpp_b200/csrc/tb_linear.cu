@@ -95,7 +95,7 @@ template <int RB>
 __global__ void __launch_bounds__(kLinThreads, 1)
 k_linear(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap, const LinParams p) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     const uint32_t stage_bytes = p.a_bytes + p.b_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * stage_bytes);
     uint32_t* s_misc = reinterpret_cast<uint32_t*>(bars + kLinBars);   // [0] tmem, [1] abort, [2] consumed
@@ -276,7 +276,7 @@ constexpr int kLinPairBars = 2 * kLinPairStages + 2 * 2 + 1;
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
 k_linear_pair(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap, const LinParams p) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     const uint32_t stage_bytes = p.a_bytes + p.b_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kLinPairStages * stage_bytes);
     uint32_t* s_misc = reinterpret_cast<uint32_t*>(bars + kLinPairBars);   // [0] tmem, [1] abort, [2] consumed

@@ -22,6 +22,13 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// The dynamic shared-memory base rounded up to 1024 bytes (the 128-byte swizzle atom). The
+// rounding stays pointer arithmetic on the shared array: a round trip through an integer hides
+// the address space, and every access through the result then compiles to a generic load or
+// store instead of a shared-memory one.
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
+    return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
 }
