@@ -469,6 +469,30 @@ def run_gpu(args):
                        "tb_dist_exchange + tb_dist_build_map, tb_dist_submconv_grow x2, D2H of owned rows "
                        "(CUDA events, slowest rank)"}
 
+    if world > 1:
+        # the z-slab partition runs once per voxel set (a decoder stage), outside the timed step:
+        # timed here on a communicator-free dist of this rank (cut, local rows, one read-back),
+        # slowest rank; -1 if it failed, so that every rank still takes the reduction below
+        part_ms = -1.0
+        try:
+            pd = ops.Dist(dev, rank, world, halo_planes=runner.halo_planes)
+            cg = runner.coords_global
+            pd.partition(cg)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(3):
+                pd.partition(cg)
+            torch.cuda.synchronize()
+            part_ms = (time.perf_counter() - t0) / 3 * 1e3
+            pd.close()
+        except Exception as ex:  # reported, never fatal: the step's numbers stand without it
+            kernel_stats["partition_error"] = str(ex)[:200]
+        tp = torch.tensor([part_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+        kernel_stats["partition_ms_slowest_rank"] = float(tp.item())
+        kernel_stats["partition_note"] = ("tb_dist_partition_zslab, once per voxel set, outside the timed step "
+                                          "(host wall clock around the call, which reads back the cut)")
+
     cpu_baseline = None
     if rank == 0 and not args.no_cpu:
         feats_c, wt1, wt2, nbr_c = _cpu_inputs(coords_np)
