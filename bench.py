@@ -938,22 +938,30 @@ def _dec_weights(rng_or_gen, make):
 
 
 def _decode(ops, w, latent, coords, masks, stage_pairs=None):
-    """decode_unet through the library's C-ABI ops (device tensors); returns (out7, coords)."""
+    """decode_unet through the library's C-ABI ops (device tensors); returns (out7, coords).
+
+    Each stage's map and ConvNeXt blocks run on the stage's rows in key order (tb_sort_rows), the
+    order whose 128-row tiles the conv kernels read as contiguous neighbour ranges; the C2S
+    block's children come parent-major, so the stage's rows are gathered into key order and the
+    blocks' output is scattered back, and every output keeps the reference's row order."""
+    import torch
     h = ops.linear(latent, w["from_latent.weight"], w["from_latent.bias"])
     for s, (c, nblk, cout) in enumerate(DEC_STAGES):
-        nbr = ops.build_neighbor_table(coords)
+        perm = ops.sort_rows(coords)
+        hs = ops.gather_rows(h, perm)
+        nbr = ops.build_neighbor_table(ops.gather_rows(coords, perm))
         if stage_pairs is not None:
             stage_pairs.append(ops.count_valid_pairs(nbr, coords.shape[0]))
         for j in range(nblk):
             p = f"blocks.{s}.{j}."
-            h = ops.sparse_convnext(h, nbr, w[p + "conv.weight"], w[p + "conv.bias"], w[p + "norm.weight"],
-                                    w[p + "norm.bias"], w[p + "mlp.0.weight"], w[p + "mlp.0.bias"],
-                                    w[p + "mlp.2.weight"], w[p + "mlp.2.bias"])
+            hs = ops.sparse_convnext(hs, nbr, w[p + "conv.weight"], w[p + "conv.bias"], w[p + "norm.weight"],
+                                     w[p + "norm.bias"], w[p + "mlp.0.weight"], w[p + "mlp.0.bias"],
+                                     w[p + "mlp.2.weight"], w[p + "mlp.2.bias"])
+        h = ops.scatter_rows(torch.empty_like(h), perm, hs)
         p = f"blocks.{s}.{nblk}."
         prm = {k[len(p):]: v for k, v in w.items() if k.startswith(p)}
         h, coords, _ = ops.sparse_c2s(coords, h, prm, cout, ext_mask=masks[s], max_children=int(masks[s].sum()))
     y = ops.layer_norm(h, eps=1e-5)
-    import torch
     return ops.linear(y, w["output_layer.weight"], w["output_layer.bias"], out_dtype=torch.float32), coords
 
 

@@ -264,6 +264,17 @@ tb_status tb_sparse_c2s(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord
                         int64_t max_children, int32_t* child_coords, void* out, uint8_t* mask_out,
                         int64_t* m_out);
 
+/* tb_sort_rows: perm (device int32 [n]) lists the rows in ascending lexicographic order of their
+ * (b, x, y, z) coordinates (signed; for non-negative coordinates the order of the reference's
+ * voxel key, src/sparse.cpp:25), stably (equal coordinates keep their input order).
+ * No reference counterpart: the reference's decoder keeps the subdivide's parent-major row order
+ * (src/sparse.cpp:205-222). The conv kernels read each 128-row tile's neighbours as three
+ * contiguous row ranges only in this order, so a caller that holds rows in another order can
+ * gather them into it (tb_gather_rows) for a stage's map and convs and scatter the results back
+ * (tb_scatter_rows). One small read-back of the coordinate bounds (synchronises the context's
+ * stream). When the key span needs more than 63 bits the rows keep their order (perm = 0..n-1). */
+tb_status tb_sort_rows(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord_stride, int32_t* perm);
+
 /* ---- host-buffer end-to-end call --------------------------------------------------------
  * Mirrors one decoder stage graph run (run1 / GraphRun::run: upload inputs, compute, read
  * back; src/shape_decoder.cpp:34-51, src/sparse.cpp:145-169), without the LayerNorm/MLP

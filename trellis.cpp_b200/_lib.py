@@ -57,6 +57,7 @@ SIGNATURES = {
     "tb_count_valid_pairs": (_st, [_vp, _vp, _i64, ctypes.POINTER(_i64)]),
     "tb_submconv": (_st, [_vp, _vp, _i64, _vp, _int, _vp, _vp, _int, _int, _int, _int, _vp]),
     "tb_submconv_range": (_st, [_vp, _vp, _i64, _i64, _i64, _vp, _int, _vp, _vp, _int, _int, _int, _int, _vp]),
+    "tb_sort_rows": (_st, [_vp, _vp, _i64, _int, _vp]),
     "tb_subdivide": (_st, [_vp, _vp, _i64, _int, _vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64)]),
     "tb_c2s_gather": (_st, [_vp, _vp, _vp, _i64, _int, _int, _vp]),
     "tb_dual_grid_mesh": (_st, [_vp, _vp, _i64, _int, _vp, _int, _vp, _vp, _i64, ctypes.POINTER(_i64)]),

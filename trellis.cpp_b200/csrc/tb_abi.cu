@@ -100,6 +100,7 @@ tb_status tb_ctx_destroy(tb_ctx* ctx) {
         for (cudaEvent_t e : ctx->stage_ev) cudaEventDestroy(e);
     if (ctx->chunk_hi_host) cudaFreeHost(ctx->chunk_hi_host);
     if (ctx->tail_ws) cudaFree(ctx->tail_ws);
+    if (ctx->sort_ws) cudaFree(ctx->sort_ws);
     if (ctx->d_err) cudaFree(ctx->d_err);
     delete ctx;
     return TB_OK;

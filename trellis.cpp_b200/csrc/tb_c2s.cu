@@ -239,6 +239,11 @@ __global__ void k_child_keys(const int32_t* __restrict__ c, int64_t m, int strid
     }
 }
 
+__global__ void k_iota(int32_t* __restrict__ v, int64_t m) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x)
+        v[i] = (int32_t)i;
+}
+
 int kind_of(tb_dtype d) { return d == TB_F32 ? 0 : (d == TB_F16 ? 1 : 2); }
 
 int grid_for(tb_ctx* ctx, int64_t work, int per_block) {
@@ -448,4 +453,60 @@ extern "C" tb_status tb_sparse_c2s(tb_ctx* ctx, const int32_t* coords, int64_t n
     s = tb_submconv(ctx, nbr2, m, hn, cout, prm->conv2_w, prm->conv2_b, cout, dtype, TB_F32, TB_EPI_NONE, o);
     if (s != TB_OK) return s;
     return tb_c2s_skip_launch(ctx, o, feats, dtype, gsel, orow, m, cin, cout, out_dtype, out);
+}
+
+// Stable order of rows by their signed (b, x, y, z) coordinates (for non-negative ones the
+// reference's key order, src/sparse.cpp:25): the coordinate
+// bounds (one small read-back), a compact key of the rows' offsets from the minima, and a stable
+// device radix sort of (key, row). Rows whose key span needs more than 63 bits keep their order.
+extern "C" tb_status tb_sort_rows(tb_ctx* ctx, const int32_t* coords, int64_t n, int coord_stride, int32_t* perm) {
+    if (!ctx) return TB_ERR_INVALID_ARG;
+    if (n < 0 || (coord_stride != 3 && coord_stride != 4))
+        return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_sort_rows: bad n or coord_stride");
+    if (n >= (int64_t)INT32_MAX) return tb_fail(ctx, TB_ERR_TOO_LARGE, "tb_sort_rows: n must be < 2^31-1");
+    if (n == 0) return TB_OK;
+    if (!coords || !perm) return tb_fail(ctx, TB_ERR_INVALID_ARG, "tb_sort_rows: null pointer");
+    TB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+    size_t cub_b = 0;
+    TB_CUDA_TRY(ctx, cub::DeviceRadixSort::SortPairs(nullptr, cub_b, (const unsigned long long*)nullptr,
+                                                     (unsigned long long*)nullptr, (const int32_t*)nullptr,
+                                                     (int32_t*)nullptr, (int)n, 0, 64, ctx->stream));
+    const size_t key_b = al((size_t)n * 8), val_b = al((size_t)n * 4);
+    cub_b = al(cub_b);
+    tb_status s = tb_ensure(ctx, &ctx->sort_ws, &ctx->sort_ws_bytes, 2 * key_b + val_b + cub_b + 256, "sort workspace");
+    if (s != TB_OK) return s;
+    uint8_t* b = reinterpret_cast<uint8_t*>(ctx->sort_ws);
+    auto* keys_in = reinterpret_cast<unsigned long long*>(b);
+    auto* keys_out = reinterpret_cast<unsigned long long*>(b + key_b);
+    int32_t* rows = reinterpret_cast<int32_t*>(b + 2 * key_b);
+    void* cub_tmp = b + 2 * key_b + val_b;
+    int* mm = reinterpret_cast<int*>(b + 2 * key_b + val_b + cub_b);
+    static const int mm0[8] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX, INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(mm, mm0, sizeof(mm0), cudaMemcpyHostToDevice, ctx->stream));
+    k_coord_bounds<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(coords, n, coord_stride, mm);
+    TB_LAUNCH_CHECK(ctx, "k_coord_bounds");
+    int bh[8];
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(bh, mm, sizeof(bh), cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    auto bits = [](int lo, int hi) {
+        const uint64_t span = (uint64_t)((int64_t)hi - lo);
+        int k = 0;
+        while (k < 33 && (span >> k) != 0) ++k;
+        return k;
+    };
+    const int bz = bits(bh[3], bh[7]), by = bits(bh[2], bh[6]), bx = bits(bh[1], bh[5]), bb = bits(bh[0], bh[4]);
+    const int total_bits = bb + bx + by + bz;
+    if (total_bits > 63) {
+        k_iota<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(perm, n);
+        TB_LAUNCH_CHECK(ctx, "k_iota");
+        return TB_OK;
+    }
+    k_child_keys<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(coords, n, coord_stride, mm, bx + by + bz, by + bz, bz,
+                                                                 keys_in, rows);
+    TB_LAUNCH_CHECK(ctx, "k_child_keys");
+    size_t tmp = cub_b;
+    TB_CUDA_TRY(ctx, cub::DeviceRadixSort::SortPairs(cub_tmp, tmp, keys_in, keys_out, rows, perm, (int)n, 0,
+                                                     std::max(1, total_bits), ctx->stream));
+    return TB_OK;
 }

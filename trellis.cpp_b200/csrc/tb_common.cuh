@@ -50,6 +50,8 @@ struct tb_ctx {
     int32_t* chunk_hi_host = nullptr;
     void* tail_ws = nullptr;       // ConvNeXt tail passes at wide C: LayerNorm output, activations
     size_t tail_ws_bytes = 0;
+    void* sort_ws = nullptr;       // tb_sort_rows: keys, values, radix-sort scratch, coordinate bounds
+    size_t sort_ws_bytes = 0;
 };
 
 // Record a failure on the context and return the status.

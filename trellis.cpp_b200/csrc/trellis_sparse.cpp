@@ -423,9 +423,16 @@ std::vector<float> decode_unet(const GgufModel& m, const std::vector<float>& lat
     for (size_t s = 0; s < st.size(); ++s) {
         const Stage& g = st[s];
         if (g.c != ch) throw std::runtime_error("trellis: decode: stage width does not match the previous stage");
-        DBuf nbr((size_t)n * 27 * 4);
-        ok(tb_build_neighbor_map(c, d_coords->as<int32_t>(), n, 3, nbr.as<int32_t>()), "stage map");
+        // The stage's map and ConvNeXt blocks run on its rows in key order (the C2S block's
+        // children come parent-major, and the conv kernels read a tile's neighbours as contiguous
+        // row ranges only in key order); the blocks' output goes back to the reference's order.
+        DBuf perm((size_t)n * 4), sc((size_t)n * 12), nbr((size_t)n * 27 * 4);
         auto h2 = std::make_unique<DBuf>((size_t)n * ch * es);
+        ok(tb_sort_rows(c, d_coords->as<int32_t>(), n, 3, perm.as<int32_t>()), "stage row order");
+        ok(tb_gather_rows(c, d_coords->p, perm.as<int32_t>(), n, 12, sc.p), "stage coords in key order");
+        ok(tb_gather_rows(c, h->p, perm.as<int32_t>(), n, (int64_t)ch * (int64_t)es, h2->p), "stage rows in key order");
+        std::swap(h, h2);
+        ok(tb_build_neighbor_map(c, sc.as<int32_t>(), n, 3, nbr.as<int32_t>()), "stage map");
         for (int j = 0; j < g.nblk; ++j) {
             const ConvNeXtWeights w = m.convnext(g.prefix + std::to_string(j));
             ok(tb_sparse_convnext(c, nbr.as<int32_t>(), n, h->p, ch, w.conv.weight, w.conv.bias, w.norm_w, w.norm_b,
@@ -433,6 +440,8 @@ std::vector<float> decode_unet(const GgufModel& m, const std::vector<float>& lat
                "ConvNeXt block");
             std::swap(h, h2);
         }
+        ok(tb_scatter_rows(c, h->p, perm.as<int32_t>(), n, (int64_t)ch * (int64_t)es, h2->p), "stage rows back");
+        std::swap(h, h2);
         const C2SWeights w = m.c2s(g.prefix + std::to_string(g.nblk));
         std::unique_ptr<DBuf> d_guide;
         if (guide) {

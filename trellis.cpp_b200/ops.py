@@ -339,6 +339,21 @@ def bias_act(x: torch.Tensor, bias: torch.Tensor | None = None, epi: str = "silu
     return x
 
 
+def sort_rows(coords: torch.Tensor) -> torch.Tensor:
+    """Stable permutation (int32 [N]) listing the rows of ``coords`` (int32 [N,3] or [N,4]) in
+    ascending (b, x, y, z) order (signed, stable), the order the conv kernels read fastest
+    (tb_sort_rows)."""
+    _need_cuda(coords)
+    if coords.dtype != torch.int32 or coords.dim() != 2 or coords.shape[1] not in (3, 4):
+        raise ValueError("coords must be int32 [N,3] or [N,4]")
+    coords = coords.contiguous()
+    n = coords.shape[0]
+    perm = torch.empty(max(n, 1), dtype=torch.int32, device=coords.device)[:n]
+    ctx = context(coords.device)
+    check(_lib.load().tb_sort_rows(ctx, _ptr(coords), n, coords.shape[1], _ptr(perm)), "tb_sort_rows", ctx)
+    return perm
+
+
 def gather_rows(src: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
     _need_cuda(src, rows)
     m = rows.numel()
